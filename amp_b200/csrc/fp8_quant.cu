@@ -1,0 +1,325 @@
+// fp8_quant.cu -- per-tensor amax-scaled FP8 E4M3 quantise / dequantise.
+//
+// The reference ships only a scalar host codec (include/fp8.hpp:15-63) and no
+// amax or device quantiser.  This file is the HBM-bound device path:
+//
+//   pass 1  k_amax_partials : grid-stride 128-bit loads, |x| max kept as a
+//                             packed bf16x2 (max.bf16x2 ignores NaN), warp
+//                             shuffle + shared-memory block reduce, one
+//                             partial per block into the workspace.
+//   pass 2  k_quant_encode  : every block folds the <= 2048 partials (L2
+//                             resident) into amax, scale = amax/448, then
+//                             encodes 16 elements per thread-iteration
+//                             (2 x 16 B loads, 1 x 16 B store) with IEEE
+//                             division and cvt.rn.satfinite.e4m3x2.  Chunks
+//                             are walked last-to-first so the tail that pass 1
+//                             read most recently is still in L2.
+//   k_dequant              : 16 codes (16 B) -> 16 bf16 (2 x 16 B) per
+//                             thread-iteration via cvt.rn.f16x2.e4m3x2.
+//
+// Algorithmic bytes: quantise 5 B/element (2 amax read + 2 read + 1 write),
+// dequantise 3 B/element (1 read + 2 write).
+#include "common.cuh"
+#include "runtime.h"
+
+namespace ampb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxParts = 2048;
+constexpr int kBlocksPerSM = 8;
+
+__device__ __forceinline__ uint32_t absmax_bf16x2(uint32_t m, uint32_t w) {
+    uint32_t a = w & 0x7fff7fffu, r;
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(a));
+    return r;
+}
+
+__device__ __forceinline__ float block_max(float f) {
+    __shared__ float red[kThreads / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    f = warp_max(f);
+    if (lane == 0) red[warp] = f;
+    __syncthreads();
+    f = lane < kThreads / 32 ? red[lane] : 0.0f;
+    f = warp_max(f);  // every warp computes the same value
+    return f;
+}
+
+__global__ void __launch_bounds__(kThreads) k_amax_partials(const uint16_t* __restrict__ x,
+                                                            int64_t n, float* __restrict__ parts,
+                                                            int vec_ok) {
+    uint32_t m = 0;
+    const int64_t nthr = (int64_t)gridDim.x * kThreads;
+    const int64_t tid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+    int64_t done = 0;
+    if (vec_ok) {
+        const int64_t nv = n >> 3;
+        const uint4* xv = reinterpret_cast<const uint4*>(x);
+        int64_t i = tid;
+        for (; i + 3 * nthr < nv; i += 4 * nthr) {
+            uint4 a = ldg_stream_v4(xv + i);
+            uint4 b = ldg_stream_v4(xv + i + nthr);
+            uint4 c = ldg_stream_v4(xv + i + 2 * nthr);
+            uint4 d = ldg_stream_v4(xv + i + 3 * nthr);
+            m = absmax_bf16x2(m, a.x); m = absmax_bf16x2(m, a.y);
+            m = absmax_bf16x2(m, a.z); m = absmax_bf16x2(m, a.w);
+            m = absmax_bf16x2(m, b.x); m = absmax_bf16x2(m, b.y);
+            m = absmax_bf16x2(m, b.z); m = absmax_bf16x2(m, b.w);
+            m = absmax_bf16x2(m, c.x); m = absmax_bf16x2(m, c.y);
+            m = absmax_bf16x2(m, c.z); m = absmax_bf16x2(m, c.w);
+            m = absmax_bf16x2(m, d.x); m = absmax_bf16x2(m, d.y);
+            m = absmax_bf16x2(m, d.z); m = absmax_bf16x2(m, d.w);
+        }
+        for (; i < nv; i += nthr) {
+            uint4 a = ldg_stream_v4(xv + i);
+            m = absmax_bf16x2(m, a.x); m = absmax_bf16x2(m, a.y);
+            m = absmax_bf16x2(m, a.z); m = absmax_bf16x2(m, a.w);
+        }
+        done = nv << 3;
+    }
+    for (int64_t j = done + tid; j < n; j += nthr) m = absmax_bf16x2(m, (uint32_t)x[j]);
+    float f = block_max(fmaxf(bf16_lo(m), bf16_hi(m)));
+    if (threadIdx.x == 0) parts[blockIdx.x] = f;
+}
+
+// 4 bf16 (two packed words) -> 4 E4M3 codes packed little-endian.
+__device__ __forceinline__ uint32_t enc4(uint32_t w0, uint32_t w1, float s) {
+    uint32_t lo = f32x2_to_e4m3x2(__fdiv_rn(bf16_lo(w0), s), __fdiv_rn(bf16_hi(w0), s));
+    uint32_t hi = f32x2_to_e4m3x2(__fdiv_rn(bf16_lo(w1), s), __fdiv_rn(bf16_hi(w1), s));
+    return lo | (hi << 16);
+}
+
+__device__ __forceinline__ uint8_t enc1(uint16_t h, float s) {
+    return (uint8_t)(f32x2_to_e4m3x2(__fdiv_rn(bf16_lo(h), s), 0.0f) & 0xffu);
+}
+
+__global__ void __launch_bounds__(kThreads) k_quant_encode(
+    const uint16_t* __restrict__ x, int64_t n, const float* __restrict__ parts, int nparts,
+    const float* __restrict__ amax_in, uint8_t* __restrict__ q, float* __restrict__ scale_out,
+    float* __restrict__ amax_out, int vec_ok) {
+    float amax;
+    if (amax_in) {
+        amax = *amax_in;
+    } else {
+        float f = 0.0f;
+        for (int i = threadIdx.x; i < nparts; i += kThreads) f = fmaxf(f, parts[i]);
+        amax = block_max(f);
+    }
+    const float s = (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 448.0f);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        if (scale_out) *scale_out = s;
+        if (amax_out) *amax_out = amax;
+    }
+    const int64_t nthr = (int64_t)gridDim.x * kThreads;
+    const int64_t tid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+    int64_t done = 0;
+    if (vec_ok) {
+        const int64_t nc = n >> 4;
+        for (int64_t c = tid; c < nc; c += nthr) {
+            const int64_t ci = nc - 1 - c;
+            const uint4* src = reinterpret_cast<const uint4*>(x + ci * 16);
+            uint4 a = ldg_stream_v4(src);
+            uint4 b = ldg_stream_v4(src + 1);
+            uint4 o;
+            o.x = enc4(a.x, a.y, s);
+            o.y = enc4(a.z, a.w, s);
+            o.z = enc4(b.x, b.y, s);
+            o.w = enc4(b.z, b.w, s);
+            stg_v4(q + ci * 16, o);
+        }
+        done = nc << 4;
+    }
+    for (int64_t j = done + tid; j < n; j += nthr) q[j] = enc1(x[j], s);
+}
+
+__device__ __forceinline__ uint32_t dec2(uint32_t codes16, float s) {
+    uint32_t h = e4m3x2_to_f16x2((uint16_t)codes16);
+    return f32x2_to_bf16x2(__fmul_rn(f16_lo_to_f32(h), s), __fmul_rn(f16_hi_to_f32(h), s));
+}
+
+__global__ void __launch_bounds__(kThreads) k_dequant(const uint8_t* __restrict__ q, int64_t n,
+                                                     const float* __restrict__ scale,
+                                                     uint16_t* __restrict__ y, int vec_ok) {
+    const float s = *scale;
+    const int64_t nthr = (int64_t)gridDim.x * kThreads;
+    const int64_t tid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+    int64_t done = 0;
+    if (vec_ok) {
+        const int64_t nc = n >> 4;
+        for (int64_t c = tid; c < nc; c += nthr) {
+            uint4 v = ldg_stream_v4(q + c * 16);
+            uint4 o0, o1;
+            o0.x = dec2(v.x & 0xffffu, s); o0.y = dec2(v.x >> 16, s);
+            o0.z = dec2(v.y & 0xffffu, s); o0.w = dec2(v.y >> 16, s);
+            o1.x = dec2(v.z & 0xffffu, s); o1.y = dec2(v.z >> 16, s);
+            o1.z = dec2(v.w & 0xffffu, s); o1.w = dec2(v.w >> 16, s);
+            stg_v4(y + c * 16, o0);
+            stg_v4(y + c * 16 + 8, o1);
+        }
+        done = nc << 4;
+    }
+    for (int64_t j = done + tid; j < n; j += nthr) y[j] = (uint16_t)(dec2(q[j], s) & 0xffffu);
+}
+
+inline int grid_for(int64_t work_items) {
+    int64_t cap = (int64_t)sm_count() * kBlocksPerSM;
+    if (cap > kMaxParts) cap = kMaxParts;
+    int64_t want = (work_items + kThreads - 1) / kThreads;
+    if (want < 1) want = 1;
+    return (int)(want < cap ? want : cap);
+}
+
+int launch_amax(const void* x, int64_t n, float* parts, int* nparts_out, cudaStream_t st) {
+    const int vec = aligned16(x);
+    const int grid = grid_for(vec ? (n >> 3) : n);
+    *nparts_out = grid;
+    k_amax_partials<<<grid, kThreads, 0, st>>>(static_cast<const uint16_t*>(x), n, parts, vec);
+    AMPB_CHECK_LAUNCH("k_amax_partials");
+    return AMP_OK;
+}
+
+int check_ws(void* ws, size_t ws_bytes) {
+    AMPB_REQUIRE(ws != nullptr, AMP_ERR_INVALID, "workspace is NULL");
+    AMPB_REQUIRE(ws_bytes >= (size_t)kMaxParts * sizeof(float), AMP_ERR_INVALID,
+                 "workspace too small: %zu < %zu bytes", ws_bytes,
+                 (size_t)kMaxParts * sizeof(float));
+    AMPB_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 3u) == 0, AMP_ERR_INVALID,
+                 "workspace must be 4-byte aligned");
+    return AMP_OK;
+}
+
+}  // namespace
+
+int quant_e4m3_dev(const void* x, int64_t n, uint8_t* q, float* scale_out, float* amax_out,
+                   void* ws, size_t ws_bytes, cudaStream_t st) {
+    AMPB_REQUIRE(n >= 0, AMP_ERR_INVALID, "n must be >= 0 (got %lld)", (long long)n);
+    AMPB_REQUIRE(scale_out != nullptr, AMP_ERR_INVALID, "scale_out is NULL");
+    AMPB_REQUIRE(n == 0 || (x != nullptr && q != nullptr), AMP_ERR_INVALID, "x or q is NULL");
+    int rc = check_ws(ws, ws_bytes);
+    if (rc) return rc;
+    float* parts = static_cast<float*>(ws);
+    int nparts = 0;
+    if (n > 0) {
+        rc = launch_amax(x, n, parts, &nparts, st);
+        if (rc) return rc;
+    }
+    const int vec = aligned16(x) && aligned16(q);
+    const int grid = grid_for(vec ? (n >> 4) : n);
+    k_quant_encode<<<grid, kThreads, 0, st>>>(static_cast<const uint16_t*>(x), n, parts, nparts,
+                                              nullptr, q, scale_out, amax_out, vec);
+    AMPB_CHECK_LAUNCH("k_quant_encode");
+    return AMP_OK;
+}
+
+}  // namespace ampb
+
+using namespace ampb;
+
+extern "C" {
+
+size_t amp_fp8_quant_workspace_bytes(int64_t) { return (size_t)kMaxParts * sizeof(float); }
+
+int amp_fp8_quant_e4m3_dev(const void* x_bf16, int64_t n, uint8_t* q, float* scale_out,
+                           float* amax_out, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+    return quant_e4m3_dev(x_bf16, n, q, scale_out, amax_out, workspace, workspace_bytes,
+                          as_stream(stream));
+}
+
+int amp_fp8_amax_bf16_dev(const void* x_bf16, int64_t n, float* amax_out, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+    AMPB_REQUIRE(n >= 0, AMP_ERR_INVALID, "n must be >= 0 (got %lld)", (long long)n);
+    AMPB_REQUIRE(amax_out != nullptr, AMP_ERR_INVALID, "amax_out is NULL");
+    AMPB_REQUIRE(n == 0 || x_bf16 != nullptr, AMP_ERR_INVALID, "x is NULL");
+    int rc = check_ws(workspace, workspace_bytes);
+    if (rc) return rc;
+    cudaStream_t st = as_stream(stream);
+    float* parts = static_cast<float*>(workspace);
+    int nparts = 0;
+    if (n > 0) {
+        rc = launch_amax(x_bf16, n, parts, &nparts, st);
+        if (rc) return rc;
+    }
+    // Fold the partials: a one-block encode launch over zero elements writes amax.
+    k_quant_encode<<<1, kThreads, 0, st>>>(nullptr, 0, parts, nparts, nullptr, nullptr, nullptr,
+                                           amax_out, 0);
+    AMPB_CHECK_LAUNCH("k_quant_encode(fold)");
+    return AMP_OK;
+}
+
+int amp_fp8_quant_e4m3_from_amax_dev(const void* x_bf16, int64_t n, const float* amax_in,
+                                     uint8_t* q, float* scale_out, void* stream) {
+    AMPB_REQUIRE(n >= 0, AMP_ERR_INVALID, "n must be >= 0 (got %lld)", (long long)n);
+    AMPB_REQUIRE(amax_in != nullptr, AMP_ERR_INVALID, "amax_in is NULL");
+    AMPB_REQUIRE(n == 0 || (x_bf16 != nullptr && q != nullptr), AMP_ERR_INVALID,
+                 "x or q is NULL");
+    const int vec = aligned16(x_bf16) && aligned16(q);
+    const int grid = grid_for(vec ? (n >> 4) : n);
+    k_quant_encode<<<grid, kThreads, 0, as_stream(stream)>>>(
+        static_cast<const uint16_t*>(x_bf16), n, nullptr, 0, amax_in, q, scale_out, nullptr, vec);
+    AMPB_CHECK_LAUNCH("k_quant_encode(amax_in)");
+    return AMP_OK;
+}
+
+int amp_fp8_dequant_e4m3_dev(const uint8_t* q, int64_t n, const float* scale, void* y_bf16,
+                             void* stream) {
+    AMPB_REQUIRE(n >= 0, AMP_ERR_INVALID, "n must be >= 0 (got %lld)", (long long)n);
+    AMPB_REQUIRE(scale != nullptr, AMP_ERR_INVALID, "scale is NULL");
+    if (n == 0) return AMP_OK;
+    AMPB_REQUIRE(q != nullptr && y_bf16 != nullptr, AMP_ERR_INVALID, "q or y is NULL");
+    const int vec = aligned16(q) && aligned16(y_bf16);
+    const int grid = grid_for(vec ? (n >> 4) : n);
+    k_dequant<<<grid, kThreads, 0, as_stream(stream)>>>(q, n, scale,
+                                                        static_cast<uint16_t*>(y_bf16), vec);
+    AMPB_CHECK_LAUNCH("k_dequant");
+    return AMP_OK;
+}
+
+int amp_user_fp8_quant_e4m3(const uint16_t* x, int64_t n, uint8_t* q, float* scale_out,
+                            uint16_t* y) {
+    AMPB_REQUIRE(n >= 0, AMP_ERR_INVALID, "n must be >= 0 (got %lld)", (long long)n);
+    AMPB_REQUIRE(scale_out != nullptr, AMP_ERR_INVALID, "scale_out is NULL");
+    AMPB_REQUIRE(n == 0 || (x != nullptr && q != nullptr), AMP_ERR_INVALID, "x or q is NULL");
+    void *dx, *dq, *dy = nullptr, *dsmall;
+    const size_t ws = amp_fp8_quant_workspace_bytes(n);
+    int rc;
+    if ((rc = staging_get(0, (size_t)n * 2, &dx))) return rc;
+    if ((rc = staging_get(1, (size_t)n, &dq))) return rc;
+    if (y && (rc = staging_get(2, (size_t)n * 2, &dy))) return rc;
+    if ((rc = staging_get(3, ws + 256, &dsmall))) return rc;
+    float* dscale = reinterpret_cast<float*>(static_cast<char*>(dsmall) + ws);
+    cudaStream_t st = 0;
+    if (n) AMPB_CHECK_CUDA(cudaMemcpyAsync(dx, x, (size_t)n * 2, cudaMemcpyHostToDevice, st));
+    if ((rc = quant_e4m3_dev(dx, n, static_cast<uint8_t*>(dq), dscale, nullptr, dsmall, ws, st)))
+        return rc;
+    if (y && (rc = amp_fp8_dequant_e4m3_dev(static_cast<uint8_t*>(dq), n, dscale, dy, st)))
+        return rc;
+    if (n) AMPB_CHECK_CUDA(cudaMemcpyAsync(q, dq, (size_t)n, cudaMemcpyDeviceToHost, st));
+    if (y && n) AMPB_CHECK_CUDA(cudaMemcpyAsync(y, dy, (size_t)n * 2, cudaMemcpyDeviceToHost, st));
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(scale_out, dscale, sizeof(float), cudaMemcpyDeviceToHost, st));
+    AMPB_CHECK_CUDA(cudaStreamSynchronize(st));
+    return AMP_OK;
+}
+
+int amp_user_fp8_dequant_e4m3(const uint8_t* q, int64_t n, float scale, uint16_t* y) {
+    AMPB_REQUIRE(n >= 0, AMP_ERR_INVALID, "n must be >= 0 (got %lld)", (long long)n);
+    if (n == 0) return AMP_OK;
+    AMPB_REQUIRE(q != nullptr && y != nullptr, AMP_ERR_INVALID, "q or y is NULL");
+    void *dq, *dy, *dsmall;
+    int rc;
+    if ((rc = staging_get(1, (size_t)n, &dq))) return rc;
+    if ((rc = staging_get(2, (size_t)n * 2, &dy))) return rc;
+    if ((rc = staging_get(4, 256, &dsmall))) return rc;
+    cudaStream_t st = 0;
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(dq, q, (size_t)n, cudaMemcpyHostToDevice, st));
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(dsmall, &scale, sizeof(float), cudaMemcpyHostToDevice, st));
+    if ((rc = amp_fp8_dequant_e4m3_dev(static_cast<uint8_t*>(dq), n,
+                                       static_cast<const float*>(dsmall), dy, st)))
+        return rc;
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(y, dy, (size_t)n * 2, cudaMemcpyDeviceToHost, st));
+    AMPB_CHECK_CUDA(cudaStreamSynchronize(st));
+    return AMP_OK;
+}
+
+}  // extern "C"

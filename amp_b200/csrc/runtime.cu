@@ -1,0 +1,84 @@
+// runtime.cu -- status reporting, device queries and the host-pointer staging
+// pool shared by the amp_user_* entry points.
+#include <cstdarg>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace ampb {
+
+namespace {
+thread_local char g_msg[512] = "ok";
+}
+
+void set_error(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    int off = std::snprintf(g_msg, sizeof g_msg, "[%d] ", code);
+    if (off < 0) off = 0;
+    std::vsnprintf(g_msg + off, sizeof g_msg - (size_t)off, fmt, ap);
+    va_end(ap);
+}
+
+int cuda_status(cudaError_t e, const char* where) {
+    set_error((int)e, "CUDA error %s (%s) at %s", cudaGetErrorName(e), cudaGetErrorString(e),
+              where);
+    return (int)e;
+}
+
+int sm_count() {
+    static int cache[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+// Grow-only per-device staging buffers for the host-pointer entry points, so
+// that repeated amp_user_* calls do not pay cudaMalloc/cudaFree each time.
+namespace {
+struct Slot {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+std::mutex g_pool_mu;
+std::vector<std::vector<Slot>> g_pool;  // [device][slot]
+}  // namespace
+
+int staging_get(int slot, size_t bytes, void** out) {
+    int dev = 0;
+    AMPB_CHECK_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    if ((int)g_pool.size() <= dev) g_pool.resize(dev + 1);
+    auto& slots = g_pool[dev];
+    if ((int)slots.size() <= slot) slots.resize(slot + 1);
+    Slot& s = slots[slot];
+    if (s.bytes < bytes) {
+        if (s.ptr) AMPB_CHECK_CUDA(cudaFree(s.ptr));
+        s.ptr = nullptr;
+        s.bytes = 0;
+        size_t want = bytes < 256 ? 256 : bytes;
+        AMPB_CHECK_CUDA(cudaMalloc(&s.ptr, want));
+        s.bytes = want;
+    }
+    *out = s.ptr;
+    return AMP_OK;
+}
+
+}  // namespace ampb
+
+extern "C" {
+
+const char* amp_last_error(void) { return ampb::g_msg; }
+
+int amp_abi_version(void) { return 100; /* 0.1.0 */ }
+
+}  // extern "C"

@@ -1,0 +1,87 @@
+/* amp_b200.h -- C ABI of the B200 (sm_100a) kernels.
+ *
+ * Conventions, shared with the plugin contract in amp_plugin.h:
+ *   - every entry point returns an int status: 0 on success, nonzero on a
+ *     hard failure (amp_plugin.h: "caller treats this as a hard error");
+ *     negative values are argument/usage errors (AMP_ERR_*), positive values
+ *     are CUDA runtime error codes; amp_last_error() returns the message;
+ *   - `amp_user_*` functions take HOST pointers and own all device work
+ *     (allocate, copy in, launch, copy out, synchronise) before returning,
+ *     exactly like amp_user_gemm_fp32;
+ *   - `*_dev` functions take DEVICE pointers and a stream (a cudaStream_t
+ *     passed as void*, NULL = legacy default stream); they only enqueue work
+ *     and do not synchronise;
+ *   - bf16 data is passed as raw 16-bit patterns (uint16_t / void*), E4M3 as
+ *     uint8_t codes; no CUDA or torch types appear in any signature.
+ */
+#ifndef AMP_B200_H
+#define AMP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define AMP_API __attribute__((visibility("default")))
+#else
+#define AMP_API
+#endif
+
+#define AMP_OK 0
+#define AMP_ERR_INVALID (-1)     /* bad argument (size, pointer, alignment, config)  */
+#define AMP_ERR_UNSUPPORTED (-2) /* valid request this build does not implement        */
+#define AMP_ERR_TIMEOUT (-3)     /* a bounded device-side wait expired                 */
+#define AMP_ERR_NO_DEVICE (-4)   /* no CUDA device visible                             */
+
+/* Message for the last nonzero status returned on this thread. */
+AMP_API const char* amp_last_error(void);
+/* ABI version: major*10000 + minor*100 + patch. */
+AMP_API int amp_abi_version(void);
+
+/* ------------------------------------------------------------------------
+ * FP8 E4M3 per-tensor amax-scaled quantise / dequantise.
+ * Replaces the host codec AMP::fp8::f32_to_e4m3 / e4m3_to_f32
+ * (include/fp8.hpp:15-63), which has no amax and no device path; the amax
+ * plumbing it would feed is GemmDesc::d_amax_c (include/gemm_vendor.hpp:55-56).
+ * Semantics (bit-exact against the oracle):
+ *   amax  = max |x| (NaN ignored);  scale = amax/448 (IEEE fp32), 1 if amax==0
+ *   q[i]  = E4M3_RNE_satfinite(x[i] / scale)      (IEEE fp32 division)
+ *   y[i]  = bf16_RNE(e4m3_to_f32(q[i]) * scale)
+ * ---------------------------------------------------------------------- */
+
+/* Scratch bytes amp_fp8_quant_e4m3_dev / amp_fp8_amax_bf16_dev need (per-block
+ * partial maxima; a small constant, independent of n). */
+AMP_API size_t amp_fp8_quant_workspace_bytes(int64_t n);
+
+/* Quantise n bf16 values; writes n codes, *scale_out and (if non-NULL) *amax_out. */
+AMP_API int amp_fp8_quant_e4m3_dev(const void* x_bf16, int64_t n, uint8_t* q, float* scale_out,
+                           float* amax_out, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* amax of n bf16 values into *amax_out (device float); the first half of the
+ * quantiser, for sharded tensors whose global amax is an all-reduce(MAX) of
+ * the per-rank values. */
+AMP_API int amp_fp8_amax_bf16_dev(const void* x_bf16, int64_t n, float* amax_out, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* Second half: quantise with a given device-resident amax. */
+AMP_API int amp_fp8_quant_e4m3_from_amax_dev(const void* x_bf16, int64_t n, const float* amax_in,
+                                     uint8_t* q, float* scale_out, void* stream);
+
+/* Dequantise n codes with the device-resident scale into bf16. */
+AMP_API int amp_fp8_dequant_e4m3_dev(const uint8_t* q, int64_t n, const float* scale, void* y_bf16,
+                             void* stream);
+
+/* Host-pointer forms: quantise (and, if y_bf16 != NULL, dequantise back). */
+AMP_API int amp_user_fp8_quant_e4m3(const uint16_t* x_bf16, int64_t n, uint8_t* q, float* scale_out,
+                            uint16_t* y_bf16);
+AMP_API int amp_user_fp8_dequant_e4m3(const uint8_t* q, int64_t n, float scale, uint16_t* y_bf16);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AMP_B200_H */
