@@ -24,6 +24,7 @@ SIGNATURES: dict[str, tuple] = {
     "amp_fp8_amax_bf16_dev": (_i32, [_vp, _i64, _vp, _vp, _sz, _vp]),
     "amp_fp8_quant_e4m3_from_amax_dev": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp]),
     "amp_fp8_dequant_e4m3_dev": (_i32, [_vp, _i64, _vp, _vp, _vp]),
+    "amp_fp8_quant_e4m3_noalloc_dev": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp]),
     "amp_user_fp8_quant_e4m3": (_i32, [_vp, _i64, _vp, _vp, _vp]),
     "amp_user_fp8_dequant_e4m3": (_i32, [_vp, _i64, _f32, _vp]),
 }

@@ -22,6 +22,8 @@
 #include "common.cuh"
 #include "runtime.h"
 
+#include <mutex>
+
 namespace ampb {
 namespace {
 
@@ -323,3 +325,79 @@ int amp_user_fp8_dequant_e4m3(const uint8_t* q, int64_t n, float scale, uint16_t
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the per-tensor quantiser.
+//
+// Some callers cannot allocate device memory at the point where they
+// quantise: an inference-engine plugin whose enqueue() may only use memory
+// the engine handed it, code running while a CUDA graph is being captured
+// (cudaMalloc is not allowed there), or a host runtime that owns every
+// device allocation itself.  amp_fp8_quant_e4m3_dev asks them for a
+// workspace; this entry point instead keeps the amax pass's per-block
+// partial maxima in a file-scope device array, so the caller passes only the
+// input and the outputs.
+//
+// Limits and sharing rules:
+//   * the array holds kNoAllocParts floats (8 KiB) on every GPU that loads
+//     the library, for the life of the process;
+//   * the number of partials does not grow with n: the amax pass launches
+//     at most kNoAllocParts blocks (8 per SM, capped) and grid-strides over
+//     the tensor, so any n >= 0 is accepted; the entry point still checks
+//     the launch's partial count against the array size and returns
+//     AMP_ERR_INVALID with a message rather than overrun it;
+//   * every call on a device shares the array and leaves its contents
+//     behind; nothing in it has to start at zero (the amax pass overwrites
+//     every slot the encode pass reads), but two calls whose kernels
+//     overlap on the GPU (different streams, no ordering between them)
+//     race on it and may produce wrong scales;
+//   * the first call on each device looks up the array's device address
+//     with cudaGetSymbolAddress (the host-side name is only a stand-in);
+//     make that first call before capturing a stream into a CUDA graph.
+// ---------------------------------------------------------------------------
+namespace ampb {
+namespace {
+
+constexpr int kNoAllocParts = 2048;
+static __device__ __align__(256) float g_noalloc_parts[kNoAllocParts];
+
+constexpr int kMaxDevices = 64;
+float* g_noalloc_addr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// Device address of g_noalloc_parts on the current device (looked up once per device).
+int noalloc_scratch(float** out) {
+    int dev = -1;
+    AMPB_CHECK_CUDA(cudaGetDevice(&dev));
+    AMPB_REQUIRE(dev >= 0 && dev < kMaxDevices, AMP_ERR_UNSUPPORTED,
+                 "device ordinal %d beyond the %d devices the no-alloc quantiser tracks", dev,
+                 kMaxDevices);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_parts);
+        if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(g_noalloc_parts)");
+        g_noalloc_addr[dev] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_addr[dev];
+    return AMP_OK;
+}
+
+}  // namespace
+}  // namespace ampb
+
+extern "C" int amp_fp8_quant_e4m3_noalloc_dev(const void* x_bf16, int64_t n, uint8_t* q,
+                                              float* scale_out, float* amax_out, void* stream) {
+    using namespace ampb;
+    AMPB_REQUIRE(n >= 0, AMP_ERR_INVALID, "n must be >= 0 (got %lld)", (long long)n);
+    const int vec = aligned16(x_bf16);
+    const int parts_needed = grid_for(vec ? (n >> 3) : n);
+    AMPB_REQUIRE(parts_needed <= kNoAllocParts, AMP_ERR_INVALID,
+                 "no-alloc quantiser: this launch needs %d partial maxima but the static "
+                 "scratch holds %d", parts_needed, kNoAllocParts);
+    float* scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    return quant_e4m3_dev(x_bf16, n, q, scale_out, amax_out, scratch,
+                          (size_t)kNoAllocParts * sizeof(float), as_stream(stream));
+}

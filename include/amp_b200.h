@@ -75,6 +75,18 @@ AMP_API int amp_fp8_quant_e4m3_from_amax_dev(const void* x_bf16, int64_t n, cons
 AMP_API int amp_fp8_dequant_e4m3_dev(const uint8_t* q, int64_t n, const float* scale, void* y_bf16,
                              void* stream);
 
+/* Allocation-free form of amp_fp8_quant_e4m3_dev, for callers that may not
+ * allocate device memory (an engine plugin limited to memory the engine hands
+ * it, code running during CUDA graph capture, a runtime that owns all device
+ * allocations).  No counterpart in the reference.  The amax pass's partial
+ * maxima live in a library-owned 8 KiB device array per GPU (held until
+ * process exit), so only input and outputs are passed; any n >= 0 is
+ * accepted.  The first call on each device resolves that array's address
+ * (cudaGetSymbolAddress): make it before capturing a stream into a graph.
+ * Calls share the array: calls whose kernels overlap on one GPU race. */
+AMP_API int amp_fp8_quant_e4m3_noalloc_dev(const void* x_bf16, int64_t n, uint8_t* q,
+                                           float* scale_out, float* amax_out, void* stream);
+
 /* Host-pointer forms: quantise (and, if y_bf16 != NULL, dequantise back). */
 AMP_API int amp_user_fp8_quant_e4m3(const uint16_t* x_bf16, int64_t n, uint8_t* q, float* scale_out,
                             uint16_t* y_bf16);
