@@ -27,6 +27,14 @@ SIGNATURES: dict[str, tuple] = {
     "amp_fp8_quant_e4m3_noalloc_dev": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp]),
     "amp_user_fp8_quant_e4m3": (_i32, [_vp, _i64, _vp, _vp, _vp]),
     "amp_user_fp8_dequant_e4m3": (_i32, [_vp, _i64, _f32, _vp]),
+    "amp_device_status": (_i32, [_i32]),
+    "amp_gemm_bf16_dev": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp]),
+    "amp_gemm_fp8e4m3_dev": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _vp]),
+    "amp_user_gemm_bf16": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32]),
+    "amp_user_gemm_fp8e4m3": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32]),
+    "amp_gemm_fp32_dev": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp]),
+    "amp_gemm_fp32_tile_dev": (_i32, [_i32, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
+    "amp_user_gemm_fp32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32]),
 }
 
 

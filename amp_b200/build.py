@@ -79,9 +79,28 @@ def build(jobs: int | None = None, force: bool = False, verbose: bool = False) -
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}\n{r.stdout}")
         os.replace(tmp, LIB)
+    build_tools(force)
     if verbose:
         print(f"built {LIB}")
     return LIB
+
+
+TOOLS = PKG / "tools"
+
+
+def build_tools(force: bool = False) -> None:
+    """Host C++ tools linked against the library (rpath: the package dir)."""
+    out_dir = TOOLS / "bin"
+    out_dir.mkdir(exist_ok=True)
+    for src in sorted(TOOLS.glob("*.cpp")):
+        exe = out_dir / ("amp_b200_" + src.stem)
+        if force or _stale(exe, [src, LIB] + _deps()):
+            cmd = [nvcc(), "-O2", "-std=c++17", "-x", "cu", *ARCH, "-I", str(ROOT / "include"),
+                   str(src), "-o", str(exe), "-L", str(PKG), "-lamp_b200",
+                   "-Xlinker", "-rpath=$ORIGIN/../.."]
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode != 0:
+                raise RuntimeError(f"tool build failed for {src.name}:\n{r.stderr}")
 
 
 def main() -> None:

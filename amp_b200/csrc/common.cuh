@@ -7,6 +7,7 @@
 #include <cstdio>
 
 #include "../../include/amp_b200.h"
+#include "../../include/amp_plugin.h"
 
 namespace ampb {
 

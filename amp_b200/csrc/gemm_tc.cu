@@ -1,0 +1,443 @@
+// gemm_tc.cu -- bf16 and FP8 E4M3 GEMM on the 5th-generation tensor cores.
+//
+// Replaces the reference's bf16 WMMA kernel (kernels/matmul.cu:47-110: one
+// warp per 16x16 tile, operands staged through shared memory every k-step,
+// fp32 C) and its FP8 route (kernels/matmul.cu:235-270 -> cuBLASLt in
+// src/gemm_vendor.cpp:154-237, per-tensor scales, fp32 C).
+//
+// Layout is AMP's: A [M,K] row-major (K-major operand), B [K,N] row-major
+// (N-major operand, consumed as an MN-major UMMA operand, no transpose), C
+// [M,N] row-major in fp32 or bf16.
+//
+// Kernel structure (persistent, one 128x256 output tile per iteration, one
+// CTA per SM, 192 threads):
+//   warp 0      TMA producer: per 128-byte k-slab, one A box [128 rows x 128 B]
+//               and 256*es/128 B boxes [BK rows x 128 B], 128-byte swizzle,
+//               into a 4-stage ring guarded by full/empty mbarriers.
+//   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators);
+//               one lane issues tcgen05.mma (M=128, N=256, K=16 bf16 / 32 fp8,
+//               4 per k-slab) and commits each stage back to its empty barrier
+//               and each finished tile to the accumulator's full barrier.
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time from their TMEM lane
+//               quadrant, apply the FP8 scales, convert, store to global; the
+//               accumulator is released as soon as it has been read, so the
+//               next tile's MMAs overlap this tile's stores.
+// Tiles are visited in groups of 16 M-tiles (a ~2K-row band) so that the
+// CTAs running at the same time share A rows and B columns in L2.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "runtime.h"
+#include "tc_common.cuh"
+
+namespace ampb {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int SLAB = 128;        // bytes of K per stage (one 128-byte swizzle row)
+constexpr int STAGES = 4;
+constexpr int kThreads = 192;
+constexpr int kGroupM = 16;
+constexpr int A_STAGE_BYTES = BM * SLAB;           // 16 KiB
+constexpr int B_STAGE_BYTES = BN * SLAB;           // 32 KiB (BK rows x 256 cols x es)
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t TMEM_COLS = 512;
+
+enum ScaleMode : int { kNoScale = 0, kTensorScale = 1, kRowColScale = 2 };
+
+struct TcParams {
+    int M, N, K;
+    int num_m, num_n, num_kb;
+    void* C;
+    const float* scale_a;   // per-tensor: [1]; row/col: [M]
+    const float* scale_b;   // per-tensor: [1]; row/col: [N]
+    int scale_mode;
+    int* status;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
+    const int per_group = kGroupM * num_n;
+    const int g = t / per_group;
+    const int first_m = g * kGroupM;
+    const int gm = min(kGroupM, num_m - first_m);
+    const int local = t - g * per_group;
+    tm = first_m + local % gm;
+    tn = local / gm;
+}
+
+template <bool kFP8, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const TcParams p) {
+    constexpr int ES = kFP8 ? 1 : 2;                 // element size
+    constexpr int BK = SLAB / ES;                    // K elements per stage
+    constexpr int UMMA_K = 32 / ES;                  // K per MMA (32 bytes)
+    constexpr int B_BOX_COLS = SLAB / ES;            // N columns per B box
+    constexpr int B_BOXES = BN / B_BOX_COLS;         // 4 (bf16) or 2 (fp8)
+    constexpr int B_BOX_BYTES = BK * SLAB;           // 8 KiB or 16 KiB
+    constexpr uint32_t IDESC = make_idesc(kFP8 ? 0 : 1, kFP8 ? 0 : 1, 0, 1, BM, BN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int total = p.num_m * p.num_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                int tm, tn;
+                tile_coords(t, p.num_m, p.num_n, tm, tn);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1, p.status)) { ok = false; break; }
+                    uint8_t* sa = smem + s * STAGE_BYTES;
+                    uint8_t* sb = sa + A_STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+                    tma_load_2d(sa, &tmA, &full[s], kb * BK, tm * BM);
+#pragma unroll
+                    for (int j = 0; j < B_BOXES; ++j)
+                        tma_load_2d(sb + j * B_BOX_BYTES, &tmB, &full[s],
+                                    tn * BN + j * B_BOX_COLS, kb * BK);
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            int i = 0;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
+                const int acc = i & 1;
+                const uint32_t acc_ph = (i >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], acc_ph ^ 1, p.status)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+                    const uint32_t sb = sa + A_STAGE_BYTES;
+#pragma unroll
+                    for (int k = 0; k < SLAB / 32; ++k) {
+                        const uint64_t ad = smem_desc_sw128(sa + k * 32, 16, 1024);
+                        const uint64_t bd = smem_desc_sw128(sb + k * UMMA_K * SLAB, B_BOX_BYTES, 1024);
+                        if constexpr (kFP8)
+                            tc_mma_f8(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+                        else
+                            tc_mma_f16(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+                    }
+                    tc_commit(&empty[s]);
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+                if (ok) tc_commit(&tfull[acc]);
+            }
+            // Every MMA this thread issued has finished before TMEM is freed.
+            tc_commit(drain);
+            mbar_wait(drain, 0, p.status);
+        }
+    } else {
+        const int quad = warp & 3;             // TMEM lanes [32*quad, 32*quad + 32)
+        const int row_in_tile = quad * 32 + lane;
+        int i = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
+            const int acc = i & 1;
+            const uint32_t acc_ph = (i >> 1) & 1;
+            int tm, tn;
+            tile_coords(t, p.num_m, p.num_n, tm, tn);
+            if (!mbar_wait(&tfull[acc], acc_ph, p.status)) break;
+            tc_fence_after();
+            const int row = tm * BM + row_in_tile;
+            const bool row_ok = row < p.M;
+            float sa = 1.0f;
+            if (p.scale_mode == kTensorScale) sa = p.scale_a[0] * p.scale_b[0];
+            else if (p.scale_mode == kRowColScale && row_ok) sa = p.scale_a[row];
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                __syncwarp();  // tcgen05.ld is warp-collective: reconverge first
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
+                tmem_ld_wait();
+                if (c == BN / 32 - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[acc]);
+                }
+                const int col0 = tn * BN + c * 32;
+                if (col0 >= p.N) continue;  // warp-uniform
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * sa;
+                if (p.scale_mode == kRowColScale) {  // all lanes take part in the shuffles
+                    const float sbv = (col0 + lane < p.N) ? p.scale_b[col0 + lane] : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] *= __shfl_sync(0xffffffffu, sbv, j);
+                }
+                if (!row_ok) continue;
+                OutT* out = static_cast<OutT*>(p.C) + (int64_t)row * p.N + col0;
+                const bool full_chunk = col0 + 32 <= p.N &&
+                                        ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
+                if constexpr (sizeof(OutT) == 4) {
+                    if (full_chunk) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4*>(out + j) =
+                                make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    } else {
+                        for (int j = 0; j < 32 && col0 + j < p.N; ++j) out[j] = v[j];
+                    }
+                } else {
+                    if (full_chunk) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) {
+                            uint4 w;
+                            w.x = f32x2_to_bf16x2(v[j], v[j + 1]);
+                            w.y = f32x2_to_bf16x2(v[j + 2], v[j + 3]);
+                            w.z = f32x2_to_bf16x2(v[j + 4], v[j + 5]);
+                            w.w = f32x2_to_bf16x2(v[j + 6], v[j + 7]);
+                            *reinterpret_cast<uint4*>(out + j) = w;
+                        }
+                    } else {
+                        uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
+                        for (int j = 0; j < 32 && col0 + j < p.N; ++j)
+                            o16[j] = (uint16_t)(f32x2_to_bf16x2(v[j], 0.0f) & 0xffffu);
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode_fn(EncodeTiledFn* out) {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    static cudaError_t err = cudaSuccess;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+        if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = (EncodeTiledFn)p;
+    });
+    if (!fn) {
+        if (err != cudaSuccess) return cuda_status(err, "cudaGetDriverEntryPoint");
+        set_error(AMP_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled not available from the driver");
+        return AMP_ERR_UNSUPPORTED;
+    }
+    *out = fn;
+    return AMP_OK;
+}
+
+// Row-major [rows, cols] matrix of `es`-byte elements, box [box_rows, 128 bytes], 128B swizzle.
+int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int es,
+              int box_rows) {
+    EncodeTiledFn enc;
+    int rc = get_encode_fn(&enc);
+    if (rc) return rc;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * es)};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                     2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    AMPB_REQUIRE(r == CUDA_SUCCESS, AMP_ERR_INVALID,
+                 "cuTensorMapEncodeTiled failed (%d) for a %lld x %lld matrix", (int)r,
+                 (long long)rows, (long long)cols);
+    return AMP_OK;
+}
+
+template <bool kFP8, typename OutT>
+int launch_tc(const void* A, const void* B, void* C, int M, int N, int K, const float* sa,
+              const float* sb, int mode, cudaStream_t st) {
+    const int es = kFP8 ? 1 : 2;
+    AMPB_REQUIRE(M > 0 && N > 0 && K > 0, AMP_ERR_INVALID, "GEMM sizes must be positive");
+    AMPB_REQUIRE(A && B && C, AMP_ERR_INVALID, "NULL operand");
+    AMPB_REQUIRE((int64_t)K * es % 16 == 0 && (int64_t)N * es % 16 == 0, AMP_ERR_UNSUPPORTED,
+                 "tensor-core GEMM needs K and N to be multiples of %d (got K=%d N=%d)", 16 / es,
+                 K, N);
+    AMPB_REQUIRE(aligned16(A) && aligned16(B), AMP_ERR_INVALID,
+                 "A and B must be 16-byte aligned");
+    CUtensorMap tmA, tmB;
+    int rc;
+    if ((rc = make_tmap(&tmA, A, M, K, es, BM))) return rc;
+    if ((rc = make_tmap(&tmB, B, K, N, es, SLAB / es))) return rc;
+    int* status = nullptr;
+    if ((rc = device_status(&status))) return rc;
+    TcParams p;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.num_m = (M + BM - 1) / BM;
+    p.num_n = (N + BN - 1) / BN;
+    p.num_kb = (int)(((int64_t)K * es + SLAB - 1) / SLAB);
+    p.C = C;
+    p.scale_a = sa;
+    p.scale_b = sb;
+    p.scale_mode = mode;
+    p.status = status;
+    auto kern = k_gemm_tc<kFP8, OutT>;
+    static uint64_t attr_done = 0;  // one bit per device ordinal (< 64)
+    int dev = 0;
+    AMPB_CHECK_CUDA(cudaGetDevice(&dev));
+    if (dev >= 64 || !(attr_done >> dev & 1)) {
+        AMPB_CHECK_CUDA(
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        if (dev < 64) attr_done |= 1ull << dev;
+    }
+    const int total = p.num_m * p.num_n;
+    const int grid = total < sm_count() ? total : sm_count();
+    kern<<<grid, kThreads, SMEM_BYTES, st>>>(tmA, tmB, p);
+    AMPB_CHECK_LAUNCH("k_gemm_tc");
+    return AMP_OK;
+}
+
+}  // namespace
+
+int gemm_bf16_dev(const void* A, const void* B, void* C, int c_is_bf16, int M, int N, int K,
+                  cudaStream_t st) {
+    if (c_is_bf16)
+        return launch_tc<false, __nv_bfloat16>(A, B, C, M, N, K, nullptr, nullptr, kNoScale, st);
+    return launch_tc<false, float>(A, B, C, M, N, K, nullptr, nullptr, kNoScale, st);
+}
+
+int gemm_fp8_dev(const void* A, const void* B, const float* sa, const float* sb, int mode,
+                 void* C, int c_is_bf16, int M, int N, int K, cudaStream_t st) {
+    AMPB_REQUIRE(mode == kTensorScale || mode == kRowColScale, AMP_ERR_INVALID,
+                 "FP8 scale mode must be 1 (per tensor) or 2 (per row of A / column of B)");
+    AMPB_REQUIRE(sa && sb, AMP_ERR_INVALID, "FP8 GEMM needs both scale pointers");
+    if (c_is_bf16)
+        return launch_tc<true, __nv_bfloat16>(A, B, C, M, N, K, sa, sb, mode, st);
+    return launch_tc<true, float>(A, B, C, M, N, K, sa, sb, mode, st);
+}
+
+}  // namespace ampb
+
+using namespace ampb;
+
+extern "C" {
+
+int amp_gemm_bf16_dev(const void* A, const void* B, void* C, int c_dtype, int M, int N, int K,
+                      void* stream) {
+    AMPB_REQUIRE(c_dtype == AMP_DTYPE_F32 || c_dtype == AMP_DTYPE_BF16, AMP_ERR_INVALID,
+                 "C dtype must be AMP_DTYPE_F32 or AMP_DTYPE_BF16");
+    return gemm_bf16_dev(A, B, C, c_dtype == AMP_DTYPE_BF16, M, N, K, as_stream(stream));
+}
+
+int amp_gemm_fp8e4m3_dev(const uint8_t* A, const uint8_t* B, const float* scale_a,
+                         const float* scale_b, int scale_mode, void* C, int c_dtype, int M, int N,
+                         int K, void* stream) {
+    AMPB_REQUIRE(c_dtype == AMP_DTYPE_F32 || c_dtype == AMP_DTYPE_BF16, AMP_ERR_INVALID,
+                 "C dtype must be AMP_DTYPE_F32 or AMP_DTYPE_BF16");
+    return gemm_fp8_dev(A, B, scale_a, scale_b, scale_mode, C, c_dtype == AMP_DTYPE_BF16, M, N, K,
+                        as_stream(stream));
+}
+
+// Host-pointer forms (the plugin convention of amp_plugin.h): A, B, C in host
+// memory, all device work done and synchronised before returning.
+int amp_user_gemm_bf16(const uint16_t* A, const uint16_t* B, void* C, int c_dtype, int M, int N,
+                       int K) {
+    AMPB_REQUIRE(M > 0 && N > 0 && K > 0 && A && B && C, AMP_ERR_INVALID, "bad GEMM arguments");
+    AMPB_REQUIRE(c_dtype == AMP_DTYPE_F32 || c_dtype == AMP_DTYPE_BF16, AMP_ERR_INVALID,
+                 "C dtype must be AMP_DTYPE_F32 or AMP_DTYPE_BF16");
+    const size_t a = (size_t)M * K * 2, b = (size_t)K * N * 2;
+    const size_t c = (size_t)M * N * (c_dtype == AMP_DTYPE_F32 ? 4 : 2);
+    void *dA, *dB, *dC;
+    int rc;
+    if ((rc = staging_get(0, a, &dA)) || (rc = staging_get(1, b, &dB)) ||
+        (rc = staging_get(2, c, &dC)))
+        return rc;
+    cudaStream_t st = 0;
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(dA, A, a, cudaMemcpyHostToDevice, st));
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(dB, B, b, cudaMemcpyHostToDevice, st));
+    if ((rc = gemm_bf16_dev(dA, dB, dC, c_dtype == AMP_DTYPE_BF16, M, N, K, st))) return rc;
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(C, dC, c, cudaMemcpyDeviceToHost, st));
+    AMPB_CHECK_CUDA(cudaStreamSynchronize(st));
+    return amp_device_status(1);
+}
+
+int amp_user_gemm_fp8e4m3(const uint8_t* A, const uint8_t* B, const float* scale_a,
+                          const float* scale_b, int scale_mode, void* C, int c_dtype, int M,
+                          int N, int K) {
+    AMPB_REQUIRE(M > 0 && N > 0 && K > 0 && A && B && C && scale_a && scale_b, AMP_ERR_INVALID,
+                 "bad GEMM arguments");
+    AMPB_REQUIRE(c_dtype == AMP_DTYPE_F32 || c_dtype == AMP_DTYPE_BF16, AMP_ERR_INVALID,
+                 "C dtype must be AMP_DTYPE_F32 or AMP_DTYPE_BF16");
+    AMPB_REQUIRE(scale_mode == 1 || scale_mode == 2, AMP_ERR_INVALID, "scale_mode must be 1 or 2");
+    const size_t a = (size_t)M * K, b = (size_t)K * N;
+    const size_t c = (size_t)M * N * (c_dtype == AMP_DTYPE_F32 ? 4 : 2);
+    const size_t ns_a = scale_mode == 2 ? (size_t)M : 1, ns_b = scale_mode == 2 ? (size_t)N : 1;
+    void *dA, *dB, *dC, *dS;
+    int rc;
+    if ((rc = staging_get(0, a, &dA)) || (rc = staging_get(1, b, &dB)) ||
+        (rc = staging_get(2, c, &dC)) || (rc = staging_get(3, (ns_a + ns_b) * 4, &dS)))
+        return rc;
+    float* dsa = static_cast<float*>(dS);
+    float* dsb = dsa + ns_a;
+    cudaStream_t st = 0;
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(dA, A, a, cudaMemcpyHostToDevice, st));
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(dB, B, b, cudaMemcpyHostToDevice, st));
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(dsa, scale_a, ns_a * 4, cudaMemcpyHostToDevice, st));
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(dsb, scale_b, ns_b * 4, cudaMemcpyHostToDevice, st));
+    if ((rc = gemm_fp8_dev(dA, dB, dsa, dsb, scale_mode, dC, c_dtype == AMP_DTYPE_BF16, M, N, K,
+                           st)))
+        return rc;
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(C, dC, c, cudaMemcpyDeviceToHost, st));
+    AMPB_CHECK_CUDA(cudaStreamSynchronize(st));
+    return amp_device_status(1);
+}
+
+}  // extern "C"

@@ -73,9 +73,44 @@ int staging_get(int slot, size_t bytes, void** out) {
     return AMP_OK;
 }
 
+namespace {
+std::mutex g_status_mu;
+std::vector<int*> g_status;  // [device]
+}  // namespace
+
+int device_status(int** out) {
+    int dev = 0;
+    AMPB_CHECK_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(g_status_mu);
+    if ((int)g_status.size() <= dev) g_status.resize(dev + 1, nullptr);
+    if (!g_status[dev]) {
+        int* p = nullptr;
+        AMPB_CHECK_CUDA(cudaMalloc(&p, sizeof(int)));
+        AMPB_CHECK_CUDA(cudaMemset(p, 0, sizeof(int)));
+        g_status[dev] = p;
+    }
+    *out = g_status[dev];
+    return AMP_OK;
+}
+
 }  // namespace ampb
 
 extern "C" {
+
+int amp_device_status(int clear) {
+    int* p = nullptr;
+    int rc = ampb::device_status(&p);
+    if (rc) return rc;
+    int v = 0;
+    AMPB_CHECK_CUDA(cudaDeviceSynchronize());
+    AMPB_CHECK_CUDA(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v && clear) AMPB_CHECK_CUDA(cudaMemset(p, 0, sizeof(int)));
+    if (v) {
+        ampb::set_error(AMP_ERR_TIMEOUT, "a kernel's bounded wait expired (device status %d)", v);
+        return AMP_ERR_TIMEOUT;
+    }
+    return AMP_OK;
+}
 
 const char* amp_last_error(void) { return ampb::g_msg; }
 

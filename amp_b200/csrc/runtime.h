@@ -9,4 +9,8 @@ namespace ampb {
 // hold several live buffers.  Not re-entrant across threads for one slot.
 int staging_get(int slot, size_t bytes, void** out);
 
+// Per-device status word written by kernels whose bounded waits expired
+// (AMP_DEV_ERR_TIMEOUT); allocated and zeroed on first use.
+int device_status(int** out);
+
 }  // namespace ampb

@@ -42,3 +42,11 @@ def quant_input_torch(n: int = QUANT_N, seed: int = 0, device="cuda"):
         pos = torch.randperm(n, generator=g, device=device)[:k]
         x[pos] = torch.randn(k, generator=g, device=device) * QUANT_OUTLIER_STD
     return x.to(torch.bfloat16)
+
+
+# fp32 GEMM workload (AMP's amp_verify_matmul shape class): A, B ~ U[-1, 1], seed 0.
+def gemm_fp32_inputs(M: int, N: int, K: int, seed: int = 0):
+    rng = np.random.default_rng(seed)
+    A = rng.uniform(-1.0, 1.0, (M, K)).astype(np.float32)
+    B = rng.uniform(-1.0, 1.0, (K, N)).astype(np.float32)
+    return A, B

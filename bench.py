@@ -2,25 +2,30 @@
 """Benchmark of the B200 hot path; prints ONE JSON line (rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
-                    [--impl amp_b200|reference]
+                    [--impl amp_b200|reference] [--size S]
 
-Default workload ``fp8_quant``: per-tensor amax-scaled FP8 E4M3 quantise +
-dequantise of 2^26 bf16 values (N(0,1) with 0.1% N(0,50) outliers).  One step
-is one quantise (amax pass + encode pass) and one dequantise of the whole
-tensor; the metric is algorithmic bytes moved (8 B/element: 5 quantise +
-3 dequantise) per second.  For N > 1 (torchrun, one process per GPU) every
-rank quantises its own 2^26-element shard (weak scaling) against the global
-amax, obtained by a 1-float NCCL all-reduce(MAX) inside the step.
+Workloads (``--workload``):
+  fp8_quant (default)  per-tensor amax-scaled FP8 E4M3 quantise + dequantise of
+                       2^26 bf16 values (N(0,1), 0.1% N(0,50) outliers); metric =
+                       algorithmic bytes (8 B/element) per second.  N > 1: each
+                       rank its own 2^26 shard against the global amax (1-float
+                       NCCL all-reduce MAX in the step), weak scaling.
+  gemm_bf16            C = A @ B, M=N=K=S (default 8192), bf16 in, fp32 accumulate,
+                       bf16 out; metric = 2*S^3 FLOP per second.  N > 1: B and C
+                       split along N, C all-gathered over NCCL (strong scaling).
+  gemm_fp8             same with E4M3 operands, per-row A / per-column B scales.
 
-Timing: W untimed warm-up steps; then K steps, each bracketed by CUDA events
-on the launching stream, with a 256 MiB L2 flush before every step (outside
-the events); barrier + synchronize on both sides; max over ranks.
-``e2e`` repeats the metric through the host-pointer C entry point
-(pinned host input, H2D + kernels + D2H inside the timed region).
+Timing: W untimed warm-up steps; then K steps, each bracketed by CUDA events on
+the launching stream with a 256 MiB L2 flush before every step (outside the
+events); barrier + synchronize on both sides; the max over ranks.  NVML samples
+SM clocks and throttle reasons during the timed region.  ``e2e`` repeats the
+metric through the host-pointer C entry point (pinned host buffers, H2D +
+kernels + D2H inside the timed region).  ``roofline`` reports the dominant
+kernel: algorithmic bytes (or FLOPs) per launch over its event-timed duration.
 
-``--impl reference`` times AMP's own CPU codec (include/fp8.hpp, compiled from
-the reference sources into oracle/_ref) on this host's cores, on a bounded
-sample of the same workload; without that build it times the oracle port.
+``--impl reference`` times the reference's own CPU code for the workload on this
+host's cores (built from the AMP sources into oracle/_ref), on a bounded sample;
+without that build it times the oracle's restatement.
 """
 from __future__ import annotations
 
@@ -45,14 +50,17 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def load_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
-        d = json.loads(p.read_text())
-        return d, "measured"
+        return json.loads(p.read_text()), "measured"
     return dict(PEAKS_FALLBACK), "fallback"
 
 
 def load_traffic():
     p = ROOT / "profiles" / "traffic.json"
     return json.loads(p.read_text()) if p.exists() else {}
+
+
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0))
 
 
 # --------------------------------------------------------------------------
@@ -66,8 +74,8 @@ class Dist:
         self.pg = None
         if self.world > 1:
             import datetime
-            import torch.distributed as dist
             import torch
+            import torch.distributed as dist
             torch.cuda.set_device(self.local_rank)
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                     device_id=torch.device("cuda", self.local_rank))
@@ -97,17 +105,17 @@ class Dist:
 # --------------------------------------------------------------------------
 class ClockSampler:
     REASONS = {
-        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
-        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
-        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
-        0x100: "display_clock_setting",
+        0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.01):
+    def __init__(self, device_index: int, period_s: float = 0.005):
         self.samples: list[tuple[int, int]] = []
         self.max_mhz = None
         self._stop = threading.Event()
         self._t = None
+        self.period = period_s
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -116,7 +124,6 @@ class ClockSampler:
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
         except Exception:  # NVML absent: report no samples rather than fail the bench
             self.nv = None
-        self.period = period_s
 
     def _run(self):
         while not self._stop.is_set():
@@ -142,13 +149,26 @@ class ClockSampler:
     def summary(self):
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
-        mhz = [m for m, _ in self.samples]
         bits = 0
         for _, r in self.samples:
             bits |= r
-        reasons = sorted(v for k, v in self.REASONS.items() if bits & k and k != 0x1)
-        return {"sm_mhz": float(statistics.median(mhz)), "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(mhz)}
+        return {"sm_mhz": float(statistics.median(m for m, _ in self.samples)),
+                "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(v for k, v in self.REASONS.items() if bits & k),
+                "samples": len(self.samples)}
+
+
+def timed_reps(fn, budget_s: float):
+    """Run fn repeatedly for ~budget_s seconds; returns (reps, seconds)."""
+    fn()
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        fn()
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= budget_s:
+            return reps, dt
 
 
 # --------------------------------------------------------------------------
@@ -158,59 +178,60 @@ class QuantWorkload:
     name = "fp8_quant"
     metric = "fp8_e4m3_quant_dequant_GBps"
     unit = "GB/s"
+    scale = 1e9
     dtype = "bf16->e4m3->bf16"
+    bound = "hbm"
+    scaling = "weak"
     bytes_per_elem = 8  # quantise 5 (amax read 2 + read 2 + write 1) + dequantise 3
 
-    def __init__(self, dist: Dist, n: int):
+    def __init__(self, dist: Dist, args):
         import torch
         from amp_b200 import fp8, workloads
         self.torch, self.fp8, self.dist = torch, fp8, dist
-        self.n = n
+        self.n = n = args.elements
         dev = torch.device("cuda", torch.cuda.current_device())
         self.x = workloads.quant_input_torch(n, seed=1234 + dist.rank, device=dev)
         self.q = torch.empty(n, dtype=torch.uint8, device=dev)
         self.y = torch.empty(n, dtype=torch.bfloat16, device=dev)
-        self.scale = torch.empty(1, dtype=torch.float32, device=dev)
+        self.scale_t = torch.empty(1, dtype=torch.float32, device=dev)
         self.amax = torch.empty(1, dtype=torch.float32, device=dev)
         self.ws = torch.empty(fp8.workspace_bytes(n), dtype=torch.uint8, device=dev)
-        self.stream = torch.cuda.current_stream()
-        self.kernel_events = None
+
+    def units_per_step(self) -> float:
+        return self.bytes_per_elem * self.n
 
     def launches_per_step(self) -> int:
         return 3 if self.dist.world == 1 else 4
 
     def config(self):
         return {"workload": "fp8_e4m3_per_tensor_quant_dequant", "elements_per_gpu": self.n,
+                "global_elements": self.n * self.dist.world,
                 "input": "bf16 N(0,1) + 0.1% N(0,50) outliers (seeded, synthetic)",
-                "scale": "amax/448, RNE satfinite", "global_elements": self.n * self.dist.world,
-                "l2": "256 MiB flush before every timed step",
+                "scale": "amax/448, RNE satfinite", "l2": "256 MiB flush before every step",
                 "parallelism": f"shard{self.dist.world}+allreduce_max(1 float)"
                 if self.dist.world > 1 else "single"}
 
-    def step(self, ev=None):
-        fp8, torch = self.fp8, self.torch
+    def kernel_table(self):
         if self.dist.world == 1:
-            if ev: ev[0].record()
-            fp8.quantize_e4m3(self.x, workspace=self.ws, out=self.q, scale=self.scale)
-            if ev: ev[1].record()
-            fp8.dequantize_e4m3(self.q, self.scale, out=self.y)
-            if ev: ev[2].record()
-        else:
+            return [("quantise (k_amax_partials + k_quant_encode)", 5 * self.n),
+                    ("dequantise (k_dequant)", 3 * self.n)]
+        return [("encode_from_amax (k_quant_encode)", 3 * self.n),
+                ("dequantise (k_dequant)", 3 * self.n)]
+
+    def step(self, ev=None):
+        fp8 = self.fp8
+        if self.dist.world > 1:
             fp8.amax_bf16(self.x, workspace=self.ws, out=self.amax)
             self.dist.pg.all_reduce(self.amax, op=self.dist.pg.ReduceOp.MAX)
-            if ev: ev[0].record()
-            fp8.quantize_e4m3_from_amax(self.x, self.amax, out=self.q, scale=self.scale)
-            if ev: ev[1].record()
-            fp8.dequantize_e4m3(self.q, self.scale, out=self.y)
-            if ev: ev[2].record()
-
-    def kernel_table(self):
-        """(name, algorithmic bytes per launch) for the per-kernel event spans."""
+        if ev: ev[0].record()
         if self.dist.world == 1:
-            return [("quantise (amax + encode)", 5 * self.n), ("dequantise", 3 * self.n)]
-        return [("encode_from_amax", 3 * self.n), ("dequantise", 3 * self.n)]
+            fp8.quantize_e4m3(self.x, workspace=self.ws, out=self.q, scale=self.scale_t)
+        else:
+            fp8.quantize_e4m3_from_amax(self.x, self.amax, out=self.q, scale=self.scale_t)
+        if ev: ev[1].record()
+        fp8.dequantize_e4m3(self.q, self.scale_t, out=self.y)
+        if ev: ev[2].record()
 
-    # ---- end to end through the host-pointer C entry point -------------
     def e2e(self, steps: int, warmup: int):
         torch = self.torch
         from amp_b200._lib import call
@@ -220,31 +241,17 @@ class QuantWorkload:
         yh = torch.empty(n, dtype=torch.bfloat16).pin_memory()
         sc = C.c_float()
         args = (xh.data_ptr(), n, qh.data_ptr(), C.byref(sc), yh.data_ptr())
-        for _ in range(warmup):
-            call("amp_user_fp8_quant_e4m3", *args)
-        legacy = torch.cuda.default_stream()  # the entry point enqueues on stream 0
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        times = []
-        for _ in range(steps):
-            s.record(legacy)
-            call("amp_user_fp8_quant_e4m3", *args)
-            e.record(legacy)
-            e.synchronize()
-            times.append(s.elapsed_time(e))
-        ms = sum(times) / len(times)
-        return {"value": self.bytes_per_elem * n / (ms * 1e-3) / 1e9, "unit": self.unit,
+        ms = _e2e_time(torch, lambda: call("amp_user_fp8_quant_e4m3", *args), steps, warmup)
+        return {"value": self.units_per_step() / (ms * 1e-3) / self.scale, "unit": self.unit,
                 "ms_per_step": ms, "h2d_bytes_per_step": 2 * n,
                 "d2h_bytes_per_step": n + 2 * n + 4, "api": "amp_user_fp8_quant_e4m3"}
 
-    # ---- CPU baseline: AMP's own codec on the host cores ----------------
-    @staticmethod
-    def cpu_baseline(n_full: int, budget_s: float = 10.0):
+    @classmethod
+    def cpu_reference(cls, args, budget_s: float, threads: int):
         import oracle
         from amp_b200 import workloads
-        threads = len(os.sched_getaffinity(0))
         r = oracle.ref_lib()
-        sample = min(n_full, 1 << 22)
+        sample = min(args.elements, 1 << 22)
         xb = workloads.quant_input_numpy(sample, seed=3)
         q = np.empty(sample, np.uint8)
         y = np.empty(sample, np.uint16)
@@ -254,164 +261,272 @@ class QuantWorkload:
             def run():
                 r.ref_quant_dequant_bf16(xb.ctypes.data, sample, q.ctypes.data, y.ctypes.data,
                                          threads)
+            what = "AMP fp8::f32_to_e4m3/e4m3_to_f32 (include/fp8.hpp) + amax loop"
         else:
             kind, cores = "port", 1
 
             def run():
                 qq, s, _ = oracle.quant_e4m3(xb)
                 oracle.dequant_e4m3(qq, s)
-        run()
-        t0 = time.perf_counter()
-        reps = 0
-        while True:
-            run()
-            reps += 1
-            if time.perf_counter() - t0 >= budget_s:
-                break
-        dt = time.perf_counter() - t0
-        v = QuantWorkload.bytes_per_elem * sample * reps / dt / 1e9
-        what = ("AMP fp8::f32_to_e4m3/e4m3_to_f32 (include/fp8.hpp) + amax loop, "
-                f"{threads} host threads" if kind == "reference"
-                else "oracle restatement (oracle/oracle.c), 1 thread")
-        return {"value": v, "unit": "GB/s", "cores": cores, "kind": kind,
-                "sample": f"{reps} x {sample} bf16 elements of the same distribution "
-                          f"({dt:.1f} s); {what}"}
+            what = "oracle restatement (oracle/oracle.c)"
+        reps, dt = timed_reps(run, budget_s)
+        return {"value": cls.bytes_per_elem * sample * reps / dt / cls.scale, "unit": cls.unit,
+                "cores": cores, "kind": kind,
+                "sample": f"{reps} x {sample} bf16 elements of the same distribution in "
+                          f"{dt:.1f} s; {what}, {cores} host thread(s)"}
 
 
-WORKLOADS = {"fp8_quant": QuantWorkload}
+class GemmWorkload:
+    name = "gemm_bf16"
+    metric = "bf16_gemm_TFLOPS"
+    unit = "TFLOP/s"
+    scale = 1e12
+    dtype = "bf16"
+    bound = "tensor"
+    scaling = "strong"
+    fp8 = False
+
+    def __init__(self, dist: Dist, args):
+        import torch
+        from amp_b200 import gemm
+        self.torch, self.gemm, self.dist = torch, gemm, dist
+        S = self.S = args.size
+        p = dist.world
+        if S % (256 * p):
+            raise SystemExit(f"--size must be a multiple of {256 * p} for {p} GPUs")
+        self.Np = S // p
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev)
+        g.manual_seed(77)
+        a = torch.randn(S, S, generator=g, device=dev)
+        b = torch.randn(S, S, generator=g, device=dev)[:, dist.rank * self.Np:(dist.rank + 1) * self.Np]
+        if self.fp8:
+            amax_a = a.abs().amax(dim=1).clamp_min(1e-30)
+            amax_b = b.abs().amax(dim=0).clamp_min(1e-30)
+            self.sa = (amax_a / 448.0).float().contiguous()
+            self.sb = (amax_b / 448.0).float().contiguous()
+            self.A = (a / self.sa[:, None]).to(torch.float8_e4m3fn).view(torch.uint8).contiguous()
+            self.B = (b / self.sb[None, :]).to(torch.float8_e4m3fn).view(torch.uint8).contiguous()
+        else:
+            self.A = a.to(torch.bfloat16).contiguous()
+            self.B = b.to(torch.bfloat16).contiguous()
+        del a, b
+        self.C = torch.empty(S, self.Np, dtype=torch.bfloat16, device=dev)
+        self.Cfull = (torch.empty(p, S, self.Np, dtype=torch.bfloat16, device=dev)
+                      if p > 1 else None)
+
+    def units_per_step(self) -> float:
+        return 2.0 * self.S * self.S * self.Np
+
+    def launches_per_step(self) -> int:
+        return 1
+
+    def config(self):
+        p = self.dist.world
+        return {"workload": f"{'fp8_e4m3' if self.fp8 else 'bf16'}_gemm", "M": self.S,
+                "N": self.S, "K": self.S, "out": "bf16",
+                "inputs": "N(0,1)" + (" quantised per row (A) / per column (B), amax/448"
+                                      if self.fp8 else ""),
+                "l2": "operands (2 x %d MiB) exceed L2; 256 MiB flush before every step"
+                      % (self.S * self.S * (1 if self.fp8 else 2) >> 20),
+                "parallelism": f"N-split over {p} GPUs + NCCL all-gather of C" if p > 1
+                else "single"}
+
+    def kernel_table(self):
+        return [(f"k_gemm_tc<{'e4m3' if self.fp8 else 'bf16'}>", self.units_per_step())]
+
+    def _launch(self):
+        if self.fp8:
+            self.gemm.launch_matmul_fp8e4m3(self.A, self.B, self.C, self.S, self.Np, self.S,
+                                            self.sa, self.sb)
+        else:
+            self.gemm.launch_matmul_bf16(self.A, self.B, self.C, self.S, self.Np, self.S)
+
+    def step(self, ev=None):
+        if ev: ev[0].record()
+        self._launch()
+        if ev: ev[1].record()
+        if self.dist.world > 1:
+            self.dist.pg.all_gather_into_tensor(self.Cfull, self.C)
+
+    def e2e(self, steps: int, warmup: int):
+        torch = self.torch
+        from amp_b200._lib import call
+        S, Np = self.S, self.Np
+        Ah = self.A.cpu().pin_memory()
+        Bh = self.B.cpu().pin_memory()
+        Ch = torch.empty(S, Np, dtype=torch.bfloat16).pin_memory()
+        if self.fp8:
+            sah, sbh = self.sa.cpu().pin_memory(), self.sb.cpu().pin_memory()
+            fn = lambda: call("amp_user_gemm_fp8e4m3", Ah.data_ptr(), Bh.data_ptr(),
+                              sah.data_ptr(), sbh.data_ptr(), 2, Ch.data_ptr(), 1, S, Np, S)
+            h2d = Ah.numel() + Bh.numel() + 4 * (S + Np)
+        else:
+            fn = lambda: call("amp_user_gemm_bf16", Ah.data_ptr(), Bh.data_ptr(), Ch.data_ptr(), 1,
+                              S, Np, S)
+            h2d = 2 * (Ah.numel() + Bh.numel())
+        ms = _e2e_time(torch, fn, steps, warmup)
+        return {"value": self.units_per_step() / (ms * 1e-3) / self.scale, "unit": self.unit,
+                "ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 2 * S * Np,
+                "api": "amp_user_gemm_fp8e4m3" if self.fp8 else "amp_user_gemm_bf16"}
+
+    @classmethod
+    def cpu_reference(cls, args, budget_s: float, threads: int):
+        """AMP's cpu_reference_gemm on a block of C rows (fp32 operands)."""
+        import oracle
+        S = args.size
+        g = oracle.ref_gemm_lib()
+        rng = np.random.default_rng(0)
+        B = rng.standard_normal((S, S), dtype=np.float32)
+        rows = max(threads, 1)
+        A = rng.standard_normal((rows, S), dtype=np.float32)
+        Cm = np.empty((rows, S), np.float32)
+        if g is not None:
+            kind, cores = "reference", threads
+            run = lambda: g.ref_cpu_reference_gemm_mt(A.ctypes.data, B.ctypes.data,
+                                                      Cm.ctypes.data, rows, S, S, threads)
+            what = "AMP cpu_reference_gemm (tests/amp_validate_kernel.cpp), rows split over threads"
+        else:
+            kind, cores = "port", 1
+            run = lambda: oracle.lib().orc_gemm_fp32_amp(A.ctypes.data, B.ctypes.data,
+                                                         Cm.ctypes.data, rows, S, S)
+            what = "oracle restatement of AMP's cpu_reference_gemm"
+        reps, dt = timed_reps(run, budget_s)
+        flops = 2.0 * rows * S * S * reps
+        return {"value": flops / dt / cls.scale, "unit": cls.unit, "cores": cores, "kind": kind,
+                "sample": f"{reps} x ({rows} rows of C, N=K={S}) in {dt:.1f} s; {what}, fp32"}
 
 
-def l2_flusher(torch):
-    buf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+class GemmFp8Workload(GemmWorkload):
+    name = "gemm_fp8"
+    metric = "fp8_e4m3_gemm_TFLOPS"
+    dtype = "e4m3"
+    fp8 = True
 
-    def flush():
-        buf.zero_()
-    return flush
+
+WORKLOADS = {w.name: w for w in (QuantWorkload, GemmWorkload, GemmFp8Workload)}
+
+
+def _e2e_time(torch, fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    legacy = torch.cuda.default_stream()  # the host-pointer entry points use stream 0
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        s.record(legacy)
+        fn()
+        e.record(legacy)
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    return sum(times) / len(times)
+
+
+def peak_for(W, peaks):
+    if W.bound == "hbm":
+        return peaks["hbm_gbs"], "GB/s", "hbm_gbs"
+    bf16 = peaks["bf16_tflops"]
+    if getattr(W, "fp8", False):
+        return 2 * bf16, "TFLOP/s", "2 x bf16_tflops (dense FP8 = 2x bf16 rate)"
+    return bf16, "TFLOP/s", "bf16_tflops (burst)"
 
 
 def run_amp(args, dist: Dist):
     import torch
-    from amp_b200 import build as ampbuild
     import amp_b200
+    from amp_b200 import build as ampbuild
     if not amp_b200.LIB_PATH.exists():
         ampbuild.build()
     torch.cuda.set_device(dist.local_rank)
-    W = WORKLOADS[args.workload](dist, args.elements)
-    flush = l2_flusher(torch)
+    W = WORKLOADS[args.workload](dist, args)
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     for _ in range(args.warmup):
-        flush()
+        flush_buf.zero_()
         W.step()
     nk = len(W.kernel_table())
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)]
-              for _ in range(args.steps)]
-    step_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(args.steps)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] for _ in range(args.steps)]
+    sev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
-    dev_index = torch.cuda.current_device()
     phys = os.environ.get("CUDA_VISIBLE_DEVICES")
+    dev_index = torch.cuda.current_device()
     nvml_index = int(phys.split(",")[dev_index]) if phys else dev_index
     with ClockSampler(nvml_index) as clocks:
         for i in range(args.steps):
-            flush()
-            step_ev[i][0].record()
-            W.step(events[i])
-            step_ev[i][1].record()
+            flush_buf.zero_()
+            sev[i][0].record()
+            W.step(ev[i])
+            sev[i][1].record()
         torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
-    step_ms = [a.elapsed_time(b) for a, b in step_ev]
-    total_ms = dist.max(sum(step_ms))
+    from amp_b200._lib import lib
+    if lib().amp_device_status(1) != 0:
+        raise SystemExit("a kernel reported a device-side timeout during the timed region")
+    total_ms = dist.max(sum(a.elapsed_time(b) for a, b in sev))
     ms_per_step = total_ms / args.steps
-    units = W.bytes_per_elem * W.n * dist.world
-    value = units / (ms_per_step * 1e-3) / 1e9
+    value = W.units_per_step() * dist.world / (ms_per_step * 1e-3) / W.scale
 
-    # per-kernel spans -> dominant kernel roofline
     spans = []
-    for k, (name, algo_bytes) in enumerate(W.kernel_table()):
-        ms = statistics.mean(events[i][k].elapsed_time(events[i][k + 1])
-                             for i in range(args.steps))
-        spans.append((ms, name, algo_bytes))
+    for k, (kname, units) in enumerate(W.kernel_table()):
+        ms = statistics.mean(ev[i][k].elapsed_time(ev[i][k + 1]) for i in range(args.steps))
+        spans.append((ms, kname, units))
     spans.sort(reverse=True)
-    dom_ms, dom_name, dom_bytes = spans[0]
+    dom_ms, dom_name, dom_units = spans[0]
     peaks, peak_src = load_peaks()
-    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
-    traffic = load_traffic().get(W.name, {}).get(dom_name)
-    roofline = {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1),
-                "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": round(achieved / peaks["hbm_gbs"], 4),
-                "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"
-                if peak_src == "measured" else "fallback 6650 GB/s",
-                "traffic": traffic, "algorithmic_bytes": dom_bytes,
-                "kernel_ms": round(dom_ms, 5),
+    peak, punit, pkey = peak_for(W, peaks)
+    achieved = dom_units / (dom_ms * 1e-3) / W.scale
+    roofline = {"bound": W.bound, "kernel": dom_name, "achieved": round(achieved, 2),
+                "peak": round(peak, 1), "unit": punit, "frac": round(achieved / peak, 4),
+                "peak_source": f"{peak_src}: MEASURED_PEAKS.json {pkey}" if peak_src == "measured"
+                else "fallback figure of the profiling recipe",
+                "traffic": load_traffic().get(W.name, {}).get(dom_name),
+                "algorithmic_units_per_launch": dom_units, "kernel_ms": round(dom_ms, 5),
                 "all_kernels": [{"kernel": n, "ms": round(m, 5),
-                                 "GBps": round(b / (m * 1e-3) / 1e9, 1)} for m, n, b in spans]}
-
-    e2e = W.e2e(max(3, min(args.steps, 20)), 2)
+                                 "rate": round(u / (m * 1e-3) / W.scale, 2)}
+                                for m, n, u in spans]}
+    e2e = None
+    if not args.skip_e2e:
+        e2e = W.e2e(max(3, min(args.steps, 10)), 2)
+        e2e["ms_per_step"] = dist.max(e2e["ms_per_step"])  # every rank runs it on its shard
+        e2e["value"] = W.units_per_step() * dist.world / (e2e["ms_per_step"] * 1e-3) / W.scale
     out = {
-        "metric": W.metric, "value": round(value, 2), "unit": W.unit, "n_gpus": dist.world,
+        "metric": W.metric, "value": round(value, 3), "unit": W.unit, "n_gpus": dist.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": W.dtype, "data": "synthetic (seeded, reference distribution)",
-        "config": W.config(), "impl": "amp_b200",
-        "gpu_launches": W.launches_per_step() * args.steps,
+        "higher_is_better": True, "scaling": W.scaling, "vs_baseline": None,
+        "dtype": W.dtype, "data": "synthetic (seeded)", "config": W.config(),
+        "impl": "amp_b200", "gpu_launches": W.launches_per_step() * args.steps,
         "clocks": clocks.summary(), "roofline": roofline,
-        "e2e": {k: (round(v, 3) if isinstance(v, float) else v) for k, v in e2e.items()},
+        "e2e": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in e2e.items()}
+        if e2e else None,
     }
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = WORKLOADS[args.workload].cpu_baseline(W.n)
+        out["cpu_baseline"] = W.cpu_reference(args, budget_s=10.0, threads=host_threads())
     return out
 
 
-def run_reference(args, dist: Dist):
+def run_reference(args):
+    """The reference's own CPU code for the workload, on this host (rank 0 only)."""
     W = WORKLOADS[args.workload]
-    if dist.rank != 0:
-        return None
-    n = args.elements
-    import oracle
-    from amp_b200 import workloads
-    threads = len(os.sched_getaffinity(0))
-    r = oracle.ref_lib()
-    sample = min(n, 1 << 22)
-    xb = workloads.quant_input_numpy(sample, seed=3)
-    q = np.empty(sample, np.uint8)
-    y = np.empty(sample, np.uint16)
-    if r is not None:
-        kind = "reference"
-
-        def run():
-            r.ref_quant_dequant_bf16(xb.ctypes.data, sample, q.ctypes.data, y.ctypes.data,
-                                     threads)
-    else:
-        kind, threads = "port", 1
-
-        def run():
-            qq, s, _ = oracle.quant_e4m3(xb)
-            oracle.dequant_e4m3(qq, s)
+    threads = host_threads()
+    # each step is one bounded sample of the workload (about a second of CPU work)
     for _ in range(args.warmup):
-        run()
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        run()
-        times.append(time.perf_counter() - t0)
-    ms = 1e3 * sum(times) / len(times)
-    v = W.bytes_per_elem * sample / (ms * 1e-3) / 1e9
-    sample_desc = (f"each step {sample} of the {n} bf16 elements (same distribution); "
-                   + ("AMP fp8::f32_to_e4m3/e4m3_to_f32 (include/fp8.hpp) + amax loop"
-                      if kind == "reference" else "oracle restatement (oracle/oracle.c)"))
+        W.cpu_reference(args, budget_s=0.0, threads=threads)
+    vals = [W.cpu_reference(args, budget_s=1.0, threads=threads) for _ in range(args.steps)]
+    v = statistics.mean(x["value"] for x in vals)
+    cb = dict(vals[-1])
+    cb["value"] = round(v, 4)
     return {
-        "metric": W.metric, "value": round(v, 3), "unit": W.unit, "n_gpus": dist.world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": W.dtype, "data": "synthetic (seeded, reference distribution)",
-        "config": {"workload": "fp8_e4m3_per_tensor_quant_dequant", "elements_per_gpu": n,
-                   "sample_elements_per_step": sample},
-        "impl": "reference",
-        "cpu_baseline": {"value": round(v, 3), "unit": W.unit, "cores": threads, "kind": kind,
-                         "sample": sample_desc},
-        "e2e": {"value": round(v, 3), "unit": W.unit, "h2d_bytes_per_step": 0,
+        "metric": W.metric, "value": round(v, 4), "unit": W.unit,
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": W.scaling,
+        "vs_baseline": None, "dtype": W.dtype, "data": "synthetic (seeded)",
+        "config": {"workload": W.name, "size": args.size, "elements": args.elements},
+        "impl": "reference", "cpu_baseline": cb,
+        "e2e": {"value": round(v, 4), "unit": W.unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
 
@@ -420,22 +535,28 @@ def main():
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="fp8_quant")
     ap.add_argument("--impl", choices=["amp_b200", "reference"], default="amp_b200")
     ap.add_argument("--elements", type=int, default=1 << 26)
+    ap.add_argument("--size", type=int, default=8192)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-e2e", action="store_true")
     args = ap.parse_args()
+    if args.impl == "reference":
+        args.steps = args.steps or 5
+        args.warmup = args.warmup if args.warmup is not None else 3
+    else:
+        heavy = args.workload.startswith("gemm")
+        args.steps = args.steps or (200 if heavy else 2000)
+        args.warmup = args.warmup if args.warmup is not None else (10 if heavy else 20)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
-        # Only rank 0 works; the other ranks exit without touching a GPU.
-        rank = int(os.environ.get("RANK", "0"))
-        if rank != 0:
-            return
-        out = run_reference(args, _RefDist())
-        print(json.dumps(out), flush=True)
+        if int(os.environ.get("RANK", "0")) != 0:
+            return  # only rank 0 runs the CPU arm; the others exit without work
+        print(json.dumps(run_reference(args)), flush=True)
         return
     dist = Dist(args.gpus)
     try:
@@ -444,13 +565,6 @@ def main():
             print(json.dumps(out), flush=True)
     finally:
         dist.close()
-
-
-class _RefDist:
-    """Rank bookkeeping for the reference arm (no process group, no GPU)."""
-    def __init__(self):
-        self.rank = int(os.environ.get("RANK", "0"))
-        self.world = int(os.environ.get("WORLD_SIZE", "1"))
 
 
 if __name__ == "__main__":

@@ -36,10 +36,19 @@ extern "C" {
 #define AMP_ERR_TIMEOUT (-3)     /* a bounded device-side wait expired                 */
 #define AMP_ERR_NO_DEVICE (-4)   /* no CUDA device visible                             */
 
+/* Element types named in signatures that take a dtype selector. */
+#define AMP_DTYPE_F32 0
+#define AMP_DTYPE_BF16 1
+
 /* Message for the last nonzero status returned on this thread. */
 AMP_API const char* amp_last_error(void);
 /* ABI version: major*10000 + minor*100 + patch. */
 AMP_API int amp_abi_version(void);
+/* Synchronises the current device and reports whether any kernel's bounded
+ * wait expired since the last clear (AMP_ERR_TIMEOUT) -- the device-side
+ * failure path of the pipelined tensor-core kernels, which end instead of
+ * hanging.  clear != 0 resets the flag. */
+AMP_API int amp_device_status(int clear);
 
 /* ------------------------------------------------------------------------
  * FP8 E4M3 per-tensor amax-scaled quantise / dequantise.
@@ -91,6 +100,49 @@ AMP_API int amp_fp8_quant_e4m3_noalloc_dev(const void* x_bf16, int64_t n, uint8_
 AMP_API int amp_user_fp8_quant_e4m3(const uint16_t* x_bf16, int64_t n, uint8_t* q, float* scale_out,
                             uint16_t* y_bf16);
 AMP_API int amp_user_fp8_dequant_e4m3(const uint8_t* q, int64_t n, float scale, uint16_t* y_bf16);
+
+/* ------------------------------------------------------------------------
+ * fp32 GEMM, row-major C[M,N] = A[M,K] * B[K,N].
+ * Replaces AMP::launch_matmul(TileCfg, dA, dB, dC, M, N, K, stream)
+ * (kernels/matmul.cuh:96-98, dispatcher kernels/matmul.cu:24-35).  The host
+ * pointer form is amp_user_gemm_fp32 in amp_plugin.h.
+ * ---------------------------------------------------------------------- */
+AMP_API int amp_gemm_fp32_dev(const float* A, const float* B, float* C, int M, int N, int K,
+                              void* stream);
+/* Same, named by one of AMP's tile configs (bm,bn,bk) in {(16,16,16),
+ * (32,16,16), (32,32,16), (32,32,32)} or (0,0,0); any other config is an
+ * error, as in the reference dispatcher ("unknown FP32 tile cfg").  The tile
+ * names the dump entry; the kernel's own blocking is chosen by size. */
+AMP_API int amp_gemm_fp32_tile_dev(int bm, int bn, int bk, const float* A, const float* B,
+                                   float* C, int M, int N, int K, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Tensor-core GEMM (tcgen05), row-major C[M,N] = A[M,K] * B[K,N].
+ * bf16: replaces AMP::launch_matmul_bf16 (kernels/matmul.cuh:103-105,
+ *       kernels/matmul.cu:47-110), fp32 accumulate, C in fp32 (AMP's choice)
+ *       or bf16 (c_dtype).
+ * FP8:  replaces AMP::launch_matmul_fp8e4m3 (kernels/matmul.cuh:120-123,
+ *       kernels/matmul.cu:235-270 -> cuBLASLt).  scale_mode 1: per-tensor,
+ *       scale_a/scale_b point to one device float each (as cuBLASLt's
+ *       A/B_SCALE_POINTER); scale_mode 2: scale_a[M] per row of A and
+ *       scale_b[N] per column of B.  C = (A8 * B8) * sa * sb.
+ * Requirements: K and N multiples of 8 (bf16) / 16 (FP8), 16-byte aligned
+ * A and B; any M.  Asynchronous on `stream`.
+ * ---------------------------------------------------------------------- */
+AMP_API int amp_gemm_bf16_dev(const void* A, const void* B, void* C, int c_dtype, int M, int N,
+                              int K, void* stream);
+AMP_API int amp_gemm_fp8e4m3_dev(const uint8_t* A, const uint8_t* B, const float* scale_a,
+                                 const float* scale_b, int scale_mode, void* C, int c_dtype,
+                                 int M, int N, int K, void* stream);
+
+/* Host-pointer forms of the two tensor-core GEMMs (plugin convention:
+ * host buffers, all device work finished before returning).  Scales are
+ * host arrays: 1 value each (scale_mode 1) or M and N values (scale_mode 2). */
+AMP_API int amp_user_gemm_bf16(const uint16_t* A, const uint16_t* B, void* C, int c_dtype, int M,
+                               int N, int K);
+AMP_API int amp_user_gemm_fp8e4m3(const uint8_t* A, const uint8_t* B, const float* scale_a,
+                                  const float* scale_b, int scale_mode, void* C, int c_dtype,
+                                  int M, int N, int K);
 
 #ifdef __cplusplus
 }

@@ -85,6 +85,24 @@ def ref_lib() -> C.CDLL | None:
     return _r
 
 
+_rg: C.CDLL | None = None
+REF_GEMM_LIB = HERE / "_ref" / "libampref_gemm.so"
+
+
+def ref_gemm_lib() -> C.CDLL | None:
+    """AMP's cpu_reference_gemm compiled from the reference sources, or None."""
+    global _rg
+    if _rg is None and REF_GEMM_LIB.exists():
+        g = C.CDLL(str(REF_GEMM_LIB))
+        vp, i32 = C.c_void_p, C.c_int
+        g.ref_cpu_reference_gemm.restype = None
+        g.ref_cpu_reference_gemm.argtypes = [vp, vp, vp, i32, i32, i32]
+        g.ref_cpu_reference_gemm_mt.restype = None
+        g.ref_cpu_reference_gemm_mt.argtypes = [vp, vp, vp, i32, i32, i32, i32]
+        _rg = g
+    return _rg
+
+
 # --------------------------------------------------------------------------
 # numpy conveniences (bf16 carried as uint16 bit patterns)
 # --------------------------------------------------------------------------

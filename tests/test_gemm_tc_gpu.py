@@ -1,0 +1,128 @@
+"""bf16 and FP8 E4M3 tensor-core GEMM on the B200 vs the fp64 oracle.
+
+Bars (AMP's metric, max|x-ref|/max(1,|ref|)): bf16 < 2e-2, FP8 < 6e-2 against
+an fp64 GEMM of the exact operand values (the dequantised codes for FP8).
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from amp_b200 import gemm
+from amp_b200._lib import AmpError, lib
+
+pytestmark = pytest.mark.gpu
+TOL_BF16 = 2e-2
+TOL_FP8 = 6e-2
+
+
+def bf16_operands(M, N, K, seed):
+    g = torch.Generator().manual_seed(seed)
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    B = torch.randn(K, N, generator=g).to(torch.bfloat16)
+    return A, B
+
+
+def run_bf16(A, B, out_dtype=torch.float32):
+    M, K = A.shape
+    N = B.shape[1]
+    dA, dB = A.cuda(), B.cuda()
+    dC = torch.full((M, N), float("nan"), dtype=out_dtype, device="cuda")
+    gemm.launch_matmul_bf16(dA, dB, dC, M, N, K)
+    torch.cuda.synchronize()
+    assert lib().amp_device_status(1) == 0
+    return dC.float().cpu().numpy()
+
+
+def ref64(A, B):
+    return A.double().numpy() @ B.double().numpy()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (128, 256, 128), (256, 512, 1024),
+                                   (100, 72, 40), (1, 8, 8), (300, 264, 200), (129, 257 + 7, 72)])
+@pytest.mark.parametrize("out", [torch.float32, torch.bfloat16])
+def test_bf16_small_and_ragged(M, N, K, out, cuda, amp_lib):
+    A, B = bf16_operands(M, N, K, seed=M + N + K)
+    C = run_bf16(A, B, out)
+    err = oracle.max_rel_err(C, ref64(A, B))
+    assert err < TOL_BF16, err
+
+
+def test_bf16_4096_cube_fp32_out(cuda, amp_lib):
+    A, B = bf16_operands(4096, 4096, 4096, seed=1)
+    C = run_bf16(A, B)
+    assert oracle.max_rel_err(C, ref64(A, B)) < TOL_BF16
+
+
+def test_bf16_8192_cube_bf16_out(cuda, amp_lib):
+    A, B = bf16_operands(8192, 8192, 8192, seed=2)
+    C = run_bf16(A, B, torch.bfloat16)
+    assert oracle.max_rel_err(C, ref64(A, B)) < TOL_BF16
+
+
+def test_bf16_rejects_unaligned_k(cuda, amp_lib):
+    A, B = bf16_operands(64, 64, 60, seed=0)
+    with pytest.raises(AmpError, match="multiples"):
+        run_bf16(A, B)
+
+
+def fp8_operands(M, N, K, seed):
+    rng = np.random.default_rng(seed)
+    a = oracle.f32_to_bf16_bits(rng.standard_normal((M, K), dtype=np.float32))
+    b = oracle.f32_to_bf16_bits(rng.standard_normal((K, N), dtype=np.float32))
+    qa, sa = oracle.quant_e4m3_rows(a)
+    qb, sb = oracle.quant_e4m3_cols(b)
+    return qa, sa, qb, sb, a, b
+
+
+def run_fp8(qa, sa, qb, sb, out=torch.bfloat16):
+    M, K = qa.shape
+    N = qb.shape[1]
+    dC = torch.full((M, N), float("nan"), dtype=out, device="cuda")
+    gemm.launch_matmul_fp8e4m3(torch.from_numpy(qa).cuda(), torch.from_numpy(qb).cuda(), dC,
+                               M, N, K, torch.from_numpy(sa).cuda(), torch.from_numpy(sb).cuda())
+    torch.cuda.synchronize()
+    assert lib().amp_device_status(1) == 0
+    return dC.float().cpu().numpy()
+
+
+def fp8_ref(qa, sa, qb, sb):
+    dec = oracle.e4m3_decode_table().astype(np.float64)
+    Af = dec[qa] * sa.astype(np.float64)[:, None]
+    Bf = dec[qb] * sb.astype(np.float64)[None, :]
+    return Af @ Bf
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (256, 512, 512), (100, 80, 48),
+                                   (333, 272, 1024)])
+@pytest.mark.parametrize("out", [torch.float32, torch.bfloat16])
+def test_fp8_rowcol_scales_small(M, N, K, out, cuda, amp_lib):
+    qa, sa, qb, sb, _, _ = fp8_operands(M, N, K, seed=M * 3 + N)
+    C = run_fp8(qa, sa, qb, sb, out)
+    assert oracle.max_rel_err(C, fp8_ref(qa, sa, qb, sb)) < TOL_FP8
+
+
+def test_fp8_per_tensor_scale(cuda, amp_lib):
+    rng = np.random.default_rng(5)
+    M, N, K = 256, 256, 256
+    a = oracle.f32_to_bf16_bits(rng.standard_normal((M, K), dtype=np.float32))
+    b = oracle.f32_to_bf16_bits(rng.standard_normal((K, N), dtype=np.float32))
+    qa, sa, _ = oracle.quant_e4m3(a)
+    qb, sb, _ = oracle.quant_e4m3(b)
+    dC = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    gemm.launch_matmul_fp8e4m3(torch.from_numpy(qa).cuda(), torch.from_numpy(qb).cuda(), dC,
+                               M, N, K, sa, sb)
+    torch.cuda.synchronize()
+    ref = fp8_ref(qa, np.full(M, sa, np.float32), qb, np.full(N, sb, np.float32))
+    assert oracle.max_rel_err(dC.cpu().numpy(), ref) < TOL_FP8
+
+
+def test_fp8_4096_cube_vs_prequant(cuda, amp_lib):
+    qa, sa, qb, sb, a, b = fp8_operands(4096, 4096, 4096, seed=9)
+    C = run_fp8(qa, sa, qb, sb)
+    assert oracle.max_rel_err(C, fp8_ref(qa, sa, qb, sb)) < TOL_FP8
+    # information, not the bar: against the unquantised bf16 operands the error
+    # is E4M3 quantisation noise (3 mantissa bits), a few percent of the range
+    pre = oracle.bf16_bits_to_f32(a).astype(np.float64) @ oracle.bf16_bits_to_f32(b).astype(
+        np.float64)
+    assert np.abs(C - pre).max() / np.abs(pre).max() < 0.1

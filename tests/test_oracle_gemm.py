@@ -1,0 +1,47 @@
+"""Pins the GEMM oracle against AMP's own CPU reference GEMM.
+
+tests/golden/amp_harness_gemm.json records AMP's validator run on the oracle's
+restatement (max_rel_err 0); when the reference tree is present the restated
+loop is also compared bit for bit with AMP's cpu_reference_gemm compiled from
+tests/amp_validate_kernel.cpp.
+"""
+import hashlib
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+GOLD = json.loads((Path(__file__).parent / "golden" / "amp_harness_gemm.json").read_text())
+
+
+@pytest.mark.parametrize("case", GOLD["cases"], ids=lambda c: f"{c['M']}x{c['N']}x{c['K']}")
+def test_harness_inputs_and_loop_match_golden(case, oracle_lib):
+    A, B = oracle_lib.amp_harness_inputs(case["M"], case["N"], case["K"], case["seed"])
+    assert hashlib.sha256(A.tobytes() + B.tobytes()).hexdigest() == case["inputs_sha256"]
+    C = oracle_lib.gemm_fp32_amp(A, B)
+    assert hashlib.sha256(C.tobytes()).hexdigest() == case["oracle_sha256"]
+    # AMP's validator ran the same computation through its own loop: zero error
+    assert case["validator_exit"] == 0 and case["validator_max_rel_err"] == 0
+    # the dump prints 6 significant digits; the sums agree to that precision
+    assert abs(case["output_sum"] - float(C.astype(np.float64).sum())) < 1e-3 * max(
+        1.0, abs(case["output_sum"]))
+
+
+def test_fp64_oracle_is_within_amp_bar_of_amp_loop(oracle_lib):
+    A, B = oracle_lib.amp_harness_inputs(96, 96, 96, 42)
+    assert oracle_lib.max_rel_err(oracle_lib.gemm_fp32_amp(A, B), oracle_lib.gemm_f64(A, B)) < 1e-3
+
+
+def test_restated_loop_is_bit_identical_to_reference_function(oracle_lib):
+    g = oracle_lib.ref_gemm_lib()
+    if g is None:
+        pytest.skip("oracle/_ref/libampref_gemm.so not built (reference tree absent)")
+    for (M, N, K, seed) in [(96, 96, 96, 42), (37, 53, 71, 1), (128, 64, 300, 9)]:
+        A, B = oracle_lib.amp_harness_inputs(M, N, K, seed)
+        want = np.empty((M, N), np.float32)
+        g.ref_cpu_reference_gemm(A.ctypes.data, B.ctypes.data, want.ctypes.data, M, N, K)
+        assert np.array_equal(oracle_lib.gemm_fp32_amp(A, B).view(np.uint32), want.view(np.uint32))
+        mt = np.empty((M, N), np.float32)
+        g.ref_cpu_reference_gemm_mt(A.ctypes.data, B.ctypes.data, mt.ctypes.data, M, N, K, 3)
+        assert np.array_equal(mt.view(np.uint32), want.view(np.uint32))
