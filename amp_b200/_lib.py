@@ -32,6 +32,10 @@ SIGNATURES: dict[str, tuple] = {
     "amp_gemm_fp8e4m3_dev": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _vp]),
     "amp_user_gemm_bf16": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32]),
     "amp_user_gemm_fp8e4m3": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32]),
+    "amp_flash_attn_fwd_bf16_dev": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
+                                           _i32, _i32, _i32, _f32, _vp]),
+    "amp_user_flash_attn_fwd_bf16": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
+                                            _i32, _i32, _i32, _f32]),
     "amp_gemm_fp32_dev": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "amp_gemm_fp32_tile_dev": (_i32, [_i32, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "amp_user_gemm_fp32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32]),

@@ -1,0 +1,450 @@
+// flash_attn.cu -- FlashAttention-2 forward (causal / full, GQA) on tcgen05.
+//
+// Replaces flash_attn_fwd_kernel<Br,Bc,D> and dispatch_flash_attn
+// (kernels/flash_attn.cu:73-283 of the reference: one warp per query row,
+// scalar fp32 dot products repeated by every lane, fp32 shared-memory tiles).
+// Same contract: Q,O [B,Hq,S_q,D] bf16, K,V [B,Hkv,S_kv,D] bf16, lse [B,Hq,S_q]
+// fp32 = ln(sum_j exp(scale * q.k_j)); kv head = hq / (Hq/Hkv)
+// (flash_attn.cu:90); causal masks key j > query i (top-left aligned,
+// flash_attn.cu:134,152) -- generalised here by an offset so that paged
+// prefill can use bottom-right alignment (key j visible iff j <= i + offset).
+//
+// One CTA per (batch*head, 128-row query tile), 192 threads:
+//   warp 0     TMA: Q tile once; K and V tiles (128 rows) into separate
+//              2-stage rings (128-byte swizzle, 3-D maps so each head's tail is
+//              zero-filled).
+//   warp 1     TMEM (512 columns: S0 | S1 | O) and one MMA-issuing lane:
+//              S_j = Q K_j^T into S[j%2] (SS form, K-major x K-major), then
+//              O += P_{j-1} V_{j-1} (TS form: P read from TMEM, V MN-major from
+//              shared memory), so QK^T of tile j overlaps softmax of tile j-1.
+//   warps 2-5  softmax, one query row per thread: tcgen05.ld the S row, mask,
+//              online max in the log2 domain (scale * log2(e) folded into one
+//              FFMA), ex2, row sum in fp32, P packed to bf16 and tcgen05.st back
+//              over S.  O is rescaled (tcgen05.ld/st) only when a row maximum
+//              grows by more than 2^8; otherwise the stale maximum is kept.
+//              Epilogue: O / l to bf16, lse = (m + log2 l) * ln 2.
+#include <cuda.h>
+
+#include <cmath>
+
+#include "common.cuh"
+#include "runtime.h"
+#include "tc_common.cuh"
+
+namespace ampb {
+
+int fa_make_tmap_3d(CUtensorMap* m, const void* base, int64_t d, int64_t s, int64_t bh);
+
+namespace {
+
+constexpr int BQ = 128;            // query rows per CTA
+constexpr int BKV = 128;           // key/value rows per tile
+constexpr int KV_STAGES = 2;
+constexpr int kThreads = 192;
+constexpr int SLAB_BYTES = 128 * 128;  // [128 rows x 128 bytes] swizzled slab
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct FaParams {
+    int B, Hq, Hkv, S_q, S_kv;
+    int causal;
+    int causal_offset;   // key j visible for query i iff j <= i + causal_offset
+    float scale_log2;    // softmax scale * log2(e)
+    void* O;
+    float* lse;
+    int* status;
+};
+
+__device__ __forceinline__ float lg2_approx(float x) {
+    float y;
+    asm("lg2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <int D>
+struct FaCfg {
+    static constexpr int SLABS = D / 64;                 // 64 bf16 = 128 bytes per slab
+    static constexpr int Q_BYTES = SLABS * SLAB_BYTES;
+    static constexpr int K_BYTES = SLABS * SLAB_BYTES;
+    static constexpr int V_BYTES = SLABS * SLAB_BYTES;
+    static constexpr int SMEM = Q_BYTES + KV_STAGES * (K_BYTES + V_BYTES) + 1024 + 256;
+    static constexpr uint32_t IDESC_QK = make_idesc(1, 1, 0, 0, BQ, BKV);
+    static constexpr uint32_t IDESC_PV = make_idesc(1, 1, 0, 1, BQ, D);
+    static constexpr uint32_t O_COL = 2 * BKV;           // S0 | S1 | O
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_flash_fwd(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, const FaParams p) {
+    using CF = FaCfg<D>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint8_t* q_s = smem;
+    uint8_t* k_s = q_s + CF::Q_BYTES;                       // [KV_STAGES][K_BYTES]
+    uint8_t* v_s = k_s + KV_STAGES * CF::K_BYTES;           // [KV_STAGES][V_BYTES]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(v_s + KV_STAGES * CF::V_BYTES);
+    uint64_t* q_full = bars;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = k_full + KV_STAGES;
+    uint64_t* v_full = k_empty + KV_STAGES;
+    uint64_t* v_empty = v_full + KV_STAGES;
+    uint64_t* s_full = v_empty + KV_STAGES;   // [2]
+    uint64_t* p_full = s_full + 2;            // [2]
+    uint64_t* pv_done = p_full + 2;           // [2]
+    uint64_t* drain = pv_done + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_qt = (p.S_q + BQ - 1) / BQ;
+    const int qt = n_qt - 1 - (int)blockIdx.x;   // heaviest causal tiles first
+    const int bh = blockIdx.y;
+    const int b = bh / p.Hq, h = bh % p.Hq;
+    const int bh_kv = b * p.Hkv + h / (p.Hq / p.Hkv);
+    const int q0 = qt * BQ;
+    int n_kv = (p.S_kv + BKV - 1) / BKV;
+    if (p.causal) {
+        const int last = q0 + BQ - 1 + p.causal_offset;   // largest visible key of the tile
+        const int lim = last < 0 ? 0 : last / BKV + 1;
+        n_kv = min(n_kv, lim);
+    }
+    if (n_kv < 1) n_kv = 1;   // fully masked rows still produce O = 0, lse = -inf
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < KV_STAGES; ++s) {
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_full[i], 4);
+            mbar_init(&pv_done[i], 1);
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tmQ);
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+            mbar_arrive_expect_tx(q_full, CF::Q_BYTES);
+#pragma unroll
+            for (int sl = 0; sl < CF::SLABS; ++sl)
+                tma_load_3d(q_s + sl * SLAB_BYTES, &tmQ, q_full, sl * 64, q0, bh);
+            for (int j = 0; j < n_kv; ++j) {
+                const int s = j % KV_STAGES;
+                const uint32_t ph = (j / KV_STAGES) & 1;
+                if (!mbar_wait(&k_empty[s], ph ^ 1, p.status)) break;
+                mbar_arrive_expect_tx(&k_full[s], CF::K_BYTES);
+#pragma unroll
+                for (int sl = 0; sl < CF::SLABS; ++sl)
+                    tma_load_3d(k_s + s * CF::K_BYTES + sl * SLAB_BYTES, &tmK, &k_full[s], sl * 64,
+                                j * BKV, bh_kv);
+                if (!mbar_wait(&v_empty[s], ph ^ 1, p.status)) break;
+                mbar_arrive_expect_tx(&v_full[s], CF::V_BYTES);
+#pragma unroll
+                for (int sl = 0; sl < CF::SLABS; ++sl)
+                    tma_load_3d(v_s + s * CF::V_BYTES + sl * SLAB_BYTES, &tmV, &v_full[s], sl * 64,
+                                j * BKV, bh_kv);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            bool ok = mbar_wait(q_full, 0, p.status);
+            const uint32_t q_addr = smem_u32(q_s);
+            for (int j = 0; ok && j <= n_kv; ++j) {
+                if (j < n_kv) {   // S_j = Q K_j^T
+                    const int sb = j & 1;
+                    if (j >= 2 && !mbar_wait(&pv_done[sb], ((j - 2) >> 1) & 1, p.status)) break;
+                    if (!mbar_wait(&k_full[j % KV_STAGES], (j / KV_STAGES) & 1, p.status)) break;
+                    tc_fence_after();
+                    const uint32_t k_addr = smem_u32(k_s + (j % KV_STAGES) * CF::K_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < D / 16; ++kk) {
+                        const uint32_t off = (kk >> 2) * SLAB_BYTES + (kk & 3) * 32;
+                        tc_mma_f16(tmem + sb * BKV, smem_desc_sw128(q_addr + off, 16, 1024),
+                                   smem_desc_sw128(k_addr + off, 16, 1024), CF::IDESC_QK, kk != 0);
+                    }
+                    tc_commit(&k_empty[j % KV_STAGES]);
+                    tc_commit(&s_full[sb]);
+                }
+                if (j >= 1) {     // O += P_i V_i
+                    const int i = j - 1, pb = i & 1;
+                    if (!mbar_wait(&p_full[pb], (i >> 1) & 1, p.status)) break;
+                    if (!mbar_wait(&v_full[i % KV_STAGES], (i / KV_STAGES) & 1, p.status)) break;
+                    tc_fence_after();
+                    const uint32_t v_addr = smem_u32(v_s + (i % KV_STAGES) * CF::V_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BKV / 16; ++kk)
+                        tc_mma_f16_ts(tmem + CF::O_COL, tmem + pb * BKV + kk * 8,
+                                      smem_desc_sw128(v_addr + kk * 16 * 128, SLAB_BYTES, 1024),
+                                      CF::IDESC_PV, (i | kk) != 0);
+                    tc_commit(&v_empty[i % KV_STAGES]);
+                    tc_commit(&pv_done[pb]);
+                }
+            }
+            tc_commit(drain);
+            mbar_wait(drain, 0, p.status);
+        }
+    } else {
+        // ---------------------------------------------------------- softmax
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;              // row within the tile == TMEM lane
+        const int qi = q0 + r;                       // query index
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+        const float c = p.scale_log2;
+        float m_run = -INFINITY, l_run = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < n_kv; ++j) {
+            const int sb = j & 1;
+            if (!mbar_wait_warp(&s_full[sb], (j >> 1) & 1, p.status)) { ok = false; break; }
+            tc_fence_after();
+            uint32_t sr[BKV / 32][32];
+            __syncwarp();
+#pragma unroll
+            for (int cch = 0; cch < BKV / 32; ++cch)
+                tmem_ld_32x32b_x32(lane_base + sb * BKV + cch * 32, sr[cch]);
+            tmem_ld_wait();
+            // mask: keys past the end, and (causal) keys after the query
+            const int k0 = j * BKV;
+            const int vis_hi = p.causal ? min(p.S_kv - 1, qi + p.causal_offset) : p.S_kv - 1;
+            if (k0 + BKV - 1 > vis_hi) {
+#pragma unroll
+                for (int cch = 0; cch < BKV / 32; ++cch)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (k0 + cch * 32 + e > vis_hi) sr[cch][e] = __float_as_uint(-INFINITY);
+            }
+            float mt = -INFINITY;
+#pragma unroll
+            for (int cch = 0; cch < BKV / 32; ++cch)
+#pragma unroll
+                for (int e = 0; e < 32; ++e) mt = fmaxf(mt, __uint_as_float(sr[cch][e]));
+            const float m_new = fmaxf(m_run, mt * c);
+            const bool need = (j == 0) || (m_new > m_run + kRescaleThreshold);
+            if (__any_sync(0xffffffffu, need)) {
+                const float alpha = (m_run == -INFINITY) ? 0.0f : ex2_approx(m_run - m_new);
+                if (j > 0) {
+                    // PV_{j-1} must have landed in O before O is rescaled
+                    if (!mbar_wait_warp(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    __syncwarp();
+#pragma unroll
+                    for (int oc = 0; oc < D / 32; ++oc) {
+                        uint32_t o[32];
+                        tmem_ld_32x32b_x32(lane_base + CF::O_COL + oc * 32, o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        tmem_st_32x32b_x32(lane_base + CF::O_COL + oc * 32, o);
+                    }
+                }
+                l_run *= alpha;
+                m_run = m_new;
+            }
+            const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+            float rs = 0.0f;
+#pragma unroll
+            for (int cch = 0; cch < BKV / 32; ++cch) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    const float p0 = ex2_approx(fmaf(__uint_as_float(sr[cch][e]), c, -m_use));
+                    const float p1 = ex2_approx(fmaf(__uint_as_float(sr[cch][e + 1]), c, -m_use));
+                    rs += p0 + p1;
+                    pk[e >> 1] = f32x2_to_bf16x2(p0, p1);
+                }
+                // P (bf16 pairs) overwrites the first 64 columns of this S buffer
+#pragma unroll
+                for (int e = 0; e < 16; ++e) sr[cch >> 1][(cch & 1) * 16 + e] = pk[e];
+                if (cch & 1) tmem_st_32x32b_x32(lane_base + sb * BKV + (cch >> 1) * 32, sr[cch >> 1]);
+            }
+            l_run += rs;
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[sb]);
+        }
+        // ---------------------------------------------------------- epilogue
+        if (ok && mbar_wait_warp(&pv_done[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, p.status)) {
+            tc_fence_after();
+            const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+            const bool row_ok = qi < p.S_q;
+            __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.O) +
+                                  ((int64_t)bh * p.S_q + (row_ok ? qi : 0)) * D;
+            __syncwarp();
+#pragma unroll
+            for (int oc = 0; oc < D / 32; ++oc) {
+                uint32_t o[32];
+                tmem_ld_32x32b_x32(lane_base + CF::O_COL + oc * 32, o);
+                tmem_ld_wait();
+                if (row_ok) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 8) {
+                        uint4 w;
+                        w.x = f32x2_to_bf16x2(__uint_as_float(o[e]) * inv_l, __uint_as_float(o[e + 1]) * inv_l);
+                        w.y = f32x2_to_bf16x2(__uint_as_float(o[e + 2]) * inv_l, __uint_as_float(o[e + 3]) * inv_l);
+                        w.z = f32x2_to_bf16x2(__uint_as_float(o[e + 4]) * inv_l, __uint_as_float(o[e + 5]) * inv_l);
+                        w.w = f32x2_to_bf16x2(__uint_as_float(o[e + 6]) * inv_l, __uint_as_float(o[e + 7]) * inv_l);
+                        *reinterpret_cast<uint4*>(orow + oc * 32 + e) = w;
+                    }
+                }
+            }
+            if (row_ok && p.lse)
+                p.lse[(int64_t)bh * p.S_q + qi] =
+                    l_run > 0.0f ? (m_run + lg2_approx(l_run)) * 0.69314718055994531f : -INFINITY;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+template <int D>
+int launch_fa(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq,
+              int Hkv, int S_q, int S_kv, int causal, int causal_offset, float scale,
+              cudaStream_t st) {
+    CUtensorMap tq, tk, tv;
+    int rc;
+    if ((rc = fa_make_tmap_3d(&tq, Q, D, S_q, (int64_t)B * Hq))) return rc;
+    if ((rc = fa_make_tmap_3d(&tk, K, D, S_kv, (int64_t)B * Hkv))) return rc;
+    if ((rc = fa_make_tmap_3d(&tv, V, D, S_kv, (int64_t)B * Hkv))) return rc;
+    int* status = nullptr;
+    if ((rc = device_status(&status))) return rc;
+    FaParams p;
+    p.B = B;
+    p.Hq = Hq;
+    p.Hkv = Hkv;
+    p.S_q = S_q;
+    p.S_kv = S_kv;
+    p.causal = causal;
+    p.causal_offset = causal_offset;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.O = O;
+    p.lse = lse;
+    p.status = status;
+    auto kern = k_flash_fwd<D>;
+    AMPB_CHECK_CUDA(
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FaCfg<D>::SMEM));
+    dim3 grid((S_q + BQ - 1) / BQ, B * Hq);
+    kern<<<grid, kThreads, FaCfg<D>::SMEM, st>>>(tq, tk, tv, p);
+    AMPB_CHECK_LAUNCH("k_flash_fwd");
+    return AMP_OK;
+}
+
+}  // namespace
+
+// [bh][s][d] bf16 tensor as a 3-D TMA map, box [1][128][64], 128-byte swizzle.
+int fa_make_tmap_3d(CUtensorMap* m, const void* base, int64_t d, int64_t s, int64_t bh) {
+    using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                       const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                       const cuuint32_t*, CUtensorMapInterleave,
+                                       CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                       CUtensorMapFloatOOBfill);
+    static EncodeTiledFn enc = nullptr;
+    if (!enc) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        AMPB_CHECK_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        AMPB_REQUIRE(q == cudaDriverEntryPointSuccess && fn, AMP_ERR_UNSUPPORTED,
+                     "cuTensorMapEncodeTiled not available");
+        enc = (EncodeTiledFn)fn;
+    }
+    cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)s, (cuuint64_t)bh};
+    cuuint64_t strides[2] = {(cuuint64_t)(d * 2), (cuuint64_t)(s * d * 2)};
+    cuuint32_t box[3] = {64, 128, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    AMPB_REQUIRE(r == CUDA_SUCCESS, AMP_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return AMP_OK;
+}
+
+int flash_attn_fwd_dev(const void* Q, const void* K, const void* V, void* O, float* lse, int B,
+                       int Hq, int Hkv, int S_q, int S_kv, int D, int causal, int causal_offset,
+                       float scale, cudaStream_t st) {
+    AMPB_REQUIRE(B > 0 && Hq > 0 && Hkv > 0 && S_q > 0 && S_kv > 0, AMP_ERR_INVALID,
+                 "attention sizes must be positive");
+    AMPB_REQUIRE(Hq % Hkv == 0, AMP_ERR_INVALID, "num_q_heads (%d) must be a multiple of "
+                 "num_kv_heads (%d)", Hq, Hkv);
+    AMPB_REQUIRE(Q && K && V && O, AMP_ERR_INVALID, "NULL tensor");
+    AMPB_REQUIRE(aligned16(Q) && aligned16(K) && aligned16(V) && aligned16(O), AMP_ERR_INVALID,
+                 "Q, K, V, O must be 16-byte aligned");
+    AMPB_REQUIRE((int64_t)B * Hq <= 65535, AMP_ERR_UNSUPPORTED, "B*Hq must be <= 65535");
+    if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)D);
+    switch (D) {
+        case 128:
+            return launch_fa<128>(Q, K, V, O, lse, B, Hq, Hkv, S_q, S_kv, causal, causal_offset,
+                                  scale, st);
+        case 64:
+            return launch_fa<64>(Q, K, V, O, lse, B, Hq, Hkv, S_q, S_kv, causal, causal_offset,
+                                 scale, st);
+        default:
+            set_error(AMP_ERR_UNSUPPORTED, "flash_attn: head_dim %d not supported (64, 128)", D);
+            return AMP_ERR_UNSUPPORTED;
+    }
+}
+
+}  // namespace ampb
+
+using namespace ampb;
+
+extern "C" int amp_flash_attn_fwd_bf16_dev(const void* Q, const void* K, const void* V, void* O,
+                                           float* lse, int B, int Hq, int Hkv, int S_q, int S_kv,
+                                           int head_dim, int causal, float scale, void* stream) {
+    return flash_attn_fwd_dev(Q, K, V, O, lse, B, Hq, Hkv, S_q, S_kv, head_dim, causal, 0, scale,
+                              as_stream(stream));
+}
+
+// Host-pointer form (plugin convention): all tensors in host memory; device
+// staging, launch and copy-back are done before returning.
+extern "C" int amp_user_flash_attn_fwd_bf16(const uint16_t* Q, const uint16_t* K,
+                                            const uint16_t* V, uint16_t* O, float* lse, int B,
+                                            int Hq, int Hkv, int S_q, int S_kv, int head_dim,
+                                            int causal, float scale) {
+    AMPB_REQUIRE(B > 0 && Hq > 0 && Hkv > 0 && S_q > 0 && S_kv > 0 && head_dim > 0,
+                 AMP_ERR_INVALID, "attention sizes must be positive");
+    AMPB_REQUIRE(Q && K && V && O, AMP_ERR_INVALID, "NULL tensor");
+    const size_t q = (size_t)B * Hq * S_q * head_dim * 2, kv = (size_t)B * Hkv * S_kv * head_dim * 2;
+    const size_t l = (size_t)B * Hq * S_q * 4;
+    void *dq, *dk, *dv, *dout, *dl;
+    int rc;
+    if ((rc = staging_get(0, q, &dq)) || (rc = staging_get(1, kv, &dk)) ||
+        (rc = staging_get(2, kv, &dv)) || (rc = staging_get(3, q, &dout)) ||
+        (rc = staging_get(4, l, &dl)))
+        return rc;
+    cudaStream_t st = 0;
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(dq, Q, q, cudaMemcpyHostToDevice, st));
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(dk, K, kv, cudaMemcpyHostToDevice, st));
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(dv, V, kv, cudaMemcpyHostToDevice, st));
+    if ((rc = flash_attn_fwd_dev(dq, dk, dv, dout, static_cast<float*>(dl), B, Hq, Hkv, S_q, S_kv,
+                                 head_dim, causal, 0, scale, st)))
+        return rc;
+    AMPB_CHECK_CUDA(cudaMemcpyAsync(O, dout, q, cudaMemcpyDeviceToHost, st));
+    if (lse) AMPB_CHECK_CUDA(cudaMemcpyAsync(lse, dl, l, cudaMemcpyDeviceToHost, st));
+    AMPB_CHECK_CUDA(cudaStreamSynchronize(st));
+    return amp_device_status(1);
+}

@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t acc_ph = (i >> 1) & 1;
             int tm, tn;
             tile_coords(t, p.num_m, p.num_n, tm, tn);
-            if (!mbar_wait(&tfull[acc], acc_ph, p.status)) break;
+            if (!mbar_wait_warp(&tfull[acc], acc_ph, p.status)) break;
             tc_fence_after();
             const int row = tm * BM + row_in_tile;
             const bool row_ok = row < p.M;

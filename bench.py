@@ -404,7 +404,99 @@ class GemmFp8Workload(GemmWorkload):
     fp8 = True
 
 
-WORKLOADS = {w.name: w for w in (QuantWorkload, GemmWorkload, GemmFp8Workload)}
+class AttentionWorkload:
+    name = "fa2_fwd"
+    metric = "fa2_fwd_causal_TFLOPS"
+    unit = "TFLOP/s"
+    scale = 1e12
+    dtype = "bf16"
+    bound = "tensor"
+    scaling = "strong"
+
+    def __init__(self, dist: Dist, args):
+        import torch
+        from amp_b200 import attention
+        self.torch, self.att, self.dist = torch, attention, dist
+        self.B, self.H, self.S, self.D = args.batch, args.heads, args.seq, 128
+        p = dist.world
+        if (self.B * self.H) % p:
+            raise SystemExit("batch*heads must divide over the GPUs")
+        self.bh = self.B * self.H // p      # (batch*head) shard of this rank
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev)
+        g.manual_seed(99 + dist.rank)
+        shape = (1, self.bh, self.S, self.D)
+        self.q = torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+        self.k = torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+        self.v = torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+        self.o = torch.empty_like(self.q)
+        self.lse = torch.empty(1, self.bh, self.S, dtype=torch.float32, device=dev)
+        self.cfg = attention.AttnCfg(self.bh, self.bh, self.D, True, 0.0)
+        self.o_all = (torch.empty(p, self.bh, self.S, self.D, dtype=torch.bfloat16, device=dev)
+                      if p > 1 else None)
+
+    def units_per_step(self) -> float:
+        # causal: 2 matmuls x 2 flop x D per (query, visible key) pair
+        return 4.0 * self.bh * self.D * self.S * (self.S + 1) / 2
+
+    def launches_per_step(self) -> int:
+        return 1
+
+    def config(self):
+        p = self.dist.world
+        return {"workload": "flash_attn2_fwd_causal", "batch": self.B, "heads": self.H,
+                "seq_len": self.S, "head_dim": self.D, "dtype": "bf16, fp32 softmax/accumulate",
+                "flop_convention": "4*B*H*D*S*(S+1)/2 (visible pairs)",
+                "l2": "Q/K/V %d MiB each exceed L2; 256 MiB flush before every step"
+                      % (self.B * self.H * self.S * self.D * 2 >> 20),
+                "parallelism": f"(batch*head) split over {p} GPUs + NCCL all-gather of O"
+                if p > 1 else "single"}
+
+    def kernel_table(self):
+        return [("k_flash_fwd<128>", self.units_per_step())]
+
+    def step(self, ev=None):
+        if ev: ev[0].record()
+        self.att.launch_flash_attn_bf16(self.q, self.k, self.v, self.o, self.lse, 1, self.S,
+                                        self.S, self.cfg)
+        if ev: ev[1].record()
+        if self.dist.world > 1:
+            self.dist.pg.all_gather_into_tensor(self.o_all, self.o[0])
+
+    def e2e(self, steps: int, warmup: int):
+        torch = self.torch
+        from amp_b200._lib import call
+        qh, kh, vh = (t.cpu().pin_memory() for t in (self.q, self.k, self.v))
+        oh = torch.empty_like(qh).pin_memory()
+        lh = torch.empty(1, self.bh, self.S, dtype=torch.float32).pin_memory()
+        fn = lambda: call("amp_user_flash_attn_fwd_bf16", qh.data_ptr(), kh.data_ptr(),
+                          vh.data_ptr(), oh.data_ptr(), lh.data_ptr(), 1, self.bh, self.bh,
+                          self.S, self.S, self.D, 1, 0.0)
+        ms = _e2e_time(torch, fn, steps, warmup)
+        n = qh.numel() * 2
+        return {"value": self.units_per_step() / (ms * 1e-3) / self.scale, "unit": self.unit,
+                "ms_per_step": ms, "h2d_bytes_per_step": 3 * n,
+                "d2h_bytes_per_step": n + lh.numel() * 4, "api": "amp_user_flash_attn_fwd_bf16"}
+
+    @classmethod
+    def cpu_reference(cls, args, budget_s: float, threads: int):
+        """AMP has no CPU attention path: the fp64 oracle (oracle/attention.py) on
+        whole heads of the same configuration, labelled as a port."""
+        from oracle import attention as ref
+        S, D = args.seq, 128
+        rng = np.random.default_rng(0)
+        q, k, v = (rng.standard_normal((1, 1, S, D)).astype(np.float32) for _ in range(3))
+        run = lambda: ref.flash_attn_fwd(q, k, v, True)
+        reps, dt = timed_reps(run, budget_s)
+        flops = 4.0 * D * S * (S + 1) / 2 * reps
+        return {"value": flops / dt / cls.scale, "unit": cls.unit, "cores": threads,
+                "kind": "port",
+                "sample": f"{reps} head(s) of S={S}, D={D} in {dt:.1f} s; fp64 numpy oracle "
+                          "(the reference has no CPU attention path)"}
+
+
+WORKLOADS = {w.name: w for w in (QuantWorkload, GemmWorkload, GemmFp8Workload,
+                                 AttentionWorkload)}
 
 
 def _e2e_time(torch, fn, steps, warmup):
@@ -541,6 +633,9 @@ def main():
     ap.add_argument("--impl", choices=["amp_b200", "reference"], default="amp_b200")
     ap.add_argument("--elements", type=int, default=1 << 26)
     ap.add_argument("--size", type=int, default=8192)
+    ap.add_argument("--batch", type=int, default=4)
+    ap.add_argument("--heads", type=int, default=32)
+    ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-e2e", action="store_true")
     args = ap.parse_args()
@@ -548,7 +643,7 @@ def main():
         args.steps = args.steps or 5
         args.warmup = args.warmup if args.warmup is not None else 3
     else:
-        heavy = args.workload.startswith("gemm")
+        heavy = args.workload != "fp8_quant"
         args.steps = args.steps or (200 if heavy else 2000)
         args.warmup = args.warmup if args.warmup is not None else (10 if heavy else 20)
     if args.warmup < 3:

@@ -135,6 +135,24 @@ AMP_API int amp_gemm_fp8e4m3_dev(const uint8_t* A, const uint8_t* B, const float
                                  const float* scale_b, int scale_mode, void* C, int c_dtype,
                                  int M, int N, int K, void* stream);
 
+/* ------------------------------------------------------------------------
+ * FlashAttention-2 forward, bf16 in/out, fp32 softmax and accumulation.
+ * Replaces AMP::launch_flash_attn_bf16 (kernels/flash_attn.cuh:50-58,
+ * kernels/flash_attn.cu:202-283): Q, O [B, Hq, S_q, head_dim]; K, V
+ * [B, Hkv, S_kv, head_dim]; lse [B, Hq, S_q] = ln sum exp(scale * q.k) (may
+ * be NULL).  GQA: kv head = q head / (Hq / Hkv).  causal != 0 masks key j >
+ * query i (top-left aligned, as the reference).  scale <= 0 selects
+ * 1/sqrt(head_dim) (AttnCfg::scale semantics).  head_dim 64 or 128.
+ * ---------------------------------------------------------------------- */
+AMP_API int amp_flash_attn_fwd_bf16_dev(const void* Q, const void* K, const void* V, void* O,
+                                        float* lse, int B, int Hq, int Hkv, int S_q, int S_kv,
+                                        int head_dim, int causal, float scale, void* stream);
+
+/* Host-pointer form of the attention forward (plugin convention). */
+AMP_API int amp_user_flash_attn_fwd_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V,
+                                         uint16_t* O, float* lse, int B, int Hq, int Hkv, int S_q,
+                                         int S_kv, int head_dim, int causal, float scale);
+
 /* Host-pointer forms of the two tensor-core GEMMs (plugin convention:
  * host buffers, all device work finished before returning).  Scales are
  * host arrays: 1 value each (scale_mode 1) or M and N values (scale_mode 2). */
