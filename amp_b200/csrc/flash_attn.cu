@@ -34,6 +34,7 @@
 namespace ampb {
 
 int fa_make_tmap_3d(CUtensorMap* m, const void* base, int64_t d, int64_t s, int64_t bh);
+int fa_make_tmap_pool(CUtensorMap* m, const void* base, int64_t d, int64_t hkv, int64_t pages);
 
 namespace {
 
@@ -52,7 +53,13 @@ struct FaParams {
     void* O;
     float* lse;
     int* status;
+    // paged K/V (prefill): pools [num_pages][Hkv][16][D], table [B][max_pages]
+    const int* block_table;
+    const int* ctx_lens;
+    int max_pages, num_pages;
 };
+
+constexpr int kPageTokens = 16;
 
 __device__ __forceinline__ float lg2_approx(float x) {
     float y;
@@ -72,7 +79,7 @@ struct FaCfg {
     static constexpr uint32_t O_COL = 2 * BKV;           // S0 | S1 | O
 };
 
-template <int D>
+template <int D, bool kPaged>
 __global__ void __launch_bounds__(kThreads, 1)
     k_flash_fwd(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const FaParams p) {
@@ -102,9 +109,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int b = bh / p.Hq, h = bh % p.Hq;
     const int bh_kv = b * p.Hkv + h / (p.Hq / p.Hkv);
     const int q0 = qt * BQ;
-    int n_kv = (p.S_kv + BKV - 1) / BKV;
+    // Paged prefill: the queries are the last S_q tokens of each sequence's
+    // context, causal with bottom-right alignment.
+    int S_kv = p.S_kv, coff = p.causal_offset;
+    if constexpr (kPaged) {
+        S_kv = max(0, p.ctx_lens[b]);
+        coff = S_kv - p.S_q;
+    }
+    int n_kv = (S_kv + BKV - 1) / BKV;
     if (p.causal) {
-        const int last = q0 + BQ - 1 + p.causal_offset;   // largest visible key of the tile
+        const int last = q0 + BQ - 1 + coff;   // largest visible key of the tile
         const int lim = last < 0 ? 0 : last / BKV + 1;
         n_kv = min(n_kv, lim);
     }
@@ -145,21 +159,53 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int sl = 0; sl < CF::SLABS; ++sl)
                 tma_load_3d(q_s + sl * SLAB_BYTES, &tmQ, q_full, sl * 64, q0, bh);
+            const int last_page = max(0, (S_kv + kPageTokens - 1) / kPageTokens - 1);
+            const int hk = h / (p.Hq / p.Hkv);
             for (int j = 0; j < n_kv; ++j) {
                 const int s = j % KV_STAGES;
                 const uint32_t ph = (j / KV_STAGES) & 1;
+                int pages[BKV / kPageTokens];
+                if constexpr (kPaged) {
+                    // 8 pages per tile; slots past the context repeat the last page
+                    // (masked in the softmax), ids outside the pool read page 0 and
+                    // raise the bad-page flag.
+                    const int* bt = p.block_table + (int64_t)b * p.max_pages;
+#pragma unroll
+                    for (int i = 0; i < BKV / kPageTokens; ++i) {
+                        const int pg = bt[min(j * (BKV / kPageTokens) + i, last_page)];
+                        const bool bad = pg < 0 || pg >= p.num_pages;
+                        if (bad && S_kv > 0) atomicExch(p.status, AMP_DEV_ERR_BAD_PAGE);
+                        pages[i] = bad ? 0 : pg;
+                    }
+                }
                 if (!mbar_wait(&k_empty[s], ph ^ 1, p.status)) break;
                 mbar_arrive_expect_tx(&k_full[s], CF::K_BYTES);
 #pragma unroll
-                for (int sl = 0; sl < CF::SLABS; ++sl)
-                    tma_load_3d(k_s + s * CF::K_BYTES + sl * SLAB_BYTES, &tmK, &k_full[s], sl * 64,
-                                j * BKV, bh_kv);
+                for (int sl = 0; sl < CF::SLABS; ++sl) {
+                    uint8_t* dst = k_s + s * CF::K_BYTES + sl * SLAB_BYTES;
+                    if constexpr (kPaged) {
+#pragma unroll
+                        for (int i = 0; i < BKV / kPageTokens; ++i)
+                            tma_load_4d(dst + i * kPageTokens * 128, &tmK, &k_full[s], sl * 64, 0,
+                                        hk, pages[i]);
+                    } else {
+                        tma_load_3d(dst, &tmK, &k_full[s], sl * 64, j * BKV, bh_kv);
+                    }
+                }
                 if (!mbar_wait(&v_empty[s], ph ^ 1, p.status)) break;
                 mbar_arrive_expect_tx(&v_full[s], CF::V_BYTES);
 #pragma unroll
-                for (int sl = 0; sl < CF::SLABS; ++sl)
-                    tma_load_3d(v_s + s * CF::V_BYTES + sl * SLAB_BYTES, &tmV, &v_full[s], sl * 64,
-                                j * BKV, bh_kv);
+                for (int sl = 0; sl < CF::SLABS; ++sl) {
+                    uint8_t* dst = v_s + s * CF::V_BYTES + sl * SLAB_BYTES;
+                    if constexpr (kPaged) {
+#pragma unroll
+                        for (int i = 0; i < BKV / kPageTokens; ++i)
+                            tma_load_4d(dst + i * kPageTokens * 128, &tmV, &v_full[s], sl * 64, 0,
+                                        hk, pages[i]);
+                    } else {
+                        tma_load_3d(dst, &tmV, &v_full[s], sl * 64, j * BKV, bh_kv);
+                    }
+                }
             }
         }
     } else if (warp == 1) {
@@ -221,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld_wait();
             // mask: keys past the end, and (causal) keys after the query
             const int k0 = j * BKV;
-            const int vis_hi = p.causal ? min(p.S_kv - 1, qi + p.causal_offset) : p.S_kv - 1;
+            const int vis_hi = p.causal ? min(S_kv - 1, qi + coff) : S_kv - 1;
             if (k0 + BKV - 1 > vis_hi) {
 #pragma unroll
                 for (int cch = 0; cch < BKV / 32; ++cch)
@@ -322,15 +368,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <int D>
+struct PagedKV {
+    const int* block_table = nullptr;
+    const int* ctx_lens = nullptr;
+    int max_pages = 0, num_pages = 0;
+};
+
+template <int D, bool kPaged>
 int launch_fa(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq,
               int Hkv, int S_q, int S_kv, int causal, int causal_offset, float scale,
-              cudaStream_t st) {
+              const PagedKV& pkv, cudaStream_t st) {
     CUtensorMap tq, tk, tv;
     int rc;
     if ((rc = fa_make_tmap_3d(&tq, Q, D, S_q, (int64_t)B * Hq))) return rc;
-    if ((rc = fa_make_tmap_3d(&tk, K, D, S_kv, (int64_t)B * Hkv))) return rc;
-    if ((rc = fa_make_tmap_3d(&tv, V, D, S_kv, (int64_t)B * Hkv))) return rc;
+    if constexpr (kPaged) {
+        if ((rc = fa_make_tmap_pool(&tk, K, D, Hkv, pkv.num_pages))) return rc;
+        if ((rc = fa_make_tmap_pool(&tv, V, D, Hkv, pkv.num_pages))) return rc;
+    } else {
+        if ((rc = fa_make_tmap_3d(&tk, K, D, S_kv, (int64_t)B * Hkv))) return rc;
+        if ((rc = fa_make_tmap_3d(&tv, V, D, S_kv, (int64_t)B * Hkv))) return rc;
+    }
     int* status = nullptr;
     if ((rc = device_status(&status))) return rc;
     FaParams p;
@@ -345,7 +402,11 @@ int launch_fa(const void* Q, const void* K, const void* V, void* O, float* lse, 
     p.O = O;
     p.lse = lse;
     p.status = status;
-    auto kern = k_flash_fwd<D>;
+    p.block_table = pkv.block_table;
+    p.ctx_lens = pkv.ctx_lens;
+    p.max_pages = pkv.max_pages;
+    p.num_pages = pkv.num_pages;
+    auto kern = k_flash_fwd<D, kPaged>;
     AMPB_CHECK_CUDA(
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FaCfg<D>::SMEM));
     dim3 grid((S_q + BQ - 1) / BQ, B * Hq);
@@ -356,8 +417,33 @@ int launch_fa(const void* Q, const void* K, const void* V, void* O, float* lse, 
 
 }  // namespace
 
+namespace {
+int fa_encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
+              const cuuint64_t* strides, const cuuint32_t* box);
+}  // namespace
+
 // [bh][s][d] bf16 tensor as a 3-D TMA map, box [1][128][64], 128-byte swizzle.
 int fa_make_tmap_3d(CUtensorMap* m, const void* base, int64_t d, int64_t s, int64_t bh) {
+    cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)s, (cuuint64_t)bh};
+    cuuint64_t strides[2] = {(cuuint64_t)(d * 2), (cuuint64_t)(s * d * 2)};
+    cuuint32_t box[3] = {64, 128, 1};
+    return fa_encode(m, base, 3, dims, strides, box);
+}
+
+// Paged pool [pages][hkv][16][d] bf16 as a 4-D TMA map, box = one page of one
+// head (16 rows x 64 columns), 128-byte swizzle.
+int fa_make_tmap_pool(CUtensorMap* m, const void* base, int64_t d, int64_t hkv, int64_t pages) {
+    cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)kPageTokens, (cuuint64_t)hkv,
+                          (cuuint64_t)pages};
+    cuuint64_t strides[3] = {(cuuint64_t)(d * 2), (cuuint64_t)(kPageTokens * d * 2),
+                             (cuuint64_t)(hkv * kPageTokens * d * 2)};
+    cuuint32_t box[4] = {64, (cuuint32_t)kPageTokens, 1, 1};
+    return fa_encode(m, base, 4, dims, strides, box);
+}
+
+namespace {
+int fa_encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
+              const cuuint64_t* strides, const cuuint32_t* box) {
     using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                        const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                        const cuuint32_t*, CUtensorMapInterleave,
@@ -372,16 +458,14 @@ int fa_make_tmap_3d(CUtensorMap* m, const void* base, int64_t d, int64_t s, int6
                      "cuTensorMapEncodeTiled not available");
         enc = (EncodeTiledFn)fn;
     }
-    cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)s, (cuuint64_t)bh};
-    cuuint64_t strides[2] = {(cuuint64_t)(d * 2), (cuuint64_t)(s * d * 2)};
-    cuuint32_t box[3] = {64, 128, 1};
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims,
                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     AMPB_REQUIRE(r == CUDA_SUCCESS, AMP_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return AMP_OK;
 }
+}  // namespace
 
 int flash_attn_fwd_dev(const void* Q, const void* K, const void* V, void* O, float* lse, int B,
                        int Hq, int Hkv, int S_q, int S_kv, int D, int causal, int causal_offset,
@@ -395,15 +479,47 @@ int flash_attn_fwd_dev(const void* Q, const void* K, const void* V, void* O, flo
                  "Q, K, V, O must be 16-byte aligned");
     AMPB_REQUIRE((int64_t)B * Hq <= 65535, AMP_ERR_UNSUPPORTED, "B*Hq must be <= 65535");
     if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)D);
+    const PagedKV none;
     switch (D) {
         case 128:
-            return launch_fa<128>(Q, K, V, O, lse, B, Hq, Hkv, S_q, S_kv, causal, causal_offset,
-                                  scale, st);
+            return launch_fa<128, false>(Q, K, V, O, lse, B, Hq, Hkv, S_q, S_kv, causal,
+                                         causal_offset, scale, none, st);
         case 64:
-            return launch_fa<64>(Q, K, V, O, lse, B, Hq, Hkv, S_q, S_kv, causal, causal_offset,
-                                 scale, st);
+            return launch_fa<64, false>(Q, K, V, O, lse, B, Hq, Hkv, S_q, S_kv, causal,
+                                        causal_offset, scale, none, st);
         default:
             set_error(AMP_ERR_UNSUPPORTED, "flash_attn: head_dim %d not supported (64, 128)", D);
+            return AMP_ERR_UNSUPPORTED;
+    }
+}
+
+int paged_prefill_dev(const void* q, const void* k_pool, const void* v_pool,
+                      const int* block_table, const int* ctx_lens, void* out, float* lse, int B,
+                      int Hq, int Hkv, int Lq, int D, int num_pages, int max_pages, float scale,
+                      cudaStream_t st) {
+    AMPB_REQUIRE(B > 0 && Hq > 0 && Hkv > 0 && Lq > 0 && num_pages > 0 && max_pages > 0,
+                 AMP_ERR_INVALID, "paged prefill sizes must be positive");
+    AMPB_REQUIRE(Hq % Hkv == 0, AMP_ERR_INVALID, "Hq (%d) must be a multiple of Hkv (%d)", Hq, Hkv);
+    AMPB_REQUIRE(q && k_pool && v_pool && block_table && ctx_lens && out, AMP_ERR_INVALID,
+                 "NULL argument");
+    AMPB_REQUIRE(aligned16(q) && aligned16(k_pool) && aligned16(v_pool) && aligned16(out),
+                 AMP_ERR_INVALID, "q, out and the pools must be 16-byte aligned");
+    AMPB_REQUIRE((int64_t)B * Hq <= 65535, AMP_ERR_UNSUPPORTED, "B*Hq must be <= 65535");
+    if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)D);
+    PagedKV pkv;
+    pkv.block_table = block_table;
+    pkv.ctx_lens = ctx_lens;
+    pkv.max_pages = max_pages;
+    pkv.num_pages = num_pages;
+    switch (D) {
+        case 128:
+            return launch_fa<128, true>(q, k_pool, v_pool, out, lse, B, Hq, Hkv, Lq, 0, 1, 0, scale,
+                                        pkv, st);
+        case 64:
+            return launch_fa<64, true>(q, k_pool, v_pool, out, lse, B, Hq, Hkv, Lq, 0, 1, 0, scale,
+                                       pkv, st);
+        default:
+            set_error(AMP_ERR_UNSUPPORTED, "paged prefill: head_dim %d not supported (64, 128)", D);
             return AMP_ERR_UNSUPPORTED;
     }
 }
@@ -411,6 +527,16 @@ int flash_attn_fwd_dev(const void* Q, const void* K, const void* V, void* O, flo
 }  // namespace ampb
 
 using namespace ampb;
+
+extern "C" int amp_paged_attn_prefill_bf16_dev(const void* q, const void* k_pool,
+                                               const void* v_pool, const int32_t* block_table,
+                                               const int32_t* ctx_lens, void* out, float* lse,
+                                               int B, int Hq, int Hkv, int Lq, int head_dim,
+                                               int num_pages, int max_pages_per_seq, float scale,
+                                               void* stream) {
+    return paged_prefill_dev(q, k_pool, v_pool, block_table, ctx_lens, out, lse, B, Hq, Hkv, Lq,
+                             head_dim, num_pages, max_pages_per_seq, scale, as_stream(stream));
+}
 
 extern "C" int amp_flash_attn_fwd_bf16_dev(const void* Q, const void* K, const void* V, void* O,
                                            float* lse, int B, int Hq, int Hkv, int S_q, int S_kv,

@@ -105,6 +105,11 @@ int amp_device_status(int clear) {
     AMPB_CHECK_CUDA(cudaDeviceSynchronize());
     AMPB_CHECK_CUDA(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost));
     if (v && clear) AMPB_CHECK_CUDA(cudaMemset(p, 0, sizeof(int)));
+    if (v == 2) {
+        ampb::set_error(AMP_ERR_INVALID, "a kernel met a page id outside the KV pool "
+                        "(device status 2); the affected pages were skipped");
+        return AMP_ERR_INVALID;
+    }
     if (v) {
         ampb::set_error(AMP_ERR_TIMEOUT, "a kernel's bounded wait expired (device status %d)", v);
         return AMP_ERR_TIMEOUT;

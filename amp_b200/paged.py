@@ -1,0 +1,81 @@
+"""Attention over a paged KV cache (16-token pages addressed by block tables).
+
+Mirrors the block-table format of the reference's scheduler
+(``Sequence::kv_page_ids``, include/scheduler.hpp:61; 16-token pages,
+include/scheduler.hpp:88) with device tensors:
+
+  k_pool, v_pool  [num_pages, Hkv, 16, D] bf16
+  block_table     int32 [B, max_pages_per_seq]
+  ctx_lens        int32 [B]
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from ._lib import call, lib
+
+PAGE_TOKENS = 16
+
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _check_pools(k_pool, v_pool, block_table, ctx_lens):
+    for t, nm in ((k_pool, "k_pool"), (v_pool, "v_pool")):
+        if not t.is_cuda or t.dtype != torch.bfloat16 or not t.is_contiguous() or t.dim() != 4 \
+                or t.shape[2] != PAGE_TOKENS:
+            raise ValueError(f"{nm}: expected contiguous bf16 CUDA [pages, Hkv, 16, D]")
+    if k_pool.shape != v_pool.shape:
+        raise ValueError("k_pool and v_pool shapes differ")
+    for t, nm in ((block_table, "block_table"), (ctx_lens, "ctx_lens")):
+        if not t.is_cuda or t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError(f"{nm}: expected a contiguous int32 CUDA tensor")
+
+
+def decode_workspace_bytes(B: int, Hq: int, D: int, max_context_len: int) -> int:
+    return int(lib().amp_paged_decode_workspace_bytes(B, Hq, D, max_context_len))
+
+
+def paged_attn_decode(q, k_pool, v_pool, block_table, ctx_lens, max_context_len: int,
+                      scale: float = 0.0, out=None, lse=None, workspace=None):
+    """One query token per sequence: q [B, Hq, D] -> (out [B, Hq, D], lse [B, Hq])."""
+    _check_pools(k_pool, v_pool, block_table, ctx_lens)
+    B, Hq, D = q.shape
+    num_pages, Hkv = k_pool.shape[0], k_pool.shape[1]
+    out = out if out is not None else torch.empty_like(q)
+    lse = lse if lse is not None else torch.empty(B, Hq, dtype=torch.float32, device=q.device)
+    ws_b = decode_workspace_bytes(B, Hq, D, max_context_len)
+    ws = workspace if workspace is not None else torch.empty(ws_b, dtype=torch.uint8,
+                                                             device=q.device)
+    call("amp_paged_attn_decode_bf16_dev", q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+         block_table.data_ptr(), ctx_lens.data_ptr(), out.data_ptr(), lse.data_ptr(), B, Hq, Hkv,
+         D, num_pages, block_table.shape[1], max_context_len, float(scale), ws.data_ptr(),
+         ws.numel(), _stream(q))
+    return out, lse
+
+
+def paged_attn_prefill(q, k_pool, v_pool, block_table, ctx_lens, scale: float = 0.0,
+                       out=None, lse=None):
+    """q [B, Hq, Lq, D]: the last Lq tokens of each context, bottom-right causal."""
+    _check_pools(k_pool, v_pool, block_table, ctx_lens)
+    B, Hq, Lq, D = q.shape
+    num_pages, Hkv = k_pool.shape[0], k_pool.shape[1]
+    out = out if out is not None else torch.empty_like(q)
+    lse = lse if lse is not None else torch.empty(B, Hq, Lq, dtype=torch.float32,
+                                                  device=q.device)
+    call("amp_paged_attn_prefill_bf16_dev", q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+         block_table.data_ptr(), ctx_lens.data_ptr(), out.data_ptr(), lse.data_ptr(), B, Hq, Hkv,
+         Lq, D, num_pages, block_table.shape[1], float(scale), _stream(q))
+    return out, lse
+
+
+def validate_block_table(block_table: np.ndarray, ctx_lens: np.ndarray, num_pages: int) -> None:
+    """Host-side check before upload (raises AmpError on the first fault)."""
+    bt = np.ascontiguousarray(block_table, np.int32)
+    cl = np.ascontiguousarray(ctx_lens, np.int32)
+    call("amp_paged_validate_block_table", bt.ctypes.data, cl.ctypes.data, bt.shape[0],
+         bt.shape[1], num_pages)

@@ -50,3 +50,44 @@ def gemm_fp32_inputs(M: int, N: int, K: int, seed: int = 0):
     A = rng.uniform(-1.0, 1.0, (M, K)).astype(np.float32)
     B = rng.uniform(-1.0, 1.0, (K, N)).astype(np.float32)
     return A, B
+
+
+# Paged-KV GQA workload: batch 8, 32 query heads, 8 kv heads, head_dim 128,
+# context lengths ~ U[512, 16384], 16-token pages scattered by a seeded
+# random-permutation block table; prefill queries are the last 512 tokens.
+PAGED_B, PAGED_HQ, PAGED_HKV, PAGED_D, PAGE = 8, 32, 8, 128, 16
+PAGED_CTX_LO, PAGED_CTX_HI, PAGED_LQ = 512, 16384, 512
+
+
+def paged_layout(ctx_lens, seed: int = 0, extra_pages: int = 0):
+    """Block table for the given context lengths: pages of the pool handed out in
+    a seeded random permutation (the pool holds exactly the pages needed, plus
+    `extra_pages`).  Returns (block_table int32 [B, max_pages], num_pages)."""
+    ctx = np.asarray(ctx_lens, np.int64)
+    need = (ctx + PAGE - 1) // PAGE
+    num_pages = int(need.sum()) + extra_pages
+    perm = np.random.default_rng(seed).permutation(num_pages).astype(np.int32)
+    max_pages = int(max(1, need.max()))
+    bt = np.zeros((len(ctx), max_pages), np.int32)
+    pos = 0
+    for b, n in enumerate(need):
+        bt[b, :n] = perm[pos:pos + n]
+        pos += n
+    return bt, num_pages
+
+
+def paged_inputs(seed: int = 0, B: int = PAGED_B, Hq: int = PAGED_HQ, Hkv: int = PAGED_HKV,
+                 D: int = PAGED_D, ctx_lo: int = PAGED_CTX_LO, ctx_hi: int = PAGED_CTX_HI,
+                 ctx_lens=None):
+    """Host-side (numpy) paged workload: context lengths, block table and pools
+    of bf16 N(0,1) values (float32 arrays holding bf16-representable values)."""
+    rng = np.random.default_rng(seed)
+    if ctx_lens is None:
+        ctx_lens = rng.integers(ctx_lo, ctx_hi + 1, size=B)
+    ctx_lens = np.asarray(ctx_lens, np.int32)
+    bt, num_pages = paged_layout(ctx_lens, seed + 1)
+    def bf16(a):
+        return (f32_to_bf16_bits(a).astype(np.uint32) << 16).view(np.float32)
+    k_pool = bf16(rng.standard_normal((num_pages, Hkv, PAGE, D), dtype=np.float32))
+    v_pool = bf16(rng.standard_normal((num_pages, Hkv, PAGE, D), dtype=np.float32))
+    return ctx_lens, bt, num_pages, k_pool, v_pool

@@ -148,6 +148,43 @@ AMP_API int amp_flash_attn_fwd_bf16_dev(const void* Q, const void* K, const void
                                         float* lse, int B, int Hq, int Hkv, int S_q, int S_kv,
                                         int head_dim, int causal, float scale, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Attention over a paged KV cache (block tables of 16-token pages, the
+ * format of Sequence::kv_page_ids / kv_page_size_tokens in the reference's
+ * include/scheduler.hpp:61,88; the reference has no kernel that reads it).
+ *   k_pool, v_pool  [num_pages][Hkv][16][head_dim] bf16
+ *   block_table     int32 [B][max_pages_per_seq]: token t of sequence b is
+ *                   slot t % 16 of page block_table[b][t / 16]
+ *   ctx_lens        int32 [B], tokens in each sequence's cache (device)
+ * Slots past a sequence's context in its last page may hold any finite
+ * values.  Page ids outside [0, num_pages) are never dereferenced: they are
+ * skipped and reported by amp_device_status (AMP_ERR_INVALID).
+ * ---------------------------------------------------------------------- */
+/* Decode: one query token per sequence, q/out [B][Hq][head_dim], lse [B][Hq]
+ * (may be NULL); split-KV with a workspace of
+ * amp_paged_decode_workspace_bytes(B, Hq, head_dim, max_context_len) bytes.
+ * head_dim 128; Hq/Hkv in {1, 2, 4, 8}. */
+AMP_API size_t amp_paged_decode_workspace_bytes(int B, int Hq, int head_dim, int max_context_len);
+AMP_API int amp_paged_attn_decode_bf16_dev(const void* q, const void* k_pool, const void* v_pool,
+                                           const int32_t* block_table, const int32_t* ctx_lens,
+                                           void* out, float* lse, int B, int Hq, int Hkv,
+                                           int head_dim, int num_pages, int max_pages_per_seq,
+                                           int max_context_len, float scale, void* workspace,
+                                           size_t workspace_bytes, void* stream);
+/* Prefill: q/out [B][Hq][Lq][head_dim] are the LAST Lq tokens of each
+ * sequence's context (ctx_lens[b] >= Lq), causal with bottom-right alignment
+ * (query i sits at position ctx_lens[b] - Lq + i); lse [B][Hq][Lq].
+ * head_dim 64 or 128. */
+AMP_API int amp_paged_attn_prefill_bf16_dev(const void* q, const void* k_pool, const void* v_pool,
+                                            const int32_t* block_table, const int32_t* ctx_lens,
+                                            void* out, float* lse, int B, int Hq, int Hkv, int Lq,
+                                            int head_dim, int num_pages, int max_pages_per_seq,
+                                            float scale, void* stream);
+/* Host-side check of a block table (host arrays) before upload: ids in range,
+ * no page used twice, rows long enough for the contexts. */
+AMP_API int amp_paged_validate_block_table(const int32_t* block_table, const int32_t* ctx_lens,
+                                           int B, int max_pages_per_seq, int num_pages);
+
 /* Host-pointer form of the attention forward (plugin convention). */
 AMP_API int amp_user_flash_attn_fwd_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V,
                                          uint16_t* O, float* lse, int B, int Hq, int Hkv, int S_q,

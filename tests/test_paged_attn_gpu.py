@@ -1,0 +1,148 @@
+"""Paged-KV GQA decode and prefill on the B200 vs the fp64 oracle.
+
+The oracle gathers each sequence's pages through the block table into a
+contiguous K/V (oracle.attention.paged_gather) and runs the fp64 attention
+restatement: decode = the query at position ctx-1 sees every key; prefill =
+the last Lq positions, causal with bottom-right alignment.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from oracle import attention as ref
+from amp_b200 import paged, workloads
+from amp_b200._lib import AmpError, lib
+
+pytestmark = pytest.mark.gpu
+TOL_O = 2e-2
+TOL_LSE = 2e-3
+
+
+def bf16_np(a):
+    return (oracle.f32_to_bf16_bits(a).astype(np.uint32) << 16).view(np.float32)
+
+
+def to_dev(ctx, bt, kp, vp):
+    return (torch.from_numpy(kp).to(torch.bfloat16).cuda(),
+            torch.from_numpy(vp).to(torch.bfloat16).cuda(),
+            torch.from_numpy(bt).cuda(), torch.from_numpy(ctx).cuda())
+
+
+def decode_ref(q, ctx, bt, kp, vp, heads=None):
+    B, Hq, D = q.shape
+    O = np.full((B, Hq, D), np.nan)
+    L = np.full((B, Hq), np.nan)
+    for b in range(B):
+        k = ref.paged_gather(kp, bt[b], int(ctx[b]))[None]     # [1, Hkv, ctx, D]
+        v = ref.paged_gather(vp, bt[b], int(ctx[b]))[None]
+        o, lse = ref.flash_attn_fwd(q[b][None, :, None, :], k, v, causal=False)
+        O[b], L[b] = o[0, :, 0], lse[0, :, 0]
+    return O, L
+
+
+def run_decode(q, ctx, bt, kp, vp):
+    k_pool, v_pool, btd, ctxd = to_dev(ctx, bt, kp, vp)
+    out, lse = paged.paged_attn_decode(torch.from_numpy(q).to(torch.bfloat16).cuda(), k_pool,
+                                       v_pool, btd, ctxd, int(ctx.max()))
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy(), lse.cpu().numpy()
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(8, 2), (4, 4), (16, 8), (32, 4)])
+def test_decode_small(Hq, Hkv, cuda, amp_lib):
+    ctx = np.array([1, 17, 1000, 513, 16], np.int32)
+    ctx, bt, npg, kp, vp = workloads.paged_inputs(seed=Hq, B=5, Hq=Hq, Hkv=Hkv, ctx_lens=ctx)
+    q = bf16_np(np.random.default_rng(Hq).standard_normal((5, Hq, 128), dtype=np.float32))
+    out, lse = run_decode(q, ctx, bt, kp, vp)
+    assert lib().amp_device_status(1) == 0
+    O, L = decode_ref(q, ctx, bt, kp, vp)
+    assert oracle.max_rel_err(out, O) < TOL_O
+    assert np.abs(lse - L).max() < TOL_LSE
+
+
+def test_decode_full_workload(cuda, amp_lib):
+    ctx, bt, npg, kp, vp = workloads.paged_inputs(seed=11)
+    q = bf16_np(np.random.default_rng(12).standard_normal((8, 32, 128), dtype=np.float32))
+    out, lse = run_decode(q, ctx, bt, kp, vp)
+    assert lib().amp_device_status(1) == 0
+    O, L = decode_ref(q, ctx, bt, kp, vp)
+    assert oracle.max_rel_err(out, O) < TOL_O
+    assert np.abs(lse - L).max() < TOL_LSE
+
+
+def test_decode_garbage_past_context_is_ignored(cuda, amp_lib):
+    ctx = np.array([20, 33], np.int32)
+    ctx, bt, npg, kp, vp = workloads.paged_inputs(seed=3, B=2, Hq=8, Hkv=2, ctx_lens=ctx)
+    kp2, vp2 = kp.copy(), vp.copy()
+    for b in range(2):   # NaN/inf in the unused slots of each last page
+        last = bt[b, (ctx[b] - 1) // 16]
+        kp2[last, :, ctx[b] % 16:] = np.nan
+        vp2[last, :, ctx[b] % 16:] = np.inf
+    q = bf16_np(np.random.default_rng(4).standard_normal((2, 8, 128), dtype=np.float32))
+    out, lse = run_decode(q, ctx, bt, kp2, vp2)
+    O, L = decode_ref(q, ctx, bt, kp, vp)
+    assert np.isfinite(out).all() and oracle.max_rel_err(out, O) < TOL_O
+
+
+def test_decode_bad_page_id_is_flagged_not_dereferenced(cuda, amp_lib):
+    ctx = np.array([40, 40], np.int32)
+    ctx, bt, npg, kp, vp = workloads.paged_inputs(seed=5, B=2, Hq=8, Hkv=2, ctx_lens=ctx)
+    bt = bt.copy()
+    bt[1, 1] = npg + 1000          # far outside the pool
+    q = bf16_np(np.random.default_rng(6).standard_normal((2, 8, 128), dtype=np.float32))
+    out, lse = run_decode(q, ctx, bt, kp, vp)
+    assert lib().amp_device_status(1) == -1   # AMP_ERR_INVALID, then cleared
+    assert lib().amp_device_status(1) == 0
+    O, L = decode_ref(q[:1], ctx[:1], bt[:1], kp, vp)
+    assert oracle.max_rel_err(out[:1], O) < TOL_O   # the other sequence is unaffected
+
+
+def prefill_ref(q, ctx, bt, kp, vp, heads):
+    B, Hq, Lq, D = q.shape
+    O = np.full(q.shape, np.nan)
+    L = np.full((B, Hq, Lq), np.nan)
+    for b in sorted({b for b, _ in heads}):
+        k = ref.paged_gather(kp, bt[b], int(ctx[b]))[None]
+        v = ref.paged_gather(vp, bt[b], int(ctx[b]))[None]
+        hs = [(0, h) for bb, h in heads if bb == b]
+        o, lse = ref.flash_attn_fwd(q[b][None], k, v, causal=True,
+                                    causal_offset=int(ctx[b]) - Lq, heads=hs)
+        for _, h in hs:
+            O[b, h], L[b, h] = o[0, h], lse[0, h]
+    return O, L
+
+
+def run_prefill(q, ctx, bt, kp, vp):
+    k_pool, v_pool, btd, ctxd = to_dev(ctx, bt, kp, vp)
+    out, lse = paged.paged_attn_prefill(torch.from_numpy(q).to(torch.bfloat16).cuda(), k_pool,
+                                        v_pool, btd, ctxd)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy(), lse.cpu().numpy()
+
+
+@pytest.mark.parametrize("Lq,ctx", [(128, [128, 300, 700]), (100, [100, 257, 1000]),
+                                    (1, [1, 16, 17]), (256, [4096, 260, 1024])])
+def test_prefill_small(Lq, ctx, cuda, amp_lib):
+    ctx = np.array(ctx, np.int32)
+    ctx, bt, npg, kp, vp = workloads.paged_inputs(seed=Lq, B=3, Hq=8, Hkv=2, ctx_lens=ctx)
+    q = bf16_np(np.random.default_rng(Lq).standard_normal((3, 8, Lq, 128), dtype=np.float32))
+    out, lse = run_prefill(q, ctx, bt, kp, vp)
+    assert lib().amp_device_status(1) == 0
+    heads = [(b, h) for b in range(3) for h in range(8)]
+    O, L = prefill_ref(q, ctx, bt, kp, vp, heads)
+    assert oracle.max_rel_err(out, O) < TOL_O
+    assert np.abs(lse - L).max() < TOL_LSE
+
+
+def test_prefill_full_workload_sampled_heads(cuda, amp_lib):
+    ctx, bt, npg, kp, vp = workloads.paged_inputs(seed=21)
+    q = bf16_np(np.random.default_rng(22).standard_normal((8, 32, 512, 128), dtype=np.float32))
+    out, lse = run_prefill(q, ctx, bt, kp, vp)
+    assert lib().amp_device_status(1) == 0
+    assert np.isfinite(out).all()
+    heads = [(0, 0), (3, 13), (7, 31), (int(np.argmax(ctx)), 5)]
+    O, L = prefill_ref(q, ctx, bt, kp, vp, heads)
+    for b, h in heads:
+        assert oracle.max_rel_err(out[b, h], O[b, h]) < TOL_O
+        assert np.abs(lse[b, h] - L[b, h]).max() < TOL_LSE
