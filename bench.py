@@ -495,8 +495,177 @@ class AttentionWorkload:
                           "(the reference has no CPU attention path)"}
 
 
+class PagedDecodeWorkload:
+    """GQA decode over the paged KV cache (B=8, Hq=32, Hkv=8, D=128, ctx ~ U[512,16384],
+    16-token pages, seeded random-permutation block table); HBM-bound."""
+    name = "paged_decode"
+    metric = "paged_gqa_decode_GBps"
+    unit = "GB/s"
+    scale = 1e9
+    dtype = "bf16"
+    bound = "hbm"
+    scaling = "weak"
+    prefill = False
+
+    def __init__(self, dist: Dist, args):
+        import torch
+        from amp_b200 import paged, workloads as wl
+        self.torch, self.paged, self.dist = torch, paged, dist
+        rng = np.random.default_rng(2025 + dist.rank)
+        self.ctx = rng.integers(wl.PAGED_CTX_LO, wl.PAGED_CTX_HI + 1, size=wl.PAGED_B).astype(np.int32)
+        bt, self.num_pages = wl.paged_layout(self.ctx, seed=2026 + dist.rank)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev)
+        g.manual_seed(7 + dist.rank)
+        self.B, self.Hq, self.Hkv, self.D = wl.PAGED_B, wl.PAGED_HQ, wl.PAGED_HKV, wl.PAGED_D
+        shape = (self.num_pages, self.Hkv, wl.PAGE, self.D)
+        self.k_pool = torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+        self.v_pool = torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+        self.bt_h = torch.from_numpy(bt).pin_memory()
+        self.ctx_h = torch.from_numpy(self.ctx).pin_memory()
+        self.bt = self.bt_h.to(dev)
+        self.ctxd = self.ctx_h.to(dev)
+        self.Lq = wl.PAGED_LQ if self.prefill else 1
+        qshape = (self.B, self.Hq, self.Lq, self.D) if self.prefill else (self.B, self.Hq, self.D)
+        self.q = torch.randn(qshape, generator=g, device=dev).to(torch.bfloat16)
+        self.out = torch.empty_like(self.q)
+        self.lse = torch.empty(qshape[:-1], dtype=torch.float32, device=dev)
+        self.max_ctx = int(self.ctx.max())
+        self.ws = (None if self.prefill else torch.empty(
+            paged.decode_workspace_bytes(self.B, self.Hq, self.D, self.max_ctx),
+            dtype=torch.uint8, device=dev))
+
+    def units_per_step(self) -> float:
+        # K + V of every context token for every kv head, plus q/out/lse/table
+        kv = int(self.ctx.sum()) * self.Hkv * self.D * 2 * 2
+        return float(kv + 2 * self.q.numel() * 2 + self.lse.numel() * 4 + self.bt.numel() * 4)
+
+    def launches_per_step(self) -> int:
+        return 2
+
+    def config(self):
+        return {"workload": "paged_gqa_decode", "batch": self.B, "q_heads": self.Hq,
+                "kv_heads": self.Hkv, "head_dim": self.D, "page_tokens": 16,
+                "context_lens": self.ctx.tolist(), "total_context": int(self.ctx.sum()),
+                "block_table": "seeded random permutation of the pool",
+                "l2": "KV pools exceed L2; 256 MiB flush before every step",
+                "parallelism": "replicas (each rank its own batch)" if self.dist.world > 1
+                else "single"}
+
+    def kernel_table(self):
+        return [("k_paged_decode + k_paged_combine", self.units_per_step())]
+
+    def _launch(self):
+        self.paged.paged_attn_decode(self.q, self.k_pool, self.v_pool, self.bt, self.ctxd,
+                                     self.max_ctx, out=self.out, lse=self.lse, workspace=self.ws)
+
+    def step(self, ev=None):
+        if ev: ev[0].record()
+        self._launch()
+        if ev: ev[1].record()
+
+    def e2e(self, steps: int, warmup: int):
+        """Public Python API with the step's inputs (q, block table, context
+        lengths) copied from pinned host memory and the output read back; the KV
+        pools are resident cache state."""
+        torch = self.torch
+        qh = self.q.cpu().pin_memory()
+        oh = torch.empty_like(qh).pin_memory()
+        dev = self.q.device
+
+        def fn():
+            self.q.copy_(qh, non_blocking=True)
+            self.bt.copy_(self.bt_h, non_blocking=True)
+            self.ctxd.copy_(self.ctx_h, non_blocking=True)
+            self._launch()
+            oh.copy_(self.out, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+        ms = _e2e_time_stream(torch, fn, steps, warmup)
+        return {"value": self.units_per_step() / (ms * 1e-3) / self.scale, "unit": self.unit,
+                "ms_per_step": ms,
+                "h2d_bytes_per_step": qh.numel() * 2 + self.bt.numel() * 4 + self.ctx.size * 4,
+                "d2h_bytes_per_step": oh.numel() * 2,
+                "api": "amp_b200.paged." + ("paged_attn_prefill" if self.prefill
+                                            else "paged_attn_decode")}
+
+    @classmethod
+    def cpu_reference(cls, args, budget_s: float, threads: int):
+        """No CPU attention path exists in the reference: the fp64 oracle on one
+        sequence of the workload (gather through the block table + attention)."""
+        from oracle import attention as ref
+        from amp_b200 import workloads as wl
+        ctx = np.array([8448], np.int32)   # the mean context of U[512, 16384]
+        ctx, bt, npg, kp, vp = wl.paged_inputs(seed=1, B=1, ctx_lens=ctx)
+        rng = np.random.default_rng(2)
+        Lq = wl.PAGED_LQ if cls.prefill else 1
+        q = rng.standard_normal((1, wl.PAGED_HQ, Lq, wl.PAGED_D)).astype(np.float32)
+
+        def run():
+            k = ref.paged_gather(kp, bt[0], int(ctx[0]))[None]
+            v = ref.paged_gather(vp, bt[0], int(ctx[0]))[None]
+            ref.flash_attn_fwd(q, k, v, causal=cls.prefill, causal_offset=int(ctx[0]) - Lq)
+        reps, dt = timed_reps(run, budget_s)
+        if cls.prefill:
+            units = 4.0 * wl.PAGED_HQ * wl.PAGED_D * sum(int(ctx[0]) - Lq + i + 1
+                                                         for i in range(Lq))
+        else:
+            units = float(int(ctx[0]) * wl.PAGED_HKV * wl.PAGED_D * 4)
+        return {"value": units * reps / dt / cls.scale, "unit": cls.unit, "cores": threads,
+                "kind": "port",
+                "sample": f"{reps} sequence(s) of context {int(ctx[0])} in {dt:.1f} s; fp64 "
+                          "numpy oracle (the reference has no attention kernel for block tables)"}
+
+
+class PagedPrefillWorkload(PagedDecodeWorkload):
+    """The last 512 tokens of every context as a paged prefill (bottom-right causal)."""
+    name = "paged_prefill"
+    metric = "paged_gqa_prefill_TFLOPS"
+    unit = "TFLOP/s"
+    scale = 1e12
+    bound = "tensor"
+    prefill = True
+
+    def units_per_step(self) -> float:
+        Lq = self.Lq
+        pairs = sum(Lq * (int(c) - Lq) + Lq * (Lq + 1) // 2 for c in self.ctx)
+        return 4.0 * self.Hq * self.D * pairs
+
+    def launches_per_step(self) -> int:
+        return 1
+
+    def config(self):
+        c = super().config()
+        c.update({"workload": "paged_gqa_prefill", "new_tokens_per_seq": self.Lq,
+                  "flop_convention": "4*Hq*D*sum(visible (query, key) pairs)"})
+        return c
+
+    def kernel_table(self):
+        return [("k_flash_fwd<128, paged>", self.units_per_step())]
+
+    def _launch(self):
+        self.paged.paged_attn_prefill(self.q, self.k_pool, self.v_pool, self.bt, self.ctxd,
+                                      out=self.out, lse=self.lse)
+
+
 WORKLOADS = {w.name: w for w in (QuantWorkload, GemmWorkload, GemmFp8Workload,
-                                 AttentionWorkload)}
+                                 AttentionWorkload, PagedDecodeWorkload, PagedPrefillWorkload)}
+
+
+def _e2e_time_stream(torch, fn, steps, warmup):
+    """Like _e2e_time, for callables that enqueue on torch's current stream."""
+    for _ in range(warmup):
+        fn()
+    st = torch.cuda.current_stream()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        s.record(st)
+        fn()
+        e.record(st)
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    return sum(times) / len(times)
 
 
 def _e2e_time(torch, fn, steps, warmup):
