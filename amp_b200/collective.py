@@ -1,0 +1,111 @@
+"""Collectives for sharded use of the kernels: the thin NCCL layer.
+
+Mirrors the operations of the reference's include/collective.hpp
+(allreduce / allgather / broadcast / reduce_scatter / barrier,
+collective.hpp:79-104, CommGroup collective.hpp:34-40) on top of
+torch.distributed, whose NCCL backend runs over NVLink / NVSwitch on a B200
+node.  Only two exchanges sit on the hot path: a 1-float all-reduce(MAX) of
+the FP8 amax and the all-gather that reassembles a sharded output.  The
+functions are backend-agnostic (gloo on CPU runs them in tests).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+_OPS = {"sum": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN,
+        "prod": dist.ReduceOp.PRODUCT}
+
+
+@dataclass
+class CommGroup:
+    """The reference's CommGroup (rank, world, device) over a process group."""
+    rank: int = 0
+    world: int = 1
+    device_id: int = 0
+    group: object = None
+
+    @classmethod
+    def current(cls, group=None) -> "CommGroup":
+        if not dist.is_available() or not dist.is_initialized():
+            return cls()
+        dev = torch.cuda.current_device() if torch.cuda.is_available() else 0
+        return cls(dist.get_rank(group), dist.get_world_size(group), dev, group)
+
+
+def allreduce(g: CommGroup, buf: torch.Tensor, op: str = "sum") -> torch.Tensor:
+    if g.world > 1:
+        dist.all_reduce(buf, op=_OPS[op], group=g.group)
+    return buf
+
+
+def broadcast(g: CommGroup, buf: torch.Tensor, root: int = 0) -> torch.Tensor:
+    if g.world > 1:
+        dist.broadcast(buf, src=root, group=g.group)
+    return buf
+
+
+def allgather(g: CommGroup, send: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[r] = send of rank r (out has a leading world dimension)."""
+    out = out if out is not None else send.new_empty((g.world, *send.shape))
+    if g.world == 1:
+        out[0].copy_(send)
+    else:
+        # the concatenated-along-dim-0 form is accepted by every backend
+        flat = out.view(g.world * send.shape[0], *send.shape[1:]) if send.dim() else out
+        dist.all_gather_into_tensor(flat, send.contiguous(), group=g.group)
+    return out
+
+
+def reduce_scatter(g: CommGroup, send: torch.Tensor, op: str = "sum") -> torch.Tensor:
+    """send has a leading world dimension; returns this rank's reduced slice."""
+    out = send.new_empty(send.shape[1:])
+    if g.world == 1:
+        out.copy_(send[0])
+    else:
+        flat = send.contiguous().view(-1, *send.shape[2:]) if send.dim() > 1 else send
+        dist.reduce_scatter_tensor(out, flat, op=_OPS[op], group=g.group)
+    return out
+
+
+def barrier(g: CommGroup) -> None:
+    if g.world > 1:
+        dist.barrier(group=g.group)
+
+
+# ----------------------------------------------------------------------
+# partitioning of the three sharded workloads
+# ----------------------------------------------------------------------
+def column_range(n: int, g: CommGroup, align: int = 1) -> tuple[int, int]:
+    """This rank's [start, stop) of n columns; every shard a multiple of `align`."""
+    if n % (g.world * align):
+        raise ValueError(f"{n} columns do not split into {g.world} shards of multiples of {align}")
+    w = n // g.world
+    return g.rank * w, (g.rank + 1) * w
+
+
+def gather_columns(g: CommGroup, c_shard: torch.Tensor) -> torch.Tensor:
+    """All-gather N-sharded C blocks [M, N/p] and lay them out as row-major [M, N]."""
+    parts = allgather(g, c_shard)                 # [p, M, N/p]
+    return parts.permute(1, 0, 2).reshape(c_shard.shape[0], -1)
+
+
+def head_range(bh: int, g: CommGroup) -> tuple[int, int]:
+    """This rank's contiguous slice of the flattened batch*heads of attention."""
+    if bh % g.world:
+        raise ValueError(f"{bh} batch*heads do not split over {g.world} ranks")
+    w = bh // g.world
+    return g.rank * w, (g.rank + 1) * w
+
+
+def gather_heads(g: CommGroup, o_shard: torch.Tensor) -> torch.Tensor:
+    """All-gather (batch*head)-sharded outputs [bh/p, ...] into [bh, ...]."""
+    parts = allgather(g, o_shard)
+    return parts.reshape(-1, *o_shard.shape[1:])
+
+
+def global_amax(g: CommGroup, local_amax: torch.Tensor) -> torch.Tensor:
+    """1-float all-reduce(MAX): the per-tensor amax of a tensor sharded over ranks."""
+    return allreduce(g, local_amax, "max")

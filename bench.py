@@ -43,6 +43,8 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
+# rank 0's stdout carries exactly one JSON line: keep NCCL's banner off it
+os.environ["NCCL_DEBUG"] = os.environ.get("AMP_B200_NCCL_DEBUG", "WARN")
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 

@@ -1,0 +1,77 @@
+"""Sharded kernels over NCCL on 2 GPUs vs the unsharded single-GPU result.
+
+Skipped on boxes with fewer than two GPUs.  Each rank is a separate process
+(one process per GPU), NVLS off, short process-group timeout.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank_main(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from amp_b200 import fp8, sharded, workloads, gemm, attention
+        dev = torch.device("cuda", rank)
+        # quantise: shard of a global tensor, global amax
+        full = workloads.quant_input_numpy(1 << 20, seed=3)
+        n = full.size // world
+        x_full = torch.from_numpy(full.view(np.int16).copy()).to(dev).view(torch.bfloat16)
+        q_shard, s_shard = sharded.quantize_e4m3_sharded(x_full[rank * n:(rank + 1) * n])
+        q_ref, s_ref = fp8.quantize_e4m3(x_full)
+        assert torch.equal(q_shard, q_ref[rank * n:(rank + 1) * n]) and s_shard.item() == s_ref.item()
+        # N-split GEMM + gather
+        g = torch.Generator(device=dev).manual_seed(5)
+        A = torch.randn(512, 256, generator=g, device=dev).to(torch.bfloat16)
+        B = torch.randn(256, 1024, generator=g, device=dev).to(torch.bfloat16)
+        w = 1024 // world
+        C = sharded.matmul_bf16_sharded(A, B[:, rank * w:(rank + 1) * w].contiguous())
+        C_ref = torch.empty(512, 1024, dtype=torch.bfloat16, device=dev)
+        gemm.launch_matmul_bf16(A, B, C_ref, 512, 1024, 256)
+        assert torch.equal(C, C_ref)
+        # (batch*head)-split attention + gather
+        qa, ka, va = (torch.randn(2, 4, 256, 128, generator=g, device=dev).to(torch.bfloat16)
+                      for _ in range(3))
+        O, L = sharded.flash_attn_sharded(qa, ka, va, True)
+        O_ref, L_ref = attention.flash_attn_fwd(qa, ka, va, True)
+        assert torch.equal(O, O_ref) and torch.equal(L, L_ref)
+        torch.cuda.synchronize()
+        q.put((rank, "ok"))
+    except Exception as e:
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharded_ops_match_single_gpu(amp_lib):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert all(v == "ok" for v in res.values()), res
