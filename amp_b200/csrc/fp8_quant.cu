@@ -8,14 +8,15 @@
 //                             shuffle + shared-memory block reduce, one
 //                             partial per block into the workspace.
 //   pass 2  k_quant_encode  : every block folds the <= 2048 partials (L2
-//                             resident) into amax, scale = amax/448, then
-//                             encodes 16 elements per thread-iteration
-//                             (2 x 16 B loads, 1 x 16 B store) with IEEE
-//                             division and cvt.rn.satfinite.e4m3x2.  Chunks
-//                             are walked last-to-first so the tail that pass 1
-//                             read most recently is still in L2.
+//                             resident) into amax, scale = amax/448,
+//                             inv = RN(1/scale), then encodes x * inv with
+//                             cvt.rn.satfinite.e4m3x2.f32, one 16-element
+//                             chunk (2 x 16 B loads, 1 x 16 B store) per
+//                             thread on a deep grid; chunks are walked
+//                             last-to-first so the tail that pass 1 read most
+//                             recently is still in L2.
 //   k_dequant              : 16 codes (16 B) -> 16 bf16 (2 x 16 B) per
-//                             thread-iteration via cvt.rn.f16x2.e4m3x2.
+//                             thread via cvt.rn.f16x2.e4m3x2, deep grid.
 //
 // Algorithmic bytes: quantise 5 B/element (2 amax read + 2 read + 1 write),
 // dequantise 3 B/element (1 read + 2 write).
@@ -29,7 +30,9 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kMaxParts = 2048;
-constexpr int kBlocksPerSM = 8;
+constexpr int kBlocksPerSM = 8;          // amax pass (one partial per block)
+constexpr int kEncodeBlocksPerSM = 32;
+constexpr int kDequantBlocksPerSM = 64;
 
 __device__ __forceinline__ uint32_t absmax_bf16x2(uint32_t m, uint32_t w) {
     uint32_t a = w & 0x7fff7fffu, r;
@@ -85,15 +88,23 @@ __global__ void __launch_bounds__(kThreads) k_amax_partials(const uint16_t* __re
     if (threadIdx.x == 0) parts[blockIdx.x] = f;
 }
 
-// 4 bf16 (two packed words) -> 4 E4M3 codes packed little-endian.
-__device__ __forceinline__ uint32_t enc4(uint32_t w0, uint32_t w1, float s) {
-    uint32_t lo = f32x2_to_e4m3x2(__fdiv_rn(bf16_lo(w0), s), __fdiv_rn(bf16_hi(w0), s));
-    uint32_t hi = f32x2_to_e4m3x2(__fdiv_rn(bf16_lo(w1), s), __fdiv_rn(bf16_hi(w1), s));
+// 1/scale, correctly rounded, clamped to FLT_MAX so that 0 * inv stays 0 for
+// a tiny (subnormal) scale.
+__device__ __forceinline__ float inv_scale(float s) {
+    const float inv = __frcp_rn(s);
+    return inv > 3.402823466e38f ? 3.402823466e38f : inv;
+}
+
+// 4 bf16 (two packed words) -> 4 E4M3 codes packed little-endian: RN(x * inv),
+// then round-to-nearest-even with saturation.
+__device__ __forceinline__ uint32_t enc4(uint32_t w0, uint32_t w1, float inv) {
+    uint32_t lo = f32x2_to_e4m3x2(__fmul_rn(bf16_lo(w0), inv), __fmul_rn(bf16_hi(w0), inv));
+    uint32_t hi = f32x2_to_e4m3x2(__fmul_rn(bf16_lo(w1), inv), __fmul_rn(bf16_hi(w1), inv));
     return lo | (hi << 16);
 }
 
-__device__ __forceinline__ uint8_t enc1(uint16_t h, float s) {
-    return (uint8_t)(f32x2_to_e4m3x2(__fdiv_rn(bf16_lo(h), s), 0.0f) & 0xffu);
+__device__ __forceinline__ uint8_t enc1(uint16_t h, float inv) {
+    return (uint8_t)(f32x2_to_e4m3x2(__fmul_rn(bf16_lo(h), inv), 0.0f) & 0xffu);
 }
 
 __global__ void __launch_bounds__(kThreads) k_quant_encode(
@@ -113,6 +124,7 @@ __global__ void __launch_bounds__(kThreads) k_quant_encode(
         if (scale_out) *scale_out = s;
         if (amax_out) *amax_out = amax;
     }
+    const float inv = inv_scale(s);
     const int64_t nthr = (int64_t)gridDim.x * kThreads;
     const int64_t tid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
     int64_t done = 0;
@@ -121,23 +133,32 @@ __global__ void __launch_bounds__(kThreads) k_quant_encode(
         for (int64_t c = tid; c < nc; c += nthr) {
             const int64_t ci = nc - 1 - c;
             const uint4* src = reinterpret_cast<const uint4*>(x + ci * 16);
-            uint4 a = ldg_stream_v4(src);
-            uint4 b = ldg_stream_v4(src + 1);
+            const uint4 a = ldg_stream_v4(src), b = ldg_stream_v4(src + 1);
             uint4 o;
-            o.x = enc4(a.x, a.y, s);
-            o.y = enc4(a.z, a.w, s);
-            o.z = enc4(b.x, b.y, s);
-            o.w = enc4(b.z, b.w, s);
+            o.x = enc4(a.x, a.y, inv);
+            o.y = enc4(a.z, a.w, inv);
+            o.z = enc4(b.x, b.y, inv);
+            o.w = enc4(b.z, b.w, inv);
             stg_v4(q + ci * 16, o);
         }
         done = nc << 4;
     }
-    for (int64_t j = done + tid; j < n; j += nthr) q[j] = enc1(x[j], s);
+    for (int64_t j = done + tid; j < n; j += nthr) q[j] = enc1(x[j], inv);
 }
 
 __device__ __forceinline__ uint32_t dec2(uint32_t codes16, float s) {
     uint32_t h = e4m3x2_to_f16x2((uint16_t)codes16);
     return f32x2_to_bf16x2(__fmul_rn(f16_lo_to_f32(h), s), __fmul_rn(f16_hi_to_f32(h), s));
+}
+
+__device__ __forceinline__ void dec16_store(uint4 v, float s, uint16_t* dst) {
+    uint4 o0, o1;
+    o0.x = dec2(v.x & 0xffffu, s); o0.y = dec2(v.x >> 16, s);
+    o0.z = dec2(v.y & 0xffffu, s); o0.w = dec2(v.y >> 16, s);
+    o1.x = dec2(v.z & 0xffffu, s); o1.y = dec2(v.z >> 16, s);
+    o1.z = dec2(v.w & 0xffffu, s); o1.w = dec2(v.w >> 16, s);
+    stg_v4(dst, o0);
+    stg_v4(dst + 8, o1);
 }
 
 __global__ void __launch_bounds__(kThreads) k_dequant(const uint8_t* __restrict__ q, int64_t n,
@@ -149,19 +170,19 @@ __global__ void __launch_bounds__(kThreads) k_dequant(const uint8_t* __restrict_
     int64_t done = 0;
     if (vec_ok) {
         const int64_t nc = n >> 4;
-        for (int64_t c = tid; c < nc; c += nthr) {
-            uint4 v = ldg_stream_v4(q + c * 16);
-            uint4 o0, o1;
-            o0.x = dec2(v.x & 0xffffu, s); o0.y = dec2(v.x >> 16, s);
-            o0.z = dec2(v.y & 0xffffu, s); o0.w = dec2(v.y >> 16, s);
-            o1.x = dec2(v.z & 0xffffu, s); o1.y = dec2(v.z >> 16, s);
-            o1.z = dec2(v.w & 0xffffu, s); o1.w = dec2(v.w >> 16, s);
-            stg_v4(y + c * 16, o0);
-            stg_v4(y + c * 16 + 8, o1);
-        }
+        for (int64_t c = tid; c < nc; c += nthr) dec16_store(ldg_stream_v4(q + c * 16), s, y + c * 16);
         done = nc << 4;
     }
     for (int64_t j = done + tid; j < n; j += nthr) y[j] = (uint16_t)(dec2(q[j], s) & 0xffffu);
+}
+
+// Grid for the elementwise passes: one work item per thread up to
+// `per_sm` blocks per SM, grid-stride beyond.
+inline int grid_deep(int64_t work_items, int per_sm) {
+    const int64_t cap = (int64_t)sm_count() * per_sm;
+    int64_t want = (work_items + kThreads - 1) / kThreads;
+    if (want < 1) want = 1;
+    return (int)(want < cap ? want : cap);
 }
 
 inline int grid_for(int64_t work_items) {
@@ -178,6 +199,26 @@ int launch_amax(const void* x, int64_t n, float* parts, int* nparts_out, cudaStr
     *nparts_out = grid;
     k_amax_partials<<<grid, kThreads, 0, st>>>(static_cast<const uint16_t*>(x), n, parts, vec);
     AMPB_CHECK_LAUNCH("k_amax_partials");
+    return AMP_OK;
+}
+
+// Encode pass: one 16-element chunk per thread and a deep grid (up to 32
+// blocks per SM, grid-stride beyond that) keeps the most loads in flight.
+int launch_encode(const void* x, int64_t n, const float* parts, int nparts, const float* amax_in,
+                  uint8_t* q, float* scale_out, float* amax_out, cudaStream_t st) {
+    const int vec = aligned16(x) && aligned16(q);
+    const int grid = grid_deep(vec ? (n >> 4) : n, kEncodeBlocksPerSM);
+    k_quant_encode<<<grid, kThreads, 0, st>>>(static_cast<const uint16_t*>(x), n, parts, nparts,
+                                              amax_in, q, scale_out, amax_out, vec);
+    AMPB_CHECK_LAUNCH("k_quant_encode");
+    return AMP_OK;
+}
+
+int launch_dequant(const uint8_t* q, int64_t n, const float* scale, void* y, cudaStream_t st) {
+    const int vec = aligned16(q) && aligned16(y);
+    const int grid = grid_deep(vec ? (n >> 4) : n, kDequantBlocksPerSM);
+    k_dequant<<<grid, kThreads, 0, st>>>(q, n, scale, static_cast<uint16_t*>(y), vec);
+    AMPB_CHECK_LAUNCH("k_dequant");
     return AMP_OK;
 }
 
@@ -206,12 +247,7 @@ int quant_e4m3_dev(const void* x, int64_t n, uint8_t* q, float* scale_out, float
         rc = launch_amax(x, n, parts, &nparts, st);
         if (rc) return rc;
     }
-    const int vec = aligned16(x) && aligned16(q);
-    const int grid = grid_for(vec ? (n >> 4) : n);
-    k_quant_encode<<<grid, kThreads, 0, st>>>(static_cast<const uint16_t*>(x), n, parts, nparts,
-                                              nullptr, q, scale_out, amax_out, vec);
-    AMPB_CHECK_LAUNCH("k_quant_encode");
-    return AMP_OK;
+    return launch_encode(x, n, parts, nparts, nullptr, q, scale_out, amax_out, st);
 }
 
 }  // namespace ampb
@@ -256,12 +292,7 @@ int amp_fp8_quant_e4m3_from_amax_dev(const void* x_bf16, int64_t n, const float*
     AMPB_REQUIRE(amax_in != nullptr, AMP_ERR_INVALID, "amax_in is NULL");
     AMPB_REQUIRE(n == 0 || (x_bf16 != nullptr && q != nullptr), AMP_ERR_INVALID,
                  "x or q is NULL");
-    const int vec = aligned16(x_bf16) && aligned16(q);
-    const int grid = grid_for(vec ? (n >> 4) : n);
-    k_quant_encode<<<grid, kThreads, 0, as_stream(stream)>>>(
-        static_cast<const uint16_t*>(x_bf16), n, nullptr, 0, amax_in, q, scale_out, nullptr, vec);
-    AMPB_CHECK_LAUNCH("k_quant_encode(amax_in)");
-    return AMP_OK;
+    return launch_encode(x_bf16, n, nullptr, 0, amax_in, q, scale_out, nullptr, as_stream(stream));
 }
 
 int amp_fp8_dequant_e4m3_dev(const uint8_t* q, int64_t n, const float* scale, void* y_bf16,
@@ -270,12 +301,7 @@ int amp_fp8_dequant_e4m3_dev(const uint8_t* q, int64_t n, const float* scale, vo
     AMPB_REQUIRE(scale != nullptr, AMP_ERR_INVALID, "scale is NULL");
     if (n == 0) return AMP_OK;
     AMPB_REQUIRE(q != nullptr && y_bf16 != nullptr, AMP_ERR_INVALID, "q or y is NULL");
-    const int vec = aligned16(q) && aligned16(y_bf16);
-    const int grid = grid_for(vec ? (n >> 4) : n);
-    k_dequant<<<grid, kThreads, 0, as_stream(stream)>>>(q, n, scale,
-                                                        static_cast<uint16_t*>(y_bf16), vec);
-    AMPB_CHECK_LAUNCH("k_dequant");
-    return AMP_OK;
+    return launch_dequant(q, n, scale, y_bf16, as_stream(stream));
 }
 
 int amp_user_fp8_quant_e4m3(const uint16_t* x, int64_t n, uint8_t* q, float* scale_out,

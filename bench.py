@@ -16,8 +16,8 @@ Workloads (``--workload``):
   gemm_fp8             same with E4M3 operands, per-row A / per-column B scales.
 
 Timing: W untimed warm-up steps; then K steps, each bracketed by CUDA events on
-the launching stream with a 256 MiB L2 flush before every step (outside the
-events); barrier + synchronize on both sides; the max over ranks.  NVML samples
+the launching stream with an L2 flush before every step (256 MiB written, then
+256 MiB read, outside the events); barrier + synchronize on both sides; the max over ranks.  NVML samples
 SM clocks and throttle reasons during the timed region.  ``e2e`` repeats the
 metric through the host-pointer C entry point (pinned host buffers, H2D +
 kernels + D2H inside the timed region).  ``roofline`` reports the dominant
@@ -209,7 +209,7 @@ class QuantWorkload:
         return {"workload": "fp8_e4m3_per_tensor_quant_dequant", "elements_per_gpu": self.n,
                 "global_elements": self.n * self.dist.world,
                 "input": "bf16 N(0,1) + 0.1% N(0,50) outliers (seeded, synthetic)",
-                "scale": "amax/448, RNE satfinite", "l2": "256 MiB flush before every step",
+                "scale": "amax/448, RNE satfinite", "l2": "L2 flushed before every step (256 MiB written, then 256 MiB read)",
                 "parallelism": f"shard{self.dist.world}+allreduce_max(1 float)"
                 if self.dist.world > 1 else "single"}
 
@@ -329,7 +329,7 @@ class GemmWorkload:
                 "N": self.S, "K": self.S, "out": "bf16",
                 "inputs": "N(0,1)" + (" quantised per row (A) / per column (B), amax/448"
                                       if self.fp8 else ""),
-                "l2": "operands (2 x %d MiB) exceed L2; 256 MiB flush before every step"
+                "l2": "operands (2 x %d MiB) exceed L2; L2 flushed before every step"
                       % (self.S * self.S * (1 if self.fp8 else 2) >> 20),
                 "parallelism": f"N-split over {p} GPUs + NCCL all-gather of C" if p > 1
                 else "single"}
@@ -449,7 +449,7 @@ class AttentionWorkload:
         return {"workload": "flash_attn2_fwd_causal", "batch": self.B, "heads": self.H,
                 "seq_len": self.S, "head_dim": self.D, "dtype": "bf16, fp32 softmax/accumulate",
                 "flop_convention": "4*B*H*D*S*(S+1)/2 (visible pairs)",
-                "l2": "Q/K/V %d MiB each exceed L2; 256 MiB flush before every step"
+                "l2": "Q/K/V %d MiB each exceed L2; L2 flushed before every step"
                       % (self.B * self.H * self.S * self.D * 2 >> 20),
                 "parallelism": f"(batch*head) split over {p} GPUs + NCCL all-gather of O"
                 if p > 1 else "single"}
@@ -550,7 +550,7 @@ class PagedDecodeWorkload:
                 "kv_heads": self.Hkv, "head_dim": self.D, "page_tokens": 16,
                 "context_lens": self.ctx.tolist(), "total_context": int(self.ctx.sum()),
                 "block_table": "seeded random permutation of the pool",
-                "l2": "KV pools exceed L2; 256 MiB flush before every step",
+                "l2": "KV pools exceed L2; L2 flushed before every step",
                 "parallelism": "replicas (each rank its own batch)" if self.dist.world > 1
                 else "single"}
 
@@ -703,9 +703,18 @@ def run_amp(args, dist: Dist):
         ampbuild.build()
     torch.cuda.set_device(dist.local_rank)
     W = WORKLOADS[args.workload](dist, args)
-    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    # L2 flush between steps (outside the timed events): write 256 MiB, then
+    # read a second 256 MiB buffer so that the flush's own dirty lines are
+    # written back before the step starts instead of during it.
+    flush_w = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    flush_r = torch.ones(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def flush():
+        flush_w.zero_()
+        flush_r.sum(dtype=torch.int64)
+
     for _ in range(args.warmup):
-        flush_buf.zero_()
+        flush()
         W.step()
     nk = len(W.kernel_table())
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] for _ in range(args.steps)]
@@ -719,7 +728,7 @@ def run_amp(args, dist: Dist):
     nvml_index = int(phys.split(",")[dev_index]) if phys else dev_index
     with ClockSampler(nvml_index) as clocks:
         for i in range(args.steps):
-            flush_buf.zero_()
+            flush()
             sev[i][0].record()
             W.step(ev[i])
             sev[i][1].record()

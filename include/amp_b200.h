@@ -57,7 +57,8 @@ AMP_API int amp_device_status(int clear);
  * plumbing it would feed is GemmDesc::d_amax_c (include/gemm_vendor.hpp:55-56).
  * Semantics (bit-exact against the oracle):
  *   amax  = max |x| (NaN ignored);  scale = amax/448 (IEEE fp32), 1 if amax==0
- *   q[i]  = E4M3_RNE_satfinite(x[i] / scale)      (IEEE fp32 division)
+ *   inv   = min(RN(1/scale), FLT_MAX)
+ *   q[i]  = E4M3_RNE_satfinite(RN(x[i] * inv))
  *   y[i]  = bf16_RNE(e4m3_to_f32(q[i]) * scale)
  * ---------------------------------------------------------------------- */
 

@@ -54,6 +54,7 @@ def lib() -> C.CDLL:
             "orc_f32_to_e4m3_ampcompat_n": (None, [vp, i64, vp]),
             "orc_amax_bf16": (f32, [vp, i64]),
             "orc_scale_from_amax": (f32, [f32]),
+            "orc_inv_scale": (f32, [f32]),
             "orc_quant_e4m3": (None, [vp, i64, vp, vp, vp]),
             "orc_quant_e4m3_with_amax": (None, [vp, i64, f32, vp]),
             "orc_dequant_e4m3": (None, [vp, i64, f32, vp]),

@@ -127,7 +127,9 @@ ORC_API void orc_f32_to_e4m3_ampcompat_n(const float* x, int64_t n, uint8_t* q) 
 /* src/gemm_vendor.cpp:186-187); the pipeline semantics are:                  */
 /*   amax  = max |x| over the bf16 inputs widened to fp32 (NaN ignored)       */
 /*   scale = amax / 448 (IEEE fp32 division); amax == 0 -> scale = 1          */
-/*   q     = E4M3_RNE_sat(x / scale)   (IEEE fp32 division)                   */
+/*   inv   = min(1 / scale, FLT_MAX)  (IEEE fp32 division, clamped so that    */
+/*           0 * inv stays 0 when scale is tiny)                              */
+/*   q     = E4M3_RNE_sat(x * inv)    (IEEE fp32 multiply)                    */
 /*   y     = bf16_RNE(e4m3_to_f32(q) * scale)                                 */
 /* ------------------------------------------------------------------------- */
 
@@ -144,20 +146,30 @@ ORC_API float orc_scale_from_amax(float amax) {
     return amax == 0.0f ? 1.0f : amax / 448.0f;
 }
 
+#include <float.h>
+ORC_API float orc_inv_scale(float scale) {
+    float inv = 1.0f / scale;
+    return inv > FLT_MAX ? FLT_MAX : inv;   /* NaN stays NaN */
+}
+
+static inline uint8_t quant1(uint16_t xb, float inv) {
+    return orc_f32_to_e4m3_rne(orc_bf16_to_f32(xb) * inv);   /* one rounded multiply */
+}
+
 /* Per-tensor quantise; returns the scale through *scale_out. */
 ORC_API void orc_quant_e4m3(const uint16_t* x, int64_t n, uint8_t* q, float* scale_out,
                             float* amax_out) {
     float amax = orc_amax_bf16(x, n);
-    float s = orc_scale_from_amax(amax);
-    for (int64_t i = 0; i < n; ++i) q[i] = orc_f32_to_e4m3_rne(orc_bf16_to_f32(x[i]) / s);
+    float s = orc_scale_from_amax(amax), inv = orc_inv_scale(s);
+    for (int64_t i = 0; i < n; ++i) q[i] = quant1(x[i], inv);
     if (scale_out) *scale_out = s;
     if (amax_out) *amax_out = amax;
 }
 
 /* Quantise with a given amax (the sharded path: global amax comes from an all-reduce). */
 ORC_API void orc_quant_e4m3_with_amax(const uint16_t* x, int64_t n, float amax, uint8_t* q) {
-    float s = orc_scale_from_amax(amax);
-    for (int64_t i = 0; i < n; ++i) q[i] = orc_f32_to_e4m3_rne(orc_bf16_to_f32(x[i]) / s);
+    float inv = orc_inv_scale(orc_scale_from_amax(amax));
+    for (int64_t i = 0; i < n; ++i) q[i] = quant1(x[i], inv);
 }
 
 ORC_API void orc_dequant_e4m3(const uint8_t* q, int64_t n, float scale, uint16_t* y) {
@@ -169,9 +181,8 @@ ORC_API void orc_quant_e4m3_rows(const uint16_t* x, int64_t rows, int64_t cols, 
                                  float* scales) {
     for (int64_t r = 0; r < rows; ++r) {
         const uint16_t* xr = x + r * cols;
-        float s = orc_scale_from_amax(orc_amax_bf16(xr, cols));
-        for (int64_t c = 0; c < cols; ++c)
-            q[r * cols + c] = orc_f32_to_e4m3_rne(orc_bf16_to_f32(xr[c]) / s);
+        float s = orc_scale_from_amax(orc_amax_bf16(xr, cols)), inv = orc_inv_scale(s);
+        for (int64_t c = 0; c < cols; ++c) q[r * cols + c] = quant1(xr[c], inv);
         scales[r] = s;
     }
 }
@@ -189,7 +200,7 @@ ORC_API void orc_quant_e4m3_cols(const uint16_t* x, int64_t rows, int64_t cols, 
     }
     for (int64_t r = 0; r < rows; ++r)
         for (int64_t c = 0; c < cols; ++c)
-            q[r * cols + c] = orc_f32_to_e4m3_rne(orc_bf16_to_f32(x[r * cols + c]) / scales[c]);
+            q[r * cols + c] = quant1(x[r * cols + c], orc_inv_scale(scales[c]));
 }
 
 /* ------------------------------------------------------------------------- */

@@ -76,8 +76,9 @@ __attribute__((visibility("default"))) float ref_quant_dequant_bf16(const uint16
     float amax = 0.0f;
     for (float m : part) amax = std::max(amax, m);
     const float scale = amax == 0.0f ? 1.0f : amax / 448.0f;
+    const float inv = std::min(1.0f / scale, 3.402823466e38f);
     parallel_for(n, threads, [&](int64_t lo, int64_t hi, int) {
-        for (int64_t i = lo; i < hi; ++i) q[i] = AMP::fp8::f32_to_e4m3(bf16_to_f32(x[i]) / scale);
+        for (int64_t i = lo; i < hi; ++i) q[i] = AMP::fp8::f32_to_e4m3(bf16_to_f32(x[i]) * inv);
         if (y)
             for (int64_t i = lo; i < hi; ++i)
                 y[i] = f32_to_bf16(AMP::fp8::e4m3_to_f32(q[i]) * scale);

@@ -116,3 +116,20 @@ def test_host_pointer_entry_points(cuda, amp_lib):
     y2 = np.empty_like(y)
     call("amp_user_fp8_dequant_e4m3", q.ctypes.data, q.size, s.value, y2.ctypes.data)
     assert same_bf16(y2, y).all()
+
+
+def test_every_bf16_value_over_many_scales(cuda, amp_lib):
+    """Every finite bf16 value against the oracle under scales spread over 40
+    binades (amax injected), including subnormal-range and saturating codes."""
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    finite = (bits & 0x7F80) != 0x7F80
+    bits = bits[finite]
+    x = to_dev_bf16(bits, cuda)
+    rng = np.random.default_rng(77)
+    amaxes = np.concatenate([np.float32(448.0) * np.ldexp(1.0 + rng.random(150), rng.integers(-20, 20, 150)),
+                             rng.uniform(100, 500, 50), [1e-40, 3e38]]).astype(np.float32)
+    for a in amaxes:
+        q, _ = fp8.quantize_e4m3_from_amax(x, torch.tensor([a], device=cuda))
+        want = oracle.quant_e4m3_with_amax(bits, a)
+        got = q.cpu().numpy()
+        assert np.array_equal(got, want), (a, np.count_nonzero(got != want))
