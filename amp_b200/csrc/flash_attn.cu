@@ -19,8 +19,8 @@
 //              shared memory), so QK^T of tile j overlaps softmax of tile j-1.
 //   warps 2-5  softmax, one query row per thread: tcgen05.ld the S row, mask,
 //              online max in the log2 domain (scale * log2(e) folded into one
-//              FFMA), ex2, row sum in fp32, P packed to bf16 and tcgen05.st back
-//              over S.  O is rescaled (tcgen05.ld/st) only when a row maximum
+//              packed f32x2 FMA per two scores), ex2, row sum in fp32 (independent
+//              accumulator chains), P packed to bf16 and tcgen05.st back over S.  O is rescaled (tcgen05.ld/st) only when a row maximum
 //              grows by more than 2^8; otherwise the stale maximum is kept.
 //              Epilogue: O / l to bf16, lse = (m + log2 l) * ln 2.
 #include <cuda.h>
@@ -65,6 +65,31 @@ __device__ __forceinline__ float lg2_approx(float x) {
     float y;
     asm("lg2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes).
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
 }
 
 template <int D>
@@ -275,11 +300,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int e = 0; e < 32; ++e)
                         if (k0 + cch * 32 + e > vis_hi) sr[cch][e] = __float_as_uint(-INFINITY);
             }
-            float mt = -INFINITY;
+            // row max over 8 independent chains (a single chain is a 64-deep
+            // dependency: measured ~4% of the kernel)
+            float mx[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
 #pragma unroll
             for (int cch = 0; cch < BKV / 32; ++cch)
 #pragma unroll
-                for (int e = 0; e < 32; ++e) mt = fmaxf(mt, __uint_as_float(sr[cch][e]));
+                for (int e = 0; e < 32; e += 16)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        mx[i] = fmax3(mx[i], __uint_as_float(sr[cch][e + 2 * i]),
+                                      __uint_as_float(sr[cch][e + 2 * i + 1]));
+            const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]),
+                                   fmaxf(mx[6], mx[7]));
             const float m_new = fmaxf(m_run, mt * c);
             const bool need = (j == 0) || (m_new > m_run + kRescaleThreshold);
             if (__any_sync(0xffffffffu, need)) {
@@ -307,15 +342,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 m_run = m_new;
             }
             const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-            float rs = 0.0f;
+            const uint64_t c2 = f2pack(c, c), nm2 = f2pack(-m_use, -m_use);
+            uint64_t rs4[4];   // row sum in 4 independent packed accumulators
+#pragma unroll
+            for (int i = 0; i < 4; ++i) rs4[i] = f2pack(0.0f, 0.0f);
 #pragma unroll
             for (int cch = 0; cch < BKV / 32; ++cch) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
-                    const float p0 = ex2_approx(fmaf(__uint_as_float(sr[cch][e]), c, -m_use));
-                    const float p1 = ex2_approx(fmaf(__uint_as_float(sr[cch][e + 1]), c, -m_use));
-                    rs += p0 + p1;
+                    float x0, x1;
+                    f2unpack(ffma2(f2pack(__uint_as_float(sr[cch][e]), __uint_as_float(sr[cch][e + 1])),
+                                   c2, nm2),
+                             x0, x1);
+                    const float p0 = ex2_approx(x0);
+                    const float p1 = ex2_approx(x1);
+                    rs4[(e >> 1) & 3] = fadd2(rs4[(e >> 1) & 3], f2pack(p0, p1));
                     pk[e >> 1] = f32x2_to_bf16x2(p0, p1);
                 }
                 // P (bf16 pairs) overwrites the first 64 columns of this S buffer
@@ -323,7 +365,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int e = 0; e < 16; ++e) sr[cch >> 1][(cch & 1) * 16 + e] = pk[e];
                 if (cch & 1) tmem_st_32x32b_x32(lane_base + sb * BKV + (cch >> 1) * 32, sr[cch >> 1]);
             }
-            l_run += rs;
+            float rs_lo, rs_hi;
+            f2unpack(fadd2(fadd2(rs4[0], rs4[1]), fadd2(rs4[2], rs4[3])), rs_lo, rs_hi);
+            l_run += rs_lo + rs_hi;
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
