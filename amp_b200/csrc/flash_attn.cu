@@ -9,19 +9,26 @@
 // flash_attn.cu:134,152) -- generalised here by an offset so that paged
 // prefill can use bottom-right alignment (key j visible iff j <= i + offset).
 //
-// One CTA per (batch*head, 128-row query tile), 192 threads:
-//   warp 0     TMA: Q tile once; K and V tiles (128 rows) into separate
+// One CTA per (batch*head, pair of 128-row query tiles), 384 threads in three
+// warpgroups (setmaxnreg: 72 registers for the first, 216 for the softmax ones):
+//   warp 0     TMA: both Q tiles once; K and V tiles (128 rows) into separate
 //              2-stage rings (128-byte swizzle, 3-D maps so each head's tail is
-//              zero-filled).
-//   warp 1     TMEM (512 columns: S0 | S1 | O) and one MMA-issuing lane:
-//              S_j = Q K_j^T into S[j%2] (SS form, K-major x K-major), then
-//              O += P_{j-1} V_{j-1} (TS form: P read from TMEM, V MN-major from
-//              shared memory), so QK^T of tile j overlaps softmax of tile j-1.
-//   warps 2-5  softmax, one query row per thread: tcgen05.ld the S row, mask,
-//              online max in the log2 domain (scale * log2(e) folded into one
-//              packed f32x2 FMA per two scores), ex2, row sum in fp32 (independent
-//              accumulator chains), P packed to bf16 and tcgen05.st back over S.  O is rescaled (tcgen05.ld/st) only when a row maximum
-//              grows by more than 2^8; otherwise the stale maximum is kept.
+//              zero-filled; 4-D page-gather maps for paged K/V).
+//   warp 1     TMEM (512 columns: S0 | S1 | O0 | O1) and one MMA-issuing lane.
+//              Per K/V tile j and query tile t: O_t += P_t,j V_j (TS form: P
+//              read from TMEM, V MN-major from shared memory), then, once that
+//              MMA has completed (P_t,j lives in S_t), S_t = Q_t K_{j+1}^T (SS
+//              form).  The two tiles' chains S -> softmax -> P -> PV -> S are
+//              offset by half a step, so the tensor core works on one tile
+//              while the other tile's softmax runs.
+//   warps 2-3  idle (they only hand their registers to the softmax warps).
+//   warps 4-7  softmax of query tile 0, warps 8-11 of query tile 1; one query
+//              row per thread: tcgen05.ld the S row, mask, online max in the
+//              log2 domain (scale * log2(e) folded into one packed f32x2 FMA
+//              per two scores), ex2, row sum in fp32 (independent accumulator
+//              chains), P packed to bf16 and tcgen05.st back over S.  O is
+//              rescaled (tcgen05.ld/st) only when a row maximum grows by more
+//              than 2^8; otherwise the stale maximum is kept.
 //              Epilogue: O / l to bf16, lse = (m + log2 l) * ln 2.
 #include <cuda.h>
 
@@ -38,10 +45,14 @@ int fa_make_tmap_pool(CUtensorMap* m, const void* base, int64_t d, int64_t hkv, 
 
 namespace {
 
-constexpr int BQ = 128;            // query rows per CTA
+constexpr int BQ = 128;            // query rows per tile (two tiles per CTA)
 constexpr int BKV = 128;           // key/value rows per tile
 constexpr int KV_STAGES = 2;
-constexpr int kThreads = 192;
+constexpr int kThreads = 384;      // 3 warpgroups
+// Register split between the control warpgroup and the two softmax warpgroups;
+// it must not exceed what the launch holds: 128*72 + 256*216 == 384*168, and the
+// kernel is compiled for exactly 168 registers a thread (__launch_bounds__(384, 1)).
+constexpr int kRegCtl = 72, kRegSoftmax = 216;
 constexpr int SLAB_BYTES = 128 * 128;  // [128 rows x 128 bytes] swizzled slab
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -94,60 +105,60 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 
 template <int D>
 struct FaCfg {
-    static constexpr int SLABS = D / 64;                 // 64 bf16 = 128 bytes per slab
-    static constexpr int Q_BYTES = SLABS * SLAB_BYTES;
-    static constexpr int K_BYTES = SLABS * SLAB_BYTES;
-    static constexpr int V_BYTES = SLABS * SLAB_BYTES;
-    static constexpr int SMEM = Q_BYTES + KV_STAGES * (K_BYTES + V_BYTES) + 1024 + 256;
+    static constexpr int SLABS = D / 64;
+    static constexpr int TILE = SLABS * SLAB_BYTES;
+    static constexpr int SMEM = 2 * TILE + KV_STAGES * 2 * TILE + 1024 + 256;
     static constexpr uint32_t IDESC_QK = make_idesc(1, 1, 0, 0, BQ, BKV);
     static constexpr uint32_t IDESC_PV = make_idesc(1, 1, 0, 1, BQ, D);
-    static constexpr uint32_t O_COL = 2 * BKV;           // S0 | S1 | O
+    static constexpr uint32_t O_COL = 2 * BKV;            // S0 | S1 | O0 | O1
 };
 
 template <int D, bool kPaged>
 __global__ void __launch_bounds__(kThreads, 1)
     k_flash_fwd(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                const __grid_constant__ CUtensorMap tmV, const FaParams p) {
+           const __grid_constant__ CUtensorMap tmV, const FaParams p) {
     using CF = FaCfg<D>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
-    uint8_t* q_s = smem;
-    uint8_t* k_s = q_s + CF::Q_BYTES;                       // [KV_STAGES][K_BYTES]
-    uint8_t* v_s = k_s + KV_STAGES * CF::K_BYTES;           // [KV_STAGES][V_BYTES]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(v_s + KV_STAGES * CF::V_BYTES);
+    uint8_t* q_s = smem;                        // [2][TILE]
+    uint8_t* k_s = q_s + 2 * CF::TILE;          // [KV_STAGES][TILE]
+    uint8_t* v_s = k_s + KV_STAGES * CF::TILE;        // [KV_STAGES][TILE]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(v_s + KV_STAGES * CF::TILE);
     uint64_t* q_full = bars;
     uint64_t* k_full = bars + 1;
     uint64_t* k_empty = k_full + KV_STAGES;
     uint64_t* v_full = k_empty + KV_STAGES;
     uint64_t* v_empty = v_full + KV_STAGES;
-    uint64_t* s_full = v_empty + KV_STAGES;   // [2]
-    uint64_t* p_full = s_full + 2;            // [2]
-    uint64_t* pv_done = p_full + 2;           // [2]
+    uint64_t* s_full = v_empty + KV_STAGES;   // [2] per query tile
+    uint64_t* p_full = s_full + 2;      // [2]
+    uint64_t* pv_done = p_full + 2;     // [2]
     uint64_t* drain = pv_done + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_qt = (p.S_q + BQ - 1) / BQ;
-    const int qt = n_qt - 1 - (int)blockIdx.x;   // heaviest causal tiles first
+    const int n_qb = (p.S_q + 2 * BQ - 1) / (2 * BQ);
+    const int qb = n_qb - 1 - (int)blockIdx.x;
     const int bh = blockIdx.y;
     const int b = bh / p.Hq, h = bh % p.Hq;
     const int bh_kv = b * p.Hkv + h / (p.Hq / p.Hkv);
-    const int q0 = qt * BQ;
-    // Paged prefill: the queries are the last S_q tokens of each sequence's
-    // context, causal with bottom-right alignment.
+    const int q0 = qb * 2 * BQ;
     int S_kv = p.S_kv, coff = p.causal_offset;
     if constexpr (kPaged) {
         S_kv = max(0, p.ctx_lens[b]);
         coff = S_kv - p.S_q;
     }
-    int n_kv = (S_kv + BKV - 1) / BKV;
-    if (p.causal) {
-        const int last = q0 + BQ - 1 + coff;   // largest visible key of the tile
-        const int lim = last < 0 ? 0 : last / BKV + 1;
-        n_kv = min(n_kv, lim);
-    }
-    if (n_kv < 1) n_kv = 1;   // fully masked rows still produce O = 0, lse = -inf
+    const int n_all = (S_kv + BKV - 1) / BKV;
+    auto nblk = [&](int row0) {
+        int n = n_all;
+        if (p.causal) {
+            const int last = row0 + BQ - 1 + coff;
+            n = min(n, last < 0 ? 0 : last / BKV + 1);
+        }
+        return max(n, 1);
+    };
+    const int n0 = nblk(q0);
+    const int n1 = max(nblk(q0 + BQ), n0);
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -175,25 +186,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegCtl));
     if (warp == 0) {
         if (lane == 0) {
             tma_prefetch_desc(&tmQ);
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
-            mbar_arrive_expect_tx(q_full, CF::Q_BYTES);
+            mbar_arrive_expect_tx(q_full, 2 * CF::TILE);
 #pragma unroll
-            for (int sl = 0; sl < CF::SLABS; ++sl)
-                tma_load_3d(q_s + sl * SLAB_BYTES, &tmQ, q_full, sl * 64, q0, bh);
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+                for (int sl = 0; sl < CF::SLABS; ++sl)
+                    tma_load_3d(q_s + t * CF::TILE + sl * SLAB_BYTES, &tmQ, q_full, sl * 64,
+                                q0 + t * BQ, bh);
             const int last_page = max(0, (S_kv + kPageTokens - 1) / kPageTokens - 1);
             const int hk = h / (p.Hq / p.Hkv);
-            for (int j = 0; j < n_kv; ++j) {
+            for (int j = 0; j < n1; ++j) {
                 const int s = j % KV_STAGES;
                 const uint32_t ph = (j / KV_STAGES) & 1;
                 int pages[BKV / kPageTokens];
                 if constexpr (kPaged) {
-                    // 8 pages per tile; slots past the context repeat the last page
-                    // (masked in the softmax), ids outside the pool read page 0 and
-                    // raise the bad-page flag.
                     const int* bt = p.block_table + (int64_t)b * p.max_pages;
 #pragma unroll
                     for (int i = 0; i < BKV / kPageTokens; ++i) {
@@ -204,10 +217,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 if (!mbar_wait(&k_empty[s], ph ^ 1, p.status)) break;
-                mbar_arrive_expect_tx(&k_full[s], CF::K_BYTES);
+                mbar_arrive_expect_tx(&k_full[s], CF::TILE);
 #pragma unroll
                 for (int sl = 0; sl < CF::SLABS; ++sl) {
-                    uint8_t* dst = k_s + s * CF::K_BYTES + sl * SLAB_BYTES;
+                    uint8_t* dst = k_s + s * CF::TILE + sl * SLAB_BYTES;
                     if constexpr (kPaged) {
 #pragma unroll
                         for (int i = 0; i < BKV / kPageTokens; ++i)
@@ -218,10 +231,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 if (!mbar_wait(&v_empty[s], ph ^ 1, p.status)) break;
-                mbar_arrive_expect_tx(&v_full[s], CF::V_BYTES);
+                mbar_arrive_expect_tx(&v_full[s], CF::TILE);
 #pragma unroll
                 for (int sl = 0; sl < CF::SLABS; ++sl) {
-                    uint8_t* dst = v_s + s * CF::V_BYTES + sl * SLAB_BYTES;
+                    uint8_t* dst = v_s + s * CF::TILE + sl * SLAB_BYTES;
                     if constexpr (kPaged) {
 #pragma unroll
                         for (int i = 0; i < BKV / kPageTokens; ++i)
@@ -235,64 +248,89 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            bool ok = mbar_wait(q_full, 0, p.status);
             const uint32_t q_addr = smem_u32(q_s);
-            for (int j = 0; ok && j <= n_kv; ++j) {
-                if (j < n_kv) {   // S_j = Q K_j^T
-                    const int sb = j & 1;
-                    if (j >= 2 && !mbar_wait(&pv_done[sb], ((j - 2) >> 1) & 1, p.status)) break;
-                    if (!mbar_wait(&k_full[j % KV_STAGES], (j / KV_STAGES) & 1, p.status)) break;
-                    tc_fence_after();
-                    const uint32_t k_addr = smem_u32(k_s + (j % KV_STAGES) * CF::K_BYTES);
+            // S_t = Q_t K^T (K-major x K-major, 16-deep steps along the head dim)
+            auto qk = [&](int t, uint32_t k_addr) {
+                const uint32_t qa = q_addr + t * CF::TILE;
 #pragma unroll
-                    for (int kk = 0; kk < D / 16; ++kk) {
-                        const uint32_t off = (kk >> 2) * SLAB_BYTES + (kk & 3) * 32;
-                        tc_mma_f16(tmem + sb * BKV, smem_desc_sw128(q_addr + off, 16, 1024),
-                                   smem_desc_sw128(k_addr + off, 16, 1024), CF::IDESC_QK, kk != 0);
-                    }
-                    tc_commit(&k_empty[j % KV_STAGES]);
-                    tc_commit(&s_full[sb]);
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * SLAB_BYTES + (kk & 3) * 32;
+                    tc_mma_f16(tmem + t * BKV, smem_desc_sw128(qa + off, 16, 1024),
+                               smem_desc_sw128(k_addr + off, 16, 1024), CF::IDESC_QK, kk != 0);
                 }
-                if (j >= 1) {     // O += P_i V_i
-                    const int i = j - 1, pb = i & 1;
-                    if (!mbar_wait(&p_full[pb], (i >> 1) & 1, p.status)) break;
-                    if (!mbar_wait(&v_full[i % KV_STAGES], (i / KV_STAGES) & 1, p.status)) break;
+            };
+            bool ok = mbar_wait(q_full, 0, p.status) && mbar_wait(&k_full[0], 0, p.status);
+            if (ok) {
+                tc_fence_after();
+                const uint32_t k_addr = smem_u32(k_s);
+                qk(0, k_addr);
+                tc_commit(&s_full[0]);
+                qk(1, k_addr);
+                tc_commit(&s_full[1]);
+                tc_commit(&k_empty[0]);
+            }
+            for (int j = 0; ok && j < n1; ++j) {
+                const int s = j % KV_STAGES, s1 = (j + 1) % KV_STAGES;
+                if (!mbar_wait(&v_full[s], (j / KV_STAGES) & 1, p.status)) break;
+                const uint32_t v_addr = smem_u32(v_s + s * CF::TILE);
+                const uint32_t k1_addr = smem_u32(k_s + s1 * CF::TILE);
+                bool k1_ready = false;
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                    const int nt = t ? n1 : n0;
+                    if (j >= nt) continue;
+                    if (!mbar_wait(&p_full[t], j & 1, p.status)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t v_addr = smem_u32(v_s + (i % KV_STAGES) * CF::V_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < BKV / 16; ++kk)
-                        tc_mma_f16_ts(tmem + CF::O_COL, tmem + pb * BKV + kk * 8,
+                        tc_mma_f16_ts(tmem + CF::O_COL + t * D, tmem + t * BKV + kk * 8,
                                       smem_desc_sw128(v_addr + kk * 16 * 128, SLAB_BYTES, 1024),
-                                      CF::IDESC_PV, (i | kk) != 0);
-                    tc_commit(&v_empty[i % KV_STAGES]);
-                    tc_commit(&pv_done[pb]);
+                                      CF::IDESC_PV, (j | kk) != 0);
+                    tc_commit(&pv_done[t]);
+                    if (t == 1) tc_commit(&v_empty[s]);
+                    if (j + 1 < nt) {
+                        if (!k1_ready) {
+                            if (!mbar_wait(&k_full[s1], ((j + 1) / KV_STAGES) & 1, p.status)) { ok = false; break; }
+                            tc_fence_after();
+                            k1_ready = true;
+                        }
+                        // P_t,j sits in S_t: PV_t,j must have read it before S_t is rewritten
+                        if (!mbar_wait(&pv_done[t], j & 1, p.status)) { ok = false; break; }
+                        tc_fence_after();
+                        qk(t, k1_addr);
+                        tc_commit(&s_full[t]);
+                        if (t == 1) tc_commit(&k_empty[s1]);
+                    }
                 }
             }
             tc_commit(drain);
             mbar_wait(drain, 0, p.status);
         }
+    }
     } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegSoftmax));
         // ---------------------------------------------------------- softmax
+        const int t = (warp - 4) >> 2;
         const int quad = warp & 3;
-        const int r = quad * 32 + lane;              // row within the tile == TMEM lane
-        const int qi = q0 + r;                       // query index
+        const int r = quad * 32 + lane;
+        const int qi = q0 + t * BQ + r;
+        const int nt = t ? n1 : n0;
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+        const uint32_t s_col = t * BKV, o_col = CF::O_COL + t * D;
         const float c = p.scale_log2;
+        const int vis_hi = p.causal ? min(S_kv - 1, qi + coff) : S_kv - 1;
         float m_run = -INFINITY, l_run = 0.0f;
         bool ok = true;
-        for (int j = 0; j < n_kv; ++j) {
-            const int sb = j & 1;
-            if (!mbar_wait_warp(&s_full[sb], (j >> 1) & 1, p.status)) { ok = false; break; }
+        for (int j = 0; j < nt; ++j) {
+            if (!mbar_wait_warp(&s_full[t], j & 1, p.status)) { ok = false; break; }
             tc_fence_after();
             uint32_t sr[BKV / 32][32];
             __syncwarp();
 #pragma unroll
             for (int cch = 0; cch < BKV / 32; ++cch)
-                tmem_ld_32x32b_x32(lane_base + sb * BKV + cch * 32, sr[cch]);
+                tmem_ld_32x32b_x32(lane_base + s_col + cch * 32, sr[cch]);
             tmem_ld_wait();
-            // mask: keys past the end, and (causal) keys after the query
             const int k0 = j * BKV;
-            const int vis_hi = p.causal ? min(S_kv - 1, qi + coff) : S_kv - 1;
             if (k0 + BKV - 1 > vis_hi) {
 #pragma unroll
                 for (int cch = 0; cch < BKV / 32; ++cch)
@@ -300,8 +338,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int e = 0; e < 32; ++e)
                         if (k0 + cch * 32 + e > vis_hi) sr[cch][e] = __float_as_uint(-INFINITY);
             }
-            // row max over 8 independent chains (a single chain is a 64-deep
-            // dependency: measured ~4% of the kernel)
             float mx[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
@@ -320,22 +356,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (__any_sync(0xffffffffu, need)) {
                 const float alpha = (m_run == -INFINITY) ? 0.0f : ex2_approx(m_run - m_new);
                 if (j > 0) {
-                    // PV_{j-1} must have landed in O before O is rescaled
-                    if (!mbar_wait_warp(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status)) {
-                        ok = false;
-                        break;
-                    }
+                    if (!mbar_wait_warp(&pv_done[t], (j - 1) & 1, p.status)) { ok = false; break; }
                     tc_fence_after();
                     __syncwarp();
 #pragma unroll
                     for (int oc = 0; oc < D / 32; ++oc) {
                         uint32_t o[32];
-                        tmem_ld_32x32b_x32(lane_base + CF::O_COL + oc * 32, o);
+                        tmem_ld_32x32b_x32(lane_base + o_col + oc * 32, o);
                         tmem_ld_wait();
 #pragma unroll
                         for (int e = 0; e < 32; ++e)
                             o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                        tmem_st_32x32b_x32(lane_base + CF::O_COL + oc * 32, o);
+                        tmem_st_32x32b_x32(lane_base + o_col + oc * 32, o);
                     }
                 }
                 l_run *= alpha;
@@ -343,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
             const uint64_t c2 = f2pack(c, c), nm2 = f2pack(-m_use, -m_use);
-            uint64_t rs4[4];   // row sum in 4 independent packed accumulators
+            uint64_t rs4[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) rs4[i] = f2pack(0.0f, 0.0f);
 #pragma unroll
@@ -351,19 +383,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t pk[16];
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
+                    const uint64_t x2 = ffma2(f2pack(__uint_as_float(sr[cch][e]), __uint_as_float(sr[cch][e + 1])), c2, nm2);
                     float x0, x1;
-                    f2unpack(ffma2(f2pack(__uint_as_float(sr[cch][e]), __uint_as_float(sr[cch][e + 1])),
-                                   c2, nm2),
-                             x0, x1);
-                    const float p0 = ex2_approx(x0);
-                    const float p1 = ex2_approx(x1);
-                    rs4[(e >> 1) & 3] = fadd2(rs4[(e >> 1) & 3], f2pack(p0, p1));
+                    f2unpack(x2, x0, x1);
+                    const uint64_t p2 = f2pack(ex2_approx(x0), ex2_approx(x1));
+                    rs4[(e >> 1) & 3] = fadd2(rs4[(e >> 1) & 3], p2);
+                    float p0, p1;
+                    f2unpack(p2, p0, p1);
                     pk[e >> 1] = f32x2_to_bf16x2(p0, p1);
                 }
-                // P (bf16 pairs) overwrites the first 64 columns of this S buffer
 #pragma unroll
                 for (int e = 0; e < 16; ++e) sr[cch >> 1][(cch & 1) * 16 + e] = pk[e];
-                if (cch & 1) tmem_st_32x32b_x32(lane_base + sb * BKV + (cch >> 1) * 32, sr[cch >> 1]);
+                if (cch & 1) tmem_st_32x32b_x32(lane_base + s_col + (cch >> 1) * 32, sr[cch >> 1]);
             }
             float rs_lo, rs_hi;
             f2unpack(fadd2(fadd2(rs4[0], rs4[1]), fadd2(rs4[2], rs4[3])), rs_lo, rs_hi);
@@ -371,10 +402,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[sb]);
+            if (lane == 0) mbar_arrive(&p_full[t]);
         }
-        // ---------------------------------------------------------- epilogue
-        if (ok && mbar_wait_warp(&pv_done[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, p.status)) {
+        if (ok && mbar_wait_warp(&pv_done[t], (nt - 1) & 1, p.status)) {
             tc_fence_after();
             const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
             const bool row_ok = qi < p.S_q;
@@ -384,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int oc = 0; oc < D / 32; ++oc) {
                 uint32_t o[32];
-                tmem_ld_32x32b_x32(lane_base + CF::O_COL + oc * 32, o);
+                tmem_ld_32x32b_x32(lane_base + o_col + oc * 32, o);
                 tmem_ld_wait();
                 if (row_ok) {
 #pragma unroll
@@ -453,7 +483,7 @@ int launch_fa(const void* Q, const void* K, const void* V, void* O, float* lse, 
     auto kern = k_flash_fwd<D, kPaged>;
     AMPB_CHECK_CUDA(
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FaCfg<D>::SMEM));
-    dim3 grid((S_q + BQ - 1) / BQ, B * Hq);
+    dim3 grid((S_q + 2 * BQ - 1) / (2 * BQ), B * Hq);
     kern<<<grid, kThreads, FaCfg<D>::SMEM, st>>>(tq, tk, tv, p);
     AMPB_CHECK_LAUNCH("k_flash_fwd");
     return AMP_OK;
