@@ -15,15 +15,27 @@
 //   ctx_lens        int32 [B]
 //   q, out          [B][Hq][D] bf16 (one new token per sequence); lse [B][Hq]
 //
-// Decode is HBM-bound (4 KiB of K+V per context token for Hkv = 8, D = 128),
-// so it runs on the CUDA cores with split-KV: one CTA per (chunk of 32 pages,
-// kv head, sequence); each of its 4 warps takes every 4th page -- lane pair
-// (2t, 2t+1) holds token t of the page, each lane half of D, so the 4 KiB
-// page row is read fully coalesced -- and keeps an online softmax for the
-// GQA group's query heads that share the kv head.  Warps merge in shared
-// memory, chunks merge in k_paged_combine through their log-sum-exp.
-// A page id outside [0, num_pages) is skipped and flagged in the device
-// status word (AMP_DEV_ERR_BAD_PAGE); it never becomes a memory access.
+// Decode is HBM-bound (4 KiB of K+V per context token for Hkv = 8, D = 128).
+// One CTA per (chunk of 32 pages, kv head, sequence), 160 threads:
+//   warp 4     producer: TMA (4-D page-gather map, 128-byte swizzle) of each
+//              page's K and V blocks (2 x 4 KiB) into an 8-stage shared-memory
+//              ring, so 64 KiB per CTA are in flight ahead of the math.
+//   warps 0-3  consumers; warp w takes pages w, w+4, ... of the chunk.  Per
+//              page, on the tensor cores (mma.sync m16n8k16, bf16 -> fp32):
+//              S^T[16 tokens x 8 heads] = K Q^T (K by ldmatrix, Q held in
+//              registers as B fragments; the GQA group's G <= 8 query heads
+//              fill the 8 columns), online softmax per head down the token
+//              rows (quad shuffles), P^T turned into B fragments by movmatrix,
+//              O^T[128 x 8] += V^T P^T (V by ldmatrix.trans).
+//   Warps merge in shared memory; chunks merge in k_paged_combine through
+//   their log-sum-exp.
+// A page id outside [0, num_pages) is never loaded: it is flagged in the device
+// status word (AMP_DEV_ERR_BAD_PAGE) and its tokens are treated as masked.
+// Slots past the context in the last page may hold anything: their scores are
+// masked and their V rows zeroed in shared memory before the PV product.
+#include <cuda.h>
+
+#include <atomic>
 #include <cmath>
 #include <vector>
 
@@ -32,16 +44,22 @@
 #include "tc_common.cuh"
 
 namespace ampb {
+
+int fa_make_tmap_pool(CUtensorMap* m, const void* base, int64_t d, int64_t hkv, int64_t pages);
+
 namespace {
 
 constexpr int kPage = 16;
 constexpr int kChunkPages = 32;     // 512 tokens per split
-constexpr int kWarps = 4;
+constexpr int kCWarps = 4;          // consumer warps
+constexpr int kThreads = (kCWarps + 1) * 32;
+constexpr int kStages = 8;
+constexpr int kSlab = kPage * 128;           // 16 rows x 128 B (64 bf16 of D), swizzled
+constexpr int kStageBytes = 4 * kSlab;       // K d0-63 | K d64-127 | V d0-63 | V d64-127
+constexpr int kDecodeSmem = kStages * kStageBytes + 1024 + 256;
 
 struct DecodeParams {
     const __nv_bfloat16* q;
-    const __nv_bfloat16* k_pool;
-    const __nv_bfloat16* v_pool;
     const int* block_table;
     const int* ctx_lens;
     float* part_o;     // [B][Hq][max_chunks][D]
@@ -53,133 +71,232 @@ struct DecodeParams {
     int* status;
 };
 
-__device__ __forceinline__ void bf16x8_to_f32(uint4 w, float* f) {
-    f[0] = bf16_lo(w.x); f[1] = bf16_hi(w.x); f[2] = bf16_lo(w.y); f[3] = bf16_hi(w.y);
-    f[4] = bf16_lo(w.z); f[5] = bf16_hi(w.z); f[6] = bf16_lo(w.w); f[7] = bf16_hi(w.w);
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// byte offset of (row, 16-byte chunk) in a [rows x 128 B] slab written by TMA with
+// the 128-byte swizzle
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+    return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-template <int D, int G>
-__global__ void __launch_bounds__(kWarps * 32) k_paged_decode(const DecodeParams p) {
-    static_assert(D == 128, "decode kernel is written for head_dim 128");
-    constexpr int HALF = D / 2;                 // elements of D per lane in the QK stage
-    constexpr int DPL = D / 32;                 // elements of D per lane in the PV stage
+template <int G>
+__global__ void __launch_bounds__(kThreads) k_paged_decode(const __grid_constant__ CUtensorMap tmK,
+                                                           const __grid_constant__ CUtensorMap tmV,
+                                                           const DecodeParams p) {
+    static_assert(G >= 1 && G <= 8, "one n8 tile holds the GQA group");
+    constexpr int D = 128;
     const int chunk = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ctx = p.ctx_lens[b];
     const int n_pages = (ctx + kPage - 1) / kPage;
     const int pg0 = chunk * kChunkPages;
     if (pg0 >= n_pages || ctx <= 0) return;     // the combine kernel knows the chunk count
-    const int pg1 = min(n_pages, pg0 + kChunkPages);
+    const int np = min(n_pages - pg0, kChunkPages);
 
-    __shared__ float q_s[G][D];
-    __shared__ float m_s[kWarps][G], l_s[kWarps][G];
-    __shared__ float o_s[kWarps][G][D];
-    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-        const int g = i / D, d = i % D;
-        q_s[g][d] = __bfloat162float(p.q[((int64_t)b * p.Hq + hk * G + g) * D + d]);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    int* page_ok = reinterpret_cast<int*>(empty + kStages);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        fence_barrier_init();
     }
     __syncthreads();
 
-    const int t = lane >> 1, half = lane & 1;
-    float m[G], l[G], o[G][DPL];
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
+    float o[8][4];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        m[g] = -INFINITY;
-        l[g] = 0.0f;
+    for (int mt = 0; mt < 8; ++mt)
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) o[g][j] = 0.0f;
-    }
-    const int* bt = p.block_table + (int64_t)b * p.max_pages;
-    for (int pi = pg0 + warp; pi < pg1; pi += kWarps) {
-        const int page = bt[pi];
-        if (page < 0 || page >= p.num_pages) {
-            if (lane == 0) atomicExch(p.status, AMP_DEV_ERR_BAD_PAGE);
-            continue;
+        for (int j = 0; j < 4; ++j) o[mt][j] = 0.0f;
+
+    if (warp == kCWarps) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+            const int* bt = p.block_table + (int64_t)b * p.max_pages;
+            int k = 0;
+            for (; k < np; ++k) {
+                const int s = k % kStages;
+                if (!mbar_wait(&empty[s], ((k / kStages) & 1) ^ 1, p.status)) break;
+                const int page = bt[pg0 + k];
+                const bool ok = page >= 0 && page < p.num_pages;
+                page_ok[s] = ok;
+                if (ok) {
+                    uint8_t* st = ring + s * kStageBytes;
+                    mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    tma_load_4d(st, &tmK, &full[s], 0, 0, hk, page);
+                    tma_load_4d(st + kSlab, &tmK, &full[s], 64, 0, hk, page);
+                    tma_load_4d(st + 2 * kSlab, &tmV, &full[s], 0, 0, hk, page);
+                    tma_load_4d(st + 3 * kSlab, &tmV, &full[s], 64, 0, hk, page);
+                } else {
+                    atomicExch(p.status, AMP_DEV_ERR_BAD_PAGE);
+                    mbar_arrive(&full[s]);
+                }
+            }
+            // every copy issued lands before the shared memory is reused or released
+            for (int kk = max(0, k - kStages); kk < k; ++kk)
+                mbar_wait(&full[kk % kStages], (kk / kStages) & 1, p.status);
         }
-        const int64_t base = ((int64_t)page * p.Hkv + hk) * kPage * D;
-        // K: lane pair (2t, 2t+1) reads token t's row, one half each (8 x 16 B)
-        const uint4* kp = reinterpret_cast<const uint4*>(p.k_pool + base + t * D + half * HALF);
-        uint4 kw[HALF / 8];
+    } else {
+        // ------------------------------------------------------------ consumers
+        // Q^T as B fragments: lane holds head n = lane/4 at d = 16kk + 2(lane%4) (+8)
+        const int n = lane >> 2, kq = 2 * (lane & 3);
+        uint32_t qb[8][2];
+        {
+            const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+                p.q + ((int64_t)b * p.Hq + hk * G + (n < G ? n : 0)) * D);
 #pragma unroll
-        for (int i = 0; i < HALF / 8; ++i) kw[i] = ldg_stream_v4(kp + i);
-        // V: lane reads DPL consecutive elements of every token row (8 B each)
-        const uint2* vp = reinterpret_cast<const uint2*>(p.v_pool + base + lane * DPL);
-        uint2 vw[kPage];
-#pragma unroll
-        for (int tt = 0; tt < kPage; ++tt) vw[tt] = *(vp + tt * (D / DPL));
-        float s[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) s[g] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < HALF / 8; ++i) {
-            float kf[8];
-            bf16x8_to_f32(kw[i], kf);
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-#pragma unroll
-                for (int g = 0; g < G; ++g) s[g] = fmaf(q_s[g][half * HALF + i * 8 + e], kf[e], s[g]);
-        }
-        const bool tok_ok = pi * kPage + t < ctx;
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            s[g] += __shfl_xor_sync(0xffffffffu, s[g], 1);
-            s[g] = tok_ok ? s[g] * p.scale_log2 : -INFINITY;
-            float mt = s[g];
-#pragma unroll
-            for (int off = 2; off < 32; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
-            const float m_new = fmaxf(m[g], mt);              // finite: token 0 of a page is valid
-            const float alpha = ex2_approx(m[g] - m_new);     // 0 when m[g] = -inf
-            const float pr = ex2_approx(s[g] - m_new);
-            float ps = half ? 0.0f : pr;                      // count each token once
-#pragma unroll
-            for (int off = 1; off < 32; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-            l[g] = l[g] * alpha + ps;
-            m[g] = m_new;
-#pragma unroll
-            for (int j = 0; j < DPL; ++j) o[g][j] *= alpha;
-            s[g] = pr;
-        }
-        // slots past the context in the last page may hold anything: zero their V
-        const int valid_tok = ctx - pi * kPage;
-#pragma unroll
-        for (int tt = 0; tt < kPage; ++tt)
-            if (tt >= valid_tok) vw[tt] = make_uint2(0u, 0u);
-#pragma unroll
-        for (int tt = 0; tt < kPage; ++tt) {
-            const float v0 = bf16_lo(vw[tt].x), v1 = bf16_hi(vw[tt].x);
-            const float v2 = bf16_lo(vw[tt].y), v3 = bf16_hi(vw[tt].y);
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float pt = __shfl_sync(0xffffffffu, s[g], 2 * tt);
-                o[g][0] = fmaf(pt, v0, o[g][0]);
-                o[g][1] = fmaf(pt, v1, o[g][1]);
-                o[g][2] = fmaf(pt, v2, o[g][2]);
-                o[g][3] = fmaf(pt, v3, o[g][3]);
+            for (int kk = 0; kk < 8; ++kk) {
+                qb[kk][0] = n < G ? qrow[(16 * kk + kq) >> 1] : 0u;
+                qb[kk][1] = n < G ? qrow[(16 * kk + 8 + kq) >> 1] : 0u;
             }
         }
-    }
-    // merge the 4 warps of this chunk
+        const float c = p.scale_log2;
+        const int r = lane >> 2;              // token row of this lane's C elements (and r + 8)
+        const int mi = lane >> 3, r8 = lane & 7;   // ldmatrix: matrix / row this lane addresses
+        for (int k = warp; k < np; k += kCWarps) {
+            const int s = k % kStages;
+            if (!mbar_wait_warp(&full[s], (k / kStages) & 1, p.status)) break;
+            const int vt = page_ok[s] ? min(kPage, ctx - (pg0 + k) * kPage) : 0;
+            uint8_t* st = ring + s * kStageBytes;
+            if (vt > 0) {
+                if (vt < kPage) {
+                    // zero V rows of the slots past the context (whole 128-byte rows,
+                    // so the swizzle does not matter)
+                    for (int i = lane; i < (kPage - vt) * 2 * 8; i += 32) {
+                        const int row = vt + (i >> 4), sl = (i >> 3) & 1, ch = i & 7;
+                        *reinterpret_cast<uint4*>(st + (2 + sl) * kSlab + row * 128 + ch * 16) =
+                            make_uint4(0u, 0u, 0u, 0u);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                }
+                // S^T = K Q^T: 8 k-steps of 16 along D
+                float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                const uint32_t kbase = smem_u32(st);
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        if (lane == 0) {
-            m_s[warp][g] = m[g];
-            l_s[warp][g] = l[g];
+                for (int kk = 0; kk < 8; ++kk) {
+                    const int row = r8 + 8 * (mi & 1);
+                    const int chunk16 = 2 * (kk & 3) + (mi >> 1);
+                    uint32_t a[4];
+                    ldsm_x4(kbase + (kk >> 2) * kSlab + swz(row, chunk16), a);
+                    mma16816(sc, a, qb[kk][0], qb[kk][1]);
+                }
+                // online softmax per head (column) down the 16 token rows
+                float x[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int tok = r + 8 * (j >> 1);
+                    x[j] = tok < vt ? sc[j] * c : -INFINITY;
+                }
+                float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
+#pragma unroll
+                for (int off = 4; off < 32; off <<= 1) {
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+                }
+                const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);   // finite: token 0 valid
+                const float al0 = ex2_approx(m[0] - mn0), al1 = ex2_approx(m[1] - mn1);
+                const float p0 = ex2_approx(x[0] - mn0), p1 = ex2_approx(x[1] - mn1);
+                const float p2 = ex2_approx(x[2] - mn0), p3 = ex2_approx(x[3] - mn1);
+                float rs0 = p0 + p2, rs1 = p1 + p3;
+#pragma unroll
+                for (int off = 4; off < 32; off <<= 1) {
+                    rs0 += __shfl_xor_sync(0xffffffffu, rs0, off);
+                    rs1 += __shfl_xor_sync(0xffffffffu, rs1, off);
+                }
+                l[0] = l[0] * al0 + rs0;
+                l[1] = l[1] * al1 + rs1;
+                m[0] = mn0;
+                m[1] = mn1;
+                if (__any_sync(0xffffffffu, al0 != 1.0f || al1 != 1.0f)) {
+#pragma unroll
+                    for (int mt = 0; mt < 8; ++mt) {
+                        o[mt][0] *= al0;
+                        o[mt][1] *= al1;
+                        o[mt][2] *= al0;
+                        o[mt][3] *= al1;
+                    }
+                }
+                // P^T as B fragments (tokens x heads), via an in-register transpose
+                const uint32_t b01 = movm_t(f32x2_to_bf16x2(p0, p1));
+                const uint32_t b23 = movm_t(f32x2_to_bf16x2(p2, p3));
+                // O^T[d][head] += V^T P^T: 8 m-tiles of 16 along D
+                const uint32_t vbase = kbase + 2 * kSlab;
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    const int tok = r8 + 8 * (mi >> 1);
+                    const int dch = 2 * mt + (mi & 1);          // 16-byte chunk along D
+                    uint32_t a[4];
+                    ldsm_x4_t(vbase + (dch >> 3) * kSlab + swz(tok, dch & 7), a);
+                    mma16816(o[mt], a, b01, b23);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
         }
+    }
+
+    // merge the consumer warps (the ring is free: every copy has landed)
+    __syncthreads();
+    float* o_s = reinterpret_cast<float*>(ring);     // [kCWarps][8][D]
+    float* m_s = o_s + kCWarps * 8 * D;              // [kCWarps][8]
+    float* l_s = m_s + kCWarps * 8;                  // [kCWarps][8]
+    if (warp < kCWarps) {
+        const int h0 = 2 * (lane & 3), r = lane >> 2;
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) o_s[warp][g][lane * DPL + j] = o[g][j];
+        for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                o_s[(warp * 8 + h0 + (j & 1)) * D + 16 * mt + r + 8 * (j >> 1)] = o[mt][j];
+        if (r == 0) {
+            m_s[warp * 8 + h0] = m[0];
+            m_s[warp * 8 + h0 + 1] = m[1];
+            l_s[warp * 8 + h0] = l[0];
+            l_s[warp * 8 + h0 + 1] = l[1];
+        }
     }
     __syncthreads();
     for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
         const int g = i / D, d = i % D;
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, m_s[w][g]);
+        for (int w = 0; w < kCWarps; ++w) M = fmaxf(M, m_s[w * 8 + g]);
         float L = 0.0f, O = 0.0f;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-            const float a = (m_s[w][g] == -INFINITY) ? 0.0f : ex2_approx(m_s[w][g] - M);
-            L += a * l_s[w][g];
-            O += a * o_s[w][g][d];
+        for (int w = 0; w < kCWarps; ++w) {
+            const float mw = m_s[w * 8 + g];
+            const float a = (mw == -INFINITY) ? 0.0f : ex2_approx(mw - M);
+            L += a * l_s[w * 8 + g];
+            O += a * o_s[(w * 8 + g) * D + d];
         }
         const int64_t row = ((int64_t)b * p.Hq + hk * G + g) * p.max_chunks + chunk;
         p.part_o[row * D + d] = O;
@@ -243,11 +360,12 @@ int paged_decode_dev(const void* q, const void* k_pool, const void* v_pool, cons
     int* status = nullptr;
     int rc = device_status(&status);
     if (rc) return rc;
+    CUtensorMap tmK, tmV;
+    if ((rc = fa_make_tmap_pool(&tmK, k_pool, D, Hkv, num_pages))) return rc;
+    if ((rc = fa_make_tmap_pool(&tmV, v_pool, D, Hkv, num_pages))) return rc;
     if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)D);
     DecodeParams p;
     p.q = static_cast<const __nv_bfloat16*>(q);
-    p.k_pool = static_cast<const __nv_bfloat16*>(k_pool);
-    p.v_pool = static_cast<const __nv_bfloat16*>(v_pool);
     p.block_table = block_table;
     p.ctx_lens = ctx_lens;
     p.max_chunks = ((max_ctx + kPage - 1) / kPage + kChunkPages - 1) / kChunkPages;
@@ -263,15 +381,29 @@ int paged_decode_dev(const void* q, const void* k_pool, const void* v_pool, cons
     p.scale_log2 = scale * 1.4426950408889634f;
     p.status = status;
     dim3 grid(p.max_chunks, Hkv, B);
+    auto go = [&](auto kern, std::atomic<uint32_t>& attr_set) {
+        int dev = 0;
+        AMPB_CHECK_CUDA(cudaGetDevice(&dev));
+        const uint32_t bit = 1u << (dev & 31);
+        if (!(attr_set.load() & bit)) {
+            AMPB_CHECK_CUDA(cudaFuncSetAttribute(
+                kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecodeSmem));
+            attr_set.fetch_or(bit);
+        }
+        kern<<<grid, kThreads, kDecodeSmem, st>>>(tmK, tmV, p);
+        return AMP_OK;
+    };
+    static std::atomic<uint32_t> attr1{0}, attr2{0}, attr4{0}, attr8{0};
     switch (Hq / Hkv) {
-        case 1: k_paged_decode<128, 1><<<grid, kWarps * 32, 0, st>>>(p); break;
-        case 2: k_paged_decode<128, 2><<<grid, kWarps * 32, 0, st>>>(p); break;
-        case 4: k_paged_decode<128, 4><<<grid, kWarps * 32, 0, st>>>(p); break;
-        case 8: k_paged_decode<128, 8><<<grid, kWarps * 32, 0, st>>>(p); break;
+        case 1: rc = go(k_paged_decode<1>, attr1); break;
+        case 2: rc = go(k_paged_decode<2>, attr2); break;
+        case 4: rc = go(k_paged_decode<4>, attr4); break;
+        case 8: rc = go(k_paged_decode<8>, attr8); break;
         default:
             set_error(AMP_ERR_UNSUPPORTED, "GQA group size %d not supported (1, 2, 4, 8)", Hq / Hkv);
             return AMP_ERR_UNSUPPORTED;
     }
+    if (rc) return rc;
     AMPB_CHECK_LAUNCH("k_paged_decode");
     k_paged_combine<128><<<B * Hq, 128, 0, st>>>(p);
     AMPB_CHECK_LAUNCH("k_paged_combine");

@@ -54,25 +54,46 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
         : "memory");
 }
 
+// kSleep: the waiting thread is suspended by the hardware until the phase
+// completes or the hint (ns) passes, so it takes no issue slots from the warps
+// that work on the same SM sub-partition -- at the cost of a slower wake-up, so
+// it suits waits off the critical path (GEMM producer/epilogue) and not the
+// tight softmax <-> MMA hand-offs of attention.
+constexpr uint32_t kWaitHintNs = 1000000u;
+
+template <bool kSleep = false>
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
+    if constexpr (kSleep) {
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;"
+            " selp.u32 %0, 1, 0, p; }"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitHintNs)
+            : "memory");
+    } else {
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;"
+            " selp.u32 %0, 1, 0, p; }"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+    }
     return ok != 0;
 }
 
 // Bounded wait for the phase with the given parity to complete.  Returns
 // false (and records a timeout in *status) if it does not within the limit.
+template <bool kSleep = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait<kSleep>(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     uint32_t n = 0;
+    // a sleeping try_wait may take up to the hint, so the clock is read every time
+    constexpr uint32_t kCheckMask = kSleep ? 0u : 1023u;
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((++n & 1023u) == 0) {
+        if (mbar_try_wait<kSleep>(bar, parity)) return true;
+        if ((++n & kCheckMask) == 0) {
             if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
                 atomicExch(status, AMP_DEV_ERR_TIMEOUT);
                 return false;
@@ -86,8 +107,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
 // Warp-uniform form for warps that go on to warp-collective tcgen05.ld/st:
 // every lane waits (each needs the acquire), then the warp agrees, so a lane
 // that gave up never leaves the others stuck at a collective.
+template <bool kSleep = false>
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status) {
-    const bool ok = mbar_wait(bar, parity, status);
+    const bool ok = mbar_wait<kSleep>(bar, parity, status);
     return __all_sync(0xffffffffu, ok);
 }
 
