@@ -34,6 +34,9 @@ def decode_ref(q, ctx, bt, kp, vp, heads=None):
     O = np.full((B, Hq, D), np.nan)
     L = np.full((B, Hq), np.nan)
     for b in range(B):
+        if ctx[b] == 0:                 # no keys: O = 0, lse = -inf
+            O[b], L[b] = 0.0, -np.inf
+            continue
         k = ref.paged_gather(kp, bt[b], int(ctx[b]))[None]     # [1, Hkv, ctx, D]
         v = ref.paged_gather(vp, bt[b], int(ctx[b]))[None]
         o, lse = ref.flash_attn_fwd(q[b][None, :, None, :], k, v, causal=False)
@@ -69,6 +72,48 @@ def test_decode_full_workload(cuda, amp_lib):
     O, L = decode_ref(q, ctx, bt, kp, vp)
     assert oracle.max_rel_err(out, O) < TOL_O
     assert np.abs(lse - L).max() < TOL_LSE
+
+
+def test_decode_many_short_sequences(cuda, amp_lib):
+    # slices of the page list cross many sequence boundaries; some contexts are empty
+    rng = np.random.default_rng(21)
+    ctx = rng.integers(0, 70, size=96).astype(np.int32)
+    ctx[[3, 40, 41]] = 0
+    ctx, bt, npg, kp, vp = workloads.paged_inputs(seed=22, B=96, Hq=8, Hkv=2, ctx_lens=ctx)
+    q = bf16_np(rng.standard_normal((96, 8, 128), dtype=np.float32))
+    out, lse = run_decode(q, ctx, bt, kp, vp)
+    assert lib().amp_device_status(1) == 0
+    O, L = decode_ref(q, ctx, bt, kp, vp)
+    assert oracle.max_rel_err(out, O) < TOL_O
+    fin = np.isfinite(L)
+    assert (np.isinf(lse) == ~fin).all() and np.abs(lse[fin] - L[fin]).max() < TOL_LSE
+
+
+def test_decode_large_batch_uses_prefix_kernel(cuda, amp_lib):
+    # above 1024 sequences the page prefix sums come from a separate kernel
+    rng = np.random.default_rng(23)
+    ctx = rng.integers(1, 40, size=1100).astype(np.int32)
+    ctx, bt, npg, kp, vp = workloads.paged_inputs(seed=24, B=1100, Hq=4, Hkv=1, ctx_lens=ctx)
+    q = bf16_np(rng.standard_normal((1100, 4, 128), dtype=np.float32))
+    out, lse = run_decode(q, ctx, bt, kp, vp)
+    assert lib().amp_device_status(1) == 0
+    O, L = decode_ref(q, ctx, bt, kp, vp)
+    assert oracle.max_rel_err(out, O) < TOL_O
+    assert np.abs(lse - L).max() < TOL_LSE
+
+
+def test_decode_context_past_max_context_len_is_flagged(cuda, amp_lib):
+    ctx = np.array([100, 50], np.int32)
+    ctx, bt, npg, kp, vp = workloads.paged_inputs(seed=25, B=2, Hq=8, Hkv=2, ctx_lens=ctx)
+    q = bf16_np(np.random.default_rng(26).standard_normal((2, 8, 128), dtype=np.float32))
+    k_pool, v_pool, btd, ctxd = to_dev(ctx, bt, kp, vp)
+    out, _ = paged.paged_attn_decode(torch.from_numpy(q).to(torch.bfloat16).cuda(), k_pool,
+                                     v_pool, btd, ctxd, 64)
+    torch.cuda.synchronize()
+    assert lib().amp_device_status(1) == -1   # sequence 0 is longer than the declared 64
+    assert lib().amp_device_status(1) == 0
+    O, _ = decode_ref(q[1:], ctx[1:], bt[1:], kp, vp)
+    assert oracle.max_rel_err(out.float().cpu().numpy()[1:], O) < TOL_O
 
 
 def test_decode_garbage_past_context_is_ignored(cuda, amp_lib):
