@@ -22,6 +22,8 @@ SIGNATURES: dict[str, tuple] = {
     "amp_fp8_quant_workspace_bytes": (_sz, [_i64]),
     "amp_fp8_quant_e4m3_dev": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "amp_fp8_amax_bf16_dev": (_i32, [_vp, _i64, _vp, _vp, _sz, _vp]),
+    "amp_fp8_amax_allreduce_peer_dev": (_i32, [_vp, _i64, _vp, _vp, _sz, _vp, _i32, _i32,
+                                               C.c_uint, _vp]),
     "amp_fp8_quant_e4m3_from_amax_dev": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp]),
     "amp_fp8_dequant_e4m3_dev": (_i32, [_vp, _i64, _vp, _vp, _vp]),
     "amp_fp8_quant_e4m3_noalloc_dev": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp]),
@@ -45,6 +47,13 @@ SIGNATURES: dict[str, tuple] = {
     "amp_gemm_fp32_dev": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "amp_gemm_fp32_tile_dev": (_i32, [_i32, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "amp_user_gemm_fp32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32]),
+    "amp_peer_mailbox_bytes": (_sz, []),
+    "amp_peer_handle_bytes": (_i32, []),
+    "amp_peer_mailbox_create": (_i32, [_vp, _vp]),
+    "amp_peer_mailbox_open": (_i32, [_vp, _vp]),
+    "amp_peer_mailbox_close": (_i32, [_vp]),
+    "amp_peer_mailbox_free": (_i32, [_vp]),
+    "amp_peer_allreduce_max_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, C.c_uint, _vp]),
 }
 
 

@@ -10,6 +10,7 @@ functions are backend-agnostic (gloo on CPU runs them in tests).
 """
 from __future__ import annotations
 
+import ctypes as C
 from dataclasses import dataclass
 
 import torch
@@ -109,3 +110,51 @@ def gather_heads(g: CommGroup, o_shard: torch.Tensor) -> torch.Tensor:
 def global_amax(g: CommGroup, local_amax: torch.Tensor) -> torch.Tensor:
     """1-float all-reduce(MAX): the per-tensor amax of a tensor sharded over ranks."""
     return allreduce(g, local_amax, "max")
+
+
+class PeerMailboxes:
+    """Each rank's small device mailbox, opened by every other rank of the node
+    through CUDA IPC, so one-word exchanges (the quantiser's amax) travel as a
+    single NVLink store per peer instead of an NCCL all-reduce.
+
+    Collective: every rank of `g` constructs it, and closes it, at the same point.
+    `table` is the device array of mailbox pointers the kernels take."""
+
+    def __init__(self, g: CommGroup):
+        from ._lib import call, lib
+        self.g, self.seq = g, 0
+        n = int(lib().amp_peer_handle_bytes())
+        handle = (C.c_ubyte * n)()
+        own = C.c_void_p()
+        call("amp_peer_mailbox_create", C.byref(own), handle)
+        self.own = own.value
+        handles = [None] * g.world
+        dist.all_gather_object(handles, bytes(handle), group=g.group)
+        ptrs, self._opened = [], []
+        for r, hb in enumerate(handles):
+            if r == g.rank:
+                ptrs.append(self.own)
+                continue
+            p = C.c_void_p()
+            call("amp_peer_mailbox_open", (C.c_ubyte * n).from_buffer_copy(hb), C.byref(p))
+            ptrs.append(p.value)
+            self._opened.append(p.value)
+        self.table = torch.tensor(ptrs, dtype=torch.int64,
+                                  device=torch.device("cuda", torch.cuda.current_device()))
+
+    def next_seq(self) -> int:
+        """Sequence number of the next exchange (1, 2, ...; the same on every rank)."""
+        self.seq = self.seq % 0xFFFFFFFF + 1
+        return self.seq
+
+    def close(self) -> None:
+        from ._lib import call
+        if self.own is None:
+            return
+        torch.cuda.synchronize()
+        barrier(self.g)                 # nobody posts any more
+        for p in self._opened:
+            call("amp_peer_mailbox_close", p)
+        barrier(self.g)                 # every peer has unmapped this rank's mailbox
+        call("amp_peer_mailbox_free", self.own)
+        self.own, self._opened = None, []

@@ -21,6 +21,7 @@
 // Algorithmic bytes: quantise 5 B/element (2 amax read + 2 read + 1 write),
 // dequantise 3 B/element (1 read + 2 write).
 #include "common.cuh"
+#include "peer.cuh"
 #include "runtime.h"
 
 #include <mutex>
@@ -193,6 +194,26 @@ inline int grid_for(int64_t work_items) {
     return (int)(want < cap ? want : cap);
 }
 
+// Sharded amax: fold this rank's partials, swap the result with every other
+// rank through the peer mailboxes (one 64-bit store per peer over NVLink) and
+// write the max over ranks -- the all-reduce(max) of one float without NCCL.
+__global__ void __launch_bounds__(kThreads) k_amax_fold_exchange(
+    const float* __restrict__ parts, int nparts, float* amax_out,
+    unsigned long long* const* mbox, int rank, int world, unsigned seq, int* status) {
+    __shared__ unsigned got[kMaxPeers];
+    float m = 0.0f;
+    for (int i = threadIdx.x; i < nparts; i += kThreads) m = fmaxf(m, parts[i]);
+    m = block_max(m);
+    if (threadIdx.x < 32) {
+        mailbox_exchange(mbox, rank, world, seq, __float_as_uint(m), got, status);
+        __syncwarp();
+        float g = m;
+        for (int p = threadIdx.x; p < world; p += 32) g = fmaxf(g, __uint_as_float(got[p]));
+        g = warp_max(g);
+        if (threadIdx.x == 0) *amax_out = g;
+    }
+}
+
 int launch_amax(const void* x, int64_t n, float* parts, int* nparts_out, cudaStream_t st) {
     const int vec = aligned16(x);
     const int grid = grid_for(vec ? (n >> 3) : n);
@@ -283,6 +304,31 @@ int amp_fp8_amax_bf16_dev(const void* x_bf16, int64_t n, float* amax_out, void* 
     k_quant_encode<<<1, kThreads, 0, st>>>(nullptr, 0, parts, nparts, nullptr, nullptr, nullptr,
                                            amax_out, 0);
     AMPB_CHECK_LAUNCH("k_quant_encode(fold)");
+    return AMP_OK;
+}
+
+int amp_fp8_amax_allreduce_peer_dev(const void* x_bf16, int64_t n, float* amax_out,
+                                    void* workspace, size_t workspace_bytes,
+                                    void* const* mailboxes, int rank, int world, unsigned seq,
+                                    void* stream) {
+    AMPB_REQUIRE(n >= 0, AMP_ERR_INVALID, "n must be >= 0 (got %lld)", (long long)n);
+    AMPB_REQUIRE(amax_out != nullptr && mailboxes != nullptr, AMP_ERR_INVALID, "NULL argument");
+    AMPB_REQUIRE(n == 0 || x_bf16 != nullptr, AMP_ERR_INVALID, "x is NULL");
+    AMPB_REQUIRE(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world, AMP_ERR_INVALID,
+                 "rank %d / world %d outside [0, %d)", rank, world, kMaxPeers);
+    AMPB_REQUIRE(seq != 0, AMP_ERR_INVALID, "sequence numbers start at 1");
+    int rc = check_ws(workspace, workspace_bytes);
+    if (rc) return rc;
+    int* status = nullptr;
+    if ((rc = device_status(&status))) return rc;
+    cudaStream_t st = as_stream(stream);
+    float* parts = static_cast<float*>(workspace);
+    int nparts = 0;
+    if (n > 0 && (rc = launch_amax(x_bf16, n, parts, &nparts, st))) return rc;
+    k_amax_fold_exchange<<<1, kThreads, 0, st>>>(
+        parts, nparts, amax_out, reinterpret_cast<unsigned long long* const*>(mailboxes), rank,
+        world, seq, status);
+    AMPB_CHECK_LAUNCH("k_amax_fold_exchange");
     return AMP_OK;
 }
 

@@ -59,6 +59,21 @@ def amax_bf16(x: torch.Tensor, workspace: torch.Tensor | None = None,
     return a
 
 
+def amax_allreduce_peer(x: torch.Tensor, mailboxes, workspace: torch.Tensor | None = None,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    """max |x| over the shards of every rank: this rank's amax swapped with the
+    others through `mailboxes` (a collective.PeerMailboxes); no NCCL call."""
+    _check_bf16(x)
+    dev = x.device
+    a = out if out is not None else torch.empty(1, dtype=torch.float32, device=dev)
+    ws_b = workspace_bytes(x.numel())
+    ws = workspace if workspace is not None else torch.empty(ws_b, dtype=torch.uint8, device=dev)
+    call("amp_fp8_amax_allreduce_peer_dev", x.data_ptr(), x.numel(), a.data_ptr(), ws.data_ptr(),
+         ws.numel(), mailboxes.table.data_ptr(), mailboxes.g.rank, mailboxes.g.world,
+         mailboxes.next_seq(), _stream(dev))
+    return a
+
+
 def quantize_e4m3_from_amax(x: torch.Tensor, amax: torch.Tensor,
                             out: torch.Tensor | None = None,
                             scale: torch.Tensor | None = None):

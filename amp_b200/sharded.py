@@ -15,10 +15,16 @@ from . import attention, fp8, gemm
 from .collective import CommGroup, gather_columns, gather_heads, global_amax, head_range
 
 
-def quantize_e4m3_sharded(x_shard: torch.Tensor, g: CommGroup | None = None):
+def quantize_e4m3_sharded(x_shard: torch.Tensor, g: CommGroup | None = None, mailboxes=None):
+    """Per-tensor FP8 quantisation of a tensor sharded over ranks: the global amax
+    comes from the peer mailboxes when given (NVLink stores), else from a 1-float
+    NCCL/gloo all-reduce."""
     g = g or CommGroup.current()
-    amax = fp8.amax_bf16(x_shard)
-    global_amax(g, amax)
+    if mailboxes is not None:
+        amax = fp8.amax_allreduce_peer(x_shard, mailboxes)
+    else:
+        amax = fp8.amax_bf16(x_shard)
+        global_amax(g, amax)
     return fp8.quantize_e4m3_from_amax(x_shard, amax)
 
 

@@ -77,6 +77,19 @@ AMP_API int amp_fp8_quant_e4m3_dev(const void* x_bf16, int64_t n, uint8_t* q, fl
 AMP_API int amp_fp8_amax_bf16_dev(const void* x_bf16, int64_t n, float* amax_out, void* workspace,
                           size_t workspace_bytes, void* stream);
 
+/* Sharded amax without NCCL: amax of this rank's n values, exchanged with every
+ * rank of the node through the peer mailboxes below, max over ranks into
+ * *amax_out (device float).  Replaces the all-reduce(MAX) of one float that
+ * AMP's collective layer would do (include/collective.hpp:79-85, allreduce).
+ * `mailboxes` is a DEVICE array of `world` mailbox pointers (own at [rank]);
+ * every rank calls with the same seq, which starts at 1 and grows by one per
+ * call.  A peer that does not post within 2 s sets AMP_ERR_TIMEOUT in
+ * amp_device_status(). */
+AMP_API int amp_fp8_amax_allreduce_peer_dev(const void* x_bf16, int64_t n, float* amax_out,
+                                            void* workspace, size_t workspace_bytes,
+                                            void* const* mailboxes, int rank, int world,
+                                            unsigned seq, void* stream);
+
 /* Second half: quantise with a given device-resident amax. */
 AMP_API int amp_fp8_quant_e4m3_from_amax_dev(const void* x_bf16, int64_t n, const float* amax_in,
                                      uint8_t* q, float* scale_out, void* stream);
@@ -199,6 +212,24 @@ AMP_API int amp_user_gemm_bf16(const uint16_t* A, const uint16_t* B, void* C, in
 AMP_API int amp_user_gemm_fp8e4m3(const uint8_t* A, const uint8_t* B, const float* scale_a,
                                   const float* scale_b, int scale_mode, void* C, int c_dtype,
                                   int M, int N, int K);
+
+/* ----------------------------------------------------------------------
+ * Peer mailboxes: small device buffers that the other processes of the node
+ * write into directly (CUDA IPC over NVLink), for one-word exchanges whose
+ * NCCL launch cost would dominate (see amp_fp8_amax_allreduce_peer_dev).
+ * A handle is amp_peer_handle_bytes() opaque bytes, shared by the caller
+ * (e.g. an all-gather over the process group); peers open it with
+ * amp_peer_mailbox_open.  Close peers' mailboxes before their owners free them.
+ * ---------------------------------------------------------------------- */
+AMP_API size_t amp_peer_mailbox_bytes(void);
+AMP_API int amp_peer_handle_bytes(void);
+AMP_API int amp_peer_mailbox_create(void** mailbox, void* handle_out);
+AMP_API int amp_peer_mailbox_open(const void* handle, void** mailbox);
+AMP_API int amp_peer_mailbox_close(void* mailbox);
+AMP_API int amp_peer_mailbox_free(void* mailbox);
+/* all-reduce(max) of one float per rank through the mailboxes (device in/out). */
+AMP_API int amp_peer_allreduce_max_f32(const float* in, float* out, void* const* mailboxes,
+                                       int rank, int world, unsigned seq, void* stream);
 
 #ifdef __cplusplus
 }

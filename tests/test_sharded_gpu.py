@@ -40,6 +40,27 @@ def _rank_main(rank, world, port, q):
         q_shard, s_shard = sharded.quantize_e4m3_sharded(x_full[rank * n:(rank + 1) * n])
         q_ref, s_ref = fp8.quantize_e4m3(x_full)
         assert torch.equal(q_shard, q_ref[rank * n:(rank + 1) * n]) and s_shard.item() == s_ref.item()
+        # the same through the peer mailboxes (NVLink stores instead of NCCL); several
+        # calls so both parity rows of the mailboxes are used and reused
+        from amp_b200._lib import call, lib
+        from amp_b200.collective import CommGroup, PeerMailboxes
+        mb = PeerMailboxes(CommGroup.current())
+        try:
+            for _ in range(5):
+                q_p, s_p = sharded.quantize_e4m3_sharded(x_full[rank * n:(rank + 1) * n],
+                                                         mailboxes=mb)
+                assert torch.equal(q_p, q_ref[rank * n:(rank + 1) * n])
+                assert s_p.item() == s_ref.item()
+            v = torch.tensor([rank + 1.5], dtype=torch.float32, device=dev)
+            m = torch.empty(1, dtype=torch.float32, device=dev)
+            for _ in range(3):
+                call("amp_peer_allreduce_max_f32", v.data_ptr(), m.data_ptr(),
+                     mb.table.data_ptr(), rank, world, mb.next_seq(), None)
+                torch.cuda.synchronize()
+                assert m.item() == world + 0.5
+            assert lib().amp_device_status(1) == 0
+        finally:
+            mb.close()
         # N-split GEMM + gather
         g = torch.Generator(device=dev).manual_seed(5)
         A = torch.randn(512, 256, generator=g, device=dev).to(torch.bfloat16)
