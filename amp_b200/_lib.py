@@ -32,6 +32,8 @@ SIGNATURES: dict[str, tuple] = {
     "amp_device_status": (_i32, [_i32]),
     "amp_gemm_bf16_dev": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp]),
     "amp_gemm_fp8e4m3_dev": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _vp]),
+    "amp_gemm_fp8e4m3_ex_dev": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _vp, _i32, _i32,
+                                       _i32, _vp]),
     "amp_user_gemm_bf16": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32]),
     "amp_user_gemm_fp8e4m3": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32]),
     "amp_flash_attn_fwd_bf16_dev": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,

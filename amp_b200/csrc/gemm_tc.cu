@@ -7,7 +7,9 @@
 //
 // Layout is AMP's: A [M,K] row-major (K-major operand), B [K,N] row-major
 // (N-major operand, consumed as an MN-major UMMA operand, no transpose), C
-// [M,N] row-major in fp32 or bf16.
+// [M,N] row-major in fp32 or bf16 -- and, for FP8 inputs, E4M3 with a caller
+// scale and/or the amax of C computed in the epilogue (what AMP's GemmDesc
+// carries as d_scale_c / d_amax_c for cuBLASLt, include/gemm_vendor.hpp:55-56).
 //
 // Kernel structure (persistent, one 128x256 output tile per iteration, one
 // CTA per SM, 192 threads):
@@ -26,6 +28,7 @@
 // CTAs running at the same time share A rows and B columns in L2.
 #include <cuda.h>
 
+#include <cfloat>
 #include <mutex>
 
 #include "common.cuh"
@@ -56,6 +59,8 @@ struct TcParams {
     const float* scale_a;   // per-tensor: [1]; row/col: [M]
     const float* scale_b;   // per-tensor: [1]; row/col: [N]
     int scale_mode;
+    const float* scale_c;   // E4M3 output: dequantisation scale of C (device float)
+    float* amax;            // optional: max |C| before output conversion (device float)
     int* status;
 };
 
@@ -180,6 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         const int quad = warp & 3;             // TMEM lanes [32*quad, 32*quad + 32)
         const int row_in_tile = quad * 32 + lane;
+        float amx = 0.0f;                      // this thread's max |C| (NaN ignored)
         int i = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
             const int acc = i & 1;
@@ -190,6 +196,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int row = tm * BM + row_in_tile;
             const bool row_ok = row < p.M;
+            float inv_c = 1.0f;
+            if constexpr (sizeof(OutT) == 1) {   // E4M3 out: the quantiser's RN(1/scale)
+                inv_c = __frcp_rn(p.scale_c[0]);
+                inv_c = inv_c > FLT_MAX ? FLT_MAX : inv_c;
+            }
             float sa = 1.0f;
             if (p.scale_mode == kTensorScale) sa = p.scale_a[0] * p.scale_b[0];
             else if (p.scale_mode == kRowColScale && row_ok) sa = p.scale_a[row];
@@ -214,17 +225,41 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 32; ++j) v[j] *= __shfl_sync(0xffffffffu, sbv, j);
                 }
                 if (!row_ok) continue;
+                if (p.amax) {
+                    const int nv = p.N - col0;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < nv) amx = fmaxf(amx, fabsf(v[j]));
+                }
                 OutT* out = static_cast<OutT*>(p.C) + (int64_t)row * p.N + col0;
                 const bool full_chunk = col0 + 32 <= p.N &&
                                         ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
-                if constexpr (sizeof(OutT) == 4) {
+                if constexpr (sizeof(OutT) == 1) {
+                    uint32_t w8[8];
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        w8[j >> 2] = f32x2_to_e4m3x2(__fmul_rn(v[j], inv_c), __fmul_rn(v[j + 1], inv_c)) |
+                                     (f32x2_to_e4m3x2(__fmul_rn(v[j + 2], inv_c),
+                                                      __fmul_rn(v[j + 3], inv_c)) << 16);
+                    if (full_chunk) {
+                        reinterpret_cast<uint4*>(out)[0] = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+                        reinterpret_cast<uint4*>(out)[1] = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+                    } else {
+                        uint8_t* o8 = reinterpret_cast<uint8_t*>(out);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)   // constant indices: w8 stays in registers
+                            if (col0 + j < p.N) o8[j] = (uint8_t)(w8[j >> 2] >> (8 * (j & 3)));
+                    }
+                } else if constexpr (sizeof(OutT) == 4) {
                     if (full_chunk) {
 #pragma unroll
                         for (int j = 0; j < 32; j += 4)
                             *reinterpret_cast<float4*>(out + j) =
                                 make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
                     } else {
-                        for (int j = 0; j < 32 && col0 + j < p.N; ++j) out[j] = v[j];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)   // constant indices: v stays in registers
+                            if (col0 + j < p.N) out[j] = v[j];
                     }
                 } else {
                     if (full_chunk) {
@@ -239,11 +274,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     } else {
                         uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
-                        for (int j = 0; j < 32 && col0 + j < p.N; ++j)
-                            o16[j] = (uint16_t)(f32x2_to_bf16x2(v[j], 0.0f) & 0xffffu);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.N)
+                                o16[j] = (uint16_t)(f32x2_to_bf16x2(v[j], 0.0f) & 0xffffu);
                     }
                 }
             }
+        }
+        if (p.amax) {   // non-negative floats order like their bit patterns
+            const float m = warp_max(amx);
+            if (lane == 0) atomicMax(reinterpret_cast<unsigned*>(p.amax), __float_as_uint(m));
         }
     }
 
@@ -302,7 +343,8 @@ int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int 
 
 template <bool kFP8, typename OutT>
 int launch_tc(const void* A, const void* B, void* C, int M, int N, int K, const float* sa,
-              const float* sb, int mode, cudaStream_t st) {
+              const float* sb, int mode, cudaStream_t st, const float* sc = nullptr,
+              float* amax = nullptr) {
     const int es = kFP8 ? 1 : 2;
     AMPB_REQUIRE(M > 0 && N > 0 && K > 0, AMP_ERR_INVALID, "GEMM sizes must be positive");
     AMPB_REQUIRE(A && B && C, AMP_ERR_INVALID, "NULL operand");
@@ -328,7 +370,10 @@ int launch_tc(const void* A, const void* B, void* C, int M, int N, int K, const 
     p.scale_a = sa;
     p.scale_b = sb;
     p.scale_mode = mode;
+    p.scale_c = sc;
+    p.amax = amax;
     p.status = status;
+    if (amax) AMPB_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st));
     auto kern = k_gemm_tc<kFP8, OutT>;
     static uint64_t attr_done = 0;  // one bit per device ordinal (< 64)
     int dev = 0;
@@ -355,13 +400,24 @@ int gemm_bf16_dev(const void* A, const void* B, void* C, int c_is_bf16, int M, i
 }
 
 int gemm_fp8_dev(const void* A, const void* B, const float* sa, const float* sb, int mode,
-                 void* C, int c_is_bf16, int M, int N, int K, cudaStream_t st) {
+                 void* C, int c_dtype, int M, int N, int K, cudaStream_t st,
+                 const float* scale_c = nullptr, float* amax_c = nullptr) {
     AMPB_REQUIRE(mode == kTensorScale || mode == kRowColScale, AMP_ERR_INVALID,
                  "FP8 scale mode must be 1 (per tensor) or 2 (per row of A / column of B)");
     AMPB_REQUIRE(sa && sb, AMP_ERR_INVALID, "FP8 GEMM needs both scale pointers");
-    if (c_is_bf16)
-        return launch_tc<true, __nv_bfloat16>(A, B, C, M, N, K, sa, sb, mode, st);
-    return launch_tc<true, float>(A, B, C, M, N, K, sa, sb, mode, st);
+    switch (c_dtype) {
+        case AMP_DTYPE_F32:
+            return launch_tc<true, float>(A, B, C, M, N, K, sa, sb, mode, st, nullptr, amax_c);
+        case AMP_DTYPE_BF16:
+            return launch_tc<true, __nv_bfloat16>(A, B, C, M, N, K, sa, sb, mode, st, nullptr,
+                                                  amax_c);
+        case AMP_DTYPE_E4M3:
+            AMPB_REQUIRE(scale_c, AMP_ERR_INVALID, "E4M3 output needs scale_c");
+            return launch_tc<true, uint8_t>(A, B, C, M, N, K, sa, sb, mode, st, scale_c, amax_c);
+        default:
+            set_error(AMP_ERR_INVALID, "C dtype must be AMP_DTYPE_F32, _BF16 or _E4M3");
+            return AMP_ERR_INVALID;
+    }
 }
 
 }  // namespace ampb
@@ -382,8 +438,16 @@ int amp_gemm_fp8e4m3_dev(const uint8_t* A, const uint8_t* B, const float* scale_
                          int K, void* stream) {
     AMPB_REQUIRE(c_dtype == AMP_DTYPE_F32 || c_dtype == AMP_DTYPE_BF16, AMP_ERR_INVALID,
                  "C dtype must be AMP_DTYPE_F32 or AMP_DTYPE_BF16");
-    return gemm_fp8_dev(A, B, scale_a, scale_b, scale_mode, C, c_dtype == AMP_DTYPE_BF16, M, N, K,
+    return gemm_fp8_dev(A, B, scale_a, scale_b, scale_mode, C, c_dtype, M, N, K,
                         as_stream(stream));
+}
+
+int amp_gemm_fp8e4m3_ex_dev(const uint8_t* A, const uint8_t* B, const float* scale_a,
+                            const float* scale_b, int scale_mode, void* C, int c_dtype,
+                            const float* scale_c, float* amax_c, int M, int N, int K,
+                            void* stream) {
+    return gemm_fp8_dev(A, B, scale_a, scale_b, scale_mode, C, c_dtype, M, N, K,
+                        as_stream(stream), scale_c, amax_c);
 }
 
 // Host-pointer forms (the plugin convention of amp_plugin.h): A, B, C in host
@@ -432,8 +496,7 @@ int amp_user_gemm_fp8e4m3(const uint8_t* A, const uint8_t* B, const float* scale
     AMPB_CHECK_CUDA(cudaMemcpyAsync(dB, B, b, cudaMemcpyHostToDevice, st));
     AMPB_CHECK_CUDA(cudaMemcpyAsync(dsa, scale_a, ns_a * 4, cudaMemcpyHostToDevice, st));
     AMPB_CHECK_CUDA(cudaMemcpyAsync(dsb, scale_b, ns_b * 4, cudaMemcpyHostToDevice, st));
-    if ((rc = gemm_fp8_dev(dA, dB, dsa, dsb, scale_mode, dC, c_dtype == AMP_DTYPE_BF16, M, N, K,
-                           st)))
+    if ((rc = gemm_fp8_dev(dA, dB, dsa, dsb, scale_mode, dC, c_dtype, M, N, K, st)))
         return rc;
     AMPB_CHECK_CUDA(cudaMemcpyAsync(C, dC, c, cudaMemcpyDeviceToHost, st));
     AMPB_CHECK_CUDA(cudaStreamSynchronize(st));

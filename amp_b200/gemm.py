@@ -106,3 +106,38 @@ def launch_matmul_fp8e4m3(dA: torch.Tensor, dB: torch.Tensor, dC: torch.Tensor,
         mode = 1
     call("amp_gemm_fp8e4m3_dev", dA.data_ptr(), dB.data_ptr(), sa.data_ptr(), sb.data_ptr(), mode,
          dC.data_ptr(), AMP_DTYPE[dC.dtype], M, N, K, _stream(dA))
+
+
+def launch_matmul_fp8e4m3_ex(dA: torch.Tensor, dB: torch.Tensor, dC: torch.Tensor,
+                             M: int, N: int, K: int, scale_a, scale_b, scale_c=None,
+                             amax_c: torch.Tensor | None = None) -> None:
+    """FP8 GEMM with output-side quantisation (AMP's GemmDesc d_scale_c / d_amax_c).
+
+    dC float32 / bfloat16: C = v;  uint8 / float8_e4m3fn: E4M3 codes of v / scale_c
+    (the quantiser's encode).  amax_c, a float32[1] device tensor, receives max |v|.
+    v = scale_a * scale_b * (A8 @ B8); scales as in launch_matmul_fp8e4m3."""
+    for t, shape, nm in ((dA, (M, K), "A"), (dB, (K, N), "B")):
+        if t.dtype not in (torch.uint8, torch.float8_e4m3fn):
+            raise ValueError(f"{nm}: expected E4M3 codes (uint8 / float8_e4m3fn)")
+        _check(t, t.dtype, shape, nm)
+    if dC.dtype in (torch.uint8, torch.float8_e4m3fn):
+        c_dtype = 2
+        if scale_c is None:
+            raise ValueError("an E4M3 C needs scale_c")
+    elif dC.dtype in AMP_DTYPE:
+        c_dtype = AMP_DTYPE[dC.dtype]
+    else:
+        raise ValueError("C must be float32, bfloat16 or E4M3 codes")
+    _check(dC, dC.dtype, (M, N), "C")
+    rowcol = isinstance(scale_a, torch.Tensor) and scale_a.numel() == M and M != 1 or \
+        isinstance(scale_b, torch.Tensor) and scale_b.numel() == N and N != 1
+    n_a, n_b, mode = (M, N, 2) if rowcol else (1, 1, 1)
+    sa = _scale_tensor(scale_a, n_a, dA.device, "scale_a")
+    sb = _scale_tensor(scale_b, n_b, dA.device, "scale_b")
+    sc = _scale_tensor(scale_c, 1, dA.device, "scale_c") if scale_c is not None else None
+    if amax_c is not None and (amax_c.dtype != torch.float32 or amax_c.numel() < 1
+                               or not amax_c.is_cuda):
+        raise ValueError("amax_c must be a float32 CUDA tensor")
+    call("amp_gemm_fp8e4m3_ex_dev", dA.data_ptr(), dB.data_ptr(), sa.data_ptr(), sb.data_ptr(),
+         mode, dC.data_ptr(), c_dtype, sc.data_ptr() if sc is not None else None,
+         amax_c.data_ptr() if amax_c is not None else None, M, N, K, _stream(dA))

@@ -39,6 +39,7 @@ extern "C" {
 /* Element types named in signatures that take a dtype selector. */
 #define AMP_DTYPE_F32 0
 #define AMP_DTYPE_BF16 1
+#define AMP_DTYPE_E4M3 2   /* FP8 GEMM output only (amp_gemm_fp8e4m3_ex_dev) */
 
 /* Message for the last nonzero status returned on this thread. */
 AMP_API const char* amp_last_error(void);
@@ -148,6 +149,18 @@ AMP_API int amp_gemm_bf16_dev(const void* A, const void* B, void* C, int c_dtype
 AMP_API int amp_gemm_fp8e4m3_dev(const uint8_t* A, const uint8_t* B, const float* scale_a,
                                  const float* scale_b, int scale_mode, void* C, int c_dtype,
                                  int M, int N, int K, void* stream);
+
+/* FP8 GEMM with output-side quantisation (AMP's GemmDesc d_scale_c / d_amax_c,
+ * include/gemm_vendor.hpp:55-56, which it hands to cuBLASLt):
+ *   v = scale_a * scale_b * (A8 . B8)  (fp32 accumulate)
+ *   c_dtype F32 / BF16: C = v;  E4M3: C = E4M3_RNE_sat(RN(v * inv)), inv =
+ *   min(RN(1/scale_c[0]), FLT_MAX) -- the quantiser's encode, so C dequantises
+ *   as code * scale_c.  amax_c (optional, device float, overwritten) = max |v|
+ *   over C, NaN ignored: the input to the next step's scale_c. */
+AMP_API int amp_gemm_fp8e4m3_ex_dev(const uint8_t* A, const uint8_t* B, const float* scale_a,
+                                    const float* scale_b, int scale_mode, void* C, int c_dtype,
+                                    const float* scale_c, float* amax_c, int M, int N, int K,
+                                    void* stream);
 
 /* ------------------------------------------------------------------------
  * FlashAttention-2 forward, bf16 in/out, fp32 softmax and accumulation.

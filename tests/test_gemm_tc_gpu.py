@@ -126,3 +126,54 @@ def test_fp8_4096_cube_vs_prequant(cuda, amp_lib):
     pre = oracle.bf16_bits_to_f32(a).astype(np.float64) @ oracle.bf16_bits_to_f32(b).astype(
         np.float64)
     assert np.abs(C - pre).max() / np.abs(pre).max() < 0.1
+
+
+@pytest.mark.parametrize("M,N,K,rowcol", [(512, 768, 1024, True), (300, 784, 512, True),
+                                          (256, 256, 256, False)])
+def test_fp8_output_quantisation_and_amax(M, N, K, rowcol, cuda, amp_lib):
+    """amax_c is max |v| of the fp32 result exactly, and the E4M3 C is the
+    quantiser's encode of that same fp32 result with scale_c = amax/448 --
+    bit-exact against the oracle's codec applied to the kernel's own fp32 C."""
+    if rowcol:
+        qa, sa, qb, sb, _, _ = fp8_operands(M, N, K, seed=M + N)
+        sa_d, sb_d = torch.from_numpy(sa).cuda(), torch.from_numpy(sb).cuda()
+    else:
+        rng = np.random.default_rng(M)
+        qa, s_a, _ = oracle.quant_e4m3(oracle.f32_to_bf16_bits(
+            rng.standard_normal((M, K), dtype=np.float32)))
+        qb, s_b, _ = oracle.quant_e4m3(oracle.f32_to_bf16_bits(
+            rng.standard_normal((K, N), dtype=np.float32)))
+        sa_d, sb_d = s_a, s_b
+    A8, B8 = torch.from_numpy(qa).cuda(), torch.from_numpy(qb).cuda()
+    amax = torch.full((1,), -1.0, device="cuda")
+    C32 = torch.empty(M, N, device="cuda")
+    gemm.launch_matmul_fp8e4m3_ex(A8, B8, C32, M, N, K, sa_d, sb_d, amax_c=amax)
+    torch.cuda.synchronize()
+    c32 = C32.cpu().numpy()
+    assert amax.item() == np.abs(c32).max()
+    # bf16 output: same amax (taken before the conversion)
+    amax_b = torch.zeros(1, device="cuda")
+    Cb = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    gemm.launch_matmul_fp8e4m3_ex(A8, B8, Cb, M, N, K, sa_d, sb_d, amax_c=amax_b)
+    # E4M3 output with the delayed-scaling scale of this result
+    scale_c = np.float32(amax.item()) / np.float32(448.0)
+    C8 = torch.empty(M, N, dtype=torch.uint8, device="cuda")
+    amax_8 = torch.zeros(1, device="cuda")
+    gemm.launch_matmul_fp8e4m3_ex(A8, B8, C8, M, N, K, sa_d, sb_d, scale_c=float(scale_c),
+                                  amax_c=amax_8)
+    torch.cuda.synchronize()
+    assert lib().amp_device_status(1) == 0
+    assert amax_b.item() == amax.item() and amax_8.item() == amax.item()
+    inv = np.float32(oracle.lib().orc_inv_scale(ctypes_float(scale_c)))
+    want = oracle.e4m3_encode((c32 * inv).astype(np.float32))
+    assert np.array_equal(C8.cpu().numpy(), want)
+    # and the dequantised codes stay within E4M3's half-step of the fp64 GEMM
+    ref = fp8_ref(qa, np.broadcast_to(np.float32(sa_d) if not rowcol else sa, (M,)).astype(np.float32),
+                  qb, np.broadcast_to(np.float32(sb_d) if not rowcol else sb, (N,)).astype(np.float32))
+    dec = oracle.e4m3_decode_table().astype(np.float64)[C8.cpu().numpy()] * float(scale_c)
+    assert np.abs(dec - ref).max() <= 0.07 * np.abs(ref).max()
+
+
+def ctypes_float(x):
+    import ctypes
+    return ctypes.c_float(float(x))
