@@ -659,4 +659,37 @@ int amp_paged_validate_block_table(const int32_t* block_table, const int32_t* ct
     return AMP_OK;
 }
 
+// Padded block table from per-sequence page lists: the shape AMP's scheduler
+// keeps (Sequence::kv_page_ids, include/scheduler.hpp:61), concatenated --
+// sequence b's pages are page_ids[seq_start[b] .. seq_start[b + 1]) in token
+// order.  block_table[b][i] = its i-th page, -1 past the list.  A list longer
+// than a table row, or shorter than the sequence's context needs, is an error.
+int amp_paged_pack_block_table(const int32_t* page_ids, const int32_t* seq_start,
+                               const int32_t* ctx_lens, int B, int max_pages_per_seq,
+                               int32_t* block_table) {
+    AMPB_REQUIRE(page_ids && seq_start && ctx_lens && block_table && B > 0 &&
+                     max_pages_per_seq > 0,
+                 AMP_ERR_INVALID, "bad block-table arguments");
+    for (int b = 0; b < B; ++b) {
+        const int n = seq_start[b + 1] - seq_start[b];
+        AMPB_REQUIRE(n >= 0 && n <= max_pages_per_seq, AMP_ERR_INVALID,
+                     "sequence %d holds %d pages, table rows hold %d", b, n, max_pages_per_seq);
+        AMPB_REQUIRE(ctx_lens[b] >= 0 && (ctx_lens[b] + kPage - 1) / kPage <= n, AMP_ERR_INVALID,
+                     "sequence %d: context %d needs %d pages, it holds %d", b, ctx_lens[b],
+                     (ctx_lens[b] + kPage - 1) / kPage, n);
+        int32_t* row = block_table + (int64_t)b * max_pages_per_seq;
+        for (int i = 0; i < max_pages_per_seq; ++i) row[i] = i < n ? page_ids[seq_start[b] + i] : -1;
+    }
+    return AMP_OK;
+}
+
+// Bytes of one contiguous K (or V) pool [num_pages][Hkv][16][head_dim] bf16.  A
+// page id handed out by a page allocator (AMP's PagePoolFast ids are 0..n-1,
+// src/pool_fast.cpp:31-60) is the pool's row, so one allocation replaces the
+// allocator's per-page cudaMalloc (src/pool_fast.cpp:11-13).
+size_t amp_paged_pool_bytes(int num_pages, int Hkv, int head_dim) {
+    if (num_pages <= 0 || Hkv <= 0 || head_dim <= 0) return 0;
+    return (size_t)num_pages * Hkv * kPage * head_dim * 2;
+}
+
 }  // extern "C"

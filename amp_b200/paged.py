@@ -79,3 +79,25 @@ def validate_block_table(block_table: np.ndarray, ctx_lens: np.ndarray, num_page
     cl = np.ascontiguousarray(ctx_lens, np.int32)
     call("amp_paged_validate_block_table", bt.ctypes.data, cl.ctypes.data, bt.shape[0],
          bt.shape[1], num_pages)
+
+
+def pack_block_table(page_lists, ctx_lens, max_pages_per_seq: int | None = None) -> np.ndarray:
+    """Padded int32 block table [B, max_pages] from per-sequence page-id lists (the
+    shape of AMP's Sequence::kv_page_ids), -1 past each list.  Raises AmpError if a
+    list cannot hold its sequence's context."""
+    lists = [np.asarray(p, np.int32).ravel() for p in page_lists]
+    B = len(lists)
+    starts = np.zeros(B + 1, np.int32)
+    starts[1:] = np.cumsum([len(p) for p in lists])
+    flat = np.concatenate(lists) if B and starts[-1] else np.zeros(1, np.int32)
+    width = max_pages_per_seq or max(1, max(len(p) for p in lists))
+    cl = np.ascontiguousarray(ctx_lens, np.int32)
+    bt = np.empty((B, width), np.int32)
+    call("amp_paged_pack_block_table", flat.ctypes.data, starts.ctypes.data, cl.ctypes.data, B,
+         width, bt.ctypes.data)
+    return bt
+
+
+def pool_bytes(num_pages: int, Hkv: int, D: int) -> int:
+    """Bytes of one contiguous K or V pool [num_pages][Hkv][16][D] bf16."""
+    return int(lib().amp_paged_pool_bytes(num_pages, Hkv, D))

@@ -212,6 +212,21 @@ AMP_API int amp_paged_attn_prefill_bf16_dev(const void* q, const void* k_pool, c
 AMP_API int amp_paged_validate_block_table(const int32_t* block_table, const int32_t* ctx_lens,
                                            int B, int max_pages_per_seq, int num_pages);
 
+/* Padded block table from per-sequence page lists (AMP's Sequence::kv_page_ids,
+ * include/scheduler.hpp:61, concatenated): sequence b's pages are
+ * page_ids[seq_start[b] .. seq_start[b+1]) in token order (seq_start has B+1
+ * entries).  Writes the HOST table block_table[B][max_pages_per_seq], -1 past
+ * each list; AMP_ERR_INVALID if a list is longer than a row or shorter than
+ * ceil(ctx_lens[b] / 16). */
+AMP_API int amp_paged_pack_block_table(const int32_t* page_ids, const int32_t* seq_start,
+                                       const int32_t* ctx_lens, int B, int max_pages_per_seq,
+                                       int32_t* block_table);
+
+/* Bytes of one contiguous K (or V) pool [num_pages][Hkv][16][head_dim] bf16; page id p
+ * (e.g. from AMP's PagePoolFast, src/pool_fast.cpp:31-60) is row p, replacing the
+ * pool's per-page cudaMalloc (src/pool_fast.cpp:11-13). */
+AMP_API size_t amp_paged_pool_bytes(int num_pages, int Hkv, int head_dim);
+
 /* Host-pointer form of the attention forward (plugin convention). */
 AMP_API int amp_user_flash_attn_fwd_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V,
                                          uint16_t* O, float* lse, int B, int Hq, int Hkv, int S_q,

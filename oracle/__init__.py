@@ -197,6 +197,50 @@ def amp_harness_inputs(M: int, N: int, K: int, seed: int = 42):
     return A.reshape(M, K), B.reshape(K, N)
 
 
+def ref_sched_lib() -> C.CDLL | None:
+    """AMP's Scheduler + PagePoolFast (CPU backend) behind a C driver, if built."""
+    path = HERE / "_ref" / "libampref_sched.so"
+    if not path.exists():
+        return None
+    r = C.CDLL(str(path))
+    vp, i32 = C.c_void_p, C.c_int
+    r.refsched_create.restype, r.refsched_create.argtypes = vp, [i32] * 5
+    r.refsched_destroy.restype, r.refsched_destroy.argtypes = None, [vp]
+    r.refsched_add.restype, r.refsched_add.argtypes = i32, [vp, i32, i32]
+    r.refsched_step.restype = i32
+    r.refsched_step.argtypes = [vp, vp, vp, vp, i32, i32]
+    return r
+
+
+class RefScheduler:
+    """Steps AMP's own scheduler and returns each batch as numpy arrays:
+    entries [n, 5] (seq id, is_prefill, n_tokens, prefill_start, ctx) and the
+    per-entry page lists."""
+
+    def __init__(self, lib_, page_tokens=16, max_pages=2048, max_batch_tokens=4096,
+                 max_seqs=256, max_prefill=512):
+        self.r = lib_
+        self.h = lib_.refsched_create(page_tokens, max_pages, max_batch_tokens, max_seqs,
+                                      max_prefill)
+
+    def add(self, prompt_len: int, max_new_tokens: int) -> int:
+        return self.r.refsched_add(self.h, prompt_len, max_new_tokens)
+
+    def step(self, cap: int = 1024, pages_cap: int = 1 << 16):
+        ent = np.zeros((cap, 5), np.int32)
+        pages = np.zeros(pages_cap, np.int32)
+        start = np.zeros(cap + 1, np.int32)
+        n = self.r.refsched_step(self.h, _vp(ent), _vp(pages), _vp(start), cap, pages_cap)
+        if n < 0:
+            raise RuntimeError(f"refsched_step: {n}")
+        return ent[:n].copy(), [pages[start[i]:start[i + 1]].copy() for i in range(n)]
+
+    def close(self):
+        if self.h:
+            self.r.refsched_destroy(self.h)
+            self.h = None
+
+
 def max_rel_err(out: np.ndarray, ref: np.ndarray) -> float:
     """AMP's metric: max |out-ref| / max(1, |ref|) (amp_validate_kernel.cpp:103-109)."""
     out = np.asarray(out, np.float64)

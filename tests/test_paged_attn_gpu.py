@@ -191,3 +191,48 @@ def test_prefill_full_workload_sampled_heads(cuda, amp_lib):
     for b, h in heads:
         assert oracle.max_rel_err(out[b, h], O[b, h]) < TOL_O
         assert np.abs(lse[b, h] - L[b, h]).max() < TOL_LSE
+
+
+def test_paged_kernels_on_amp_scheduler_batches(cuda, amp_lib):
+    """Batches from AMP's own Scheduler::schedule() (page ids from its PagePoolFast)
+    drive the decode and prefill kernels over one contiguous pool per K and V."""
+    r = oracle.ref_sched_lib()
+    if r is None:
+        pytest.skip("AMP's scheduler driver is not built (make -C oracle ref)")
+    Hq, Hkv, D, NP = 8, 2, 128, 512
+    rng = np.random.default_rng(7)
+    kp = bf16_np(rng.standard_normal((NP, Hkv, 16, D), dtype=np.float32))
+    vp = bf16_np(rng.standard_normal((NP, Hkv, 16, D), dtype=np.float32))
+    s = oracle.RefScheduler(r, max_pages=NP, max_batch_tokens=1024, max_prefill=128)
+    for _ in range(6):
+        s.add(int(rng.integers(20, 300)), int(rng.integers(2, 12)))
+    n_pre = n_dec = 0
+    try:
+        for _ in range(60):
+            ent, lists = s.step()
+            if len(ent) == 0:
+                break
+            ctx = ent[:, 4].astype(np.int32)
+            bt = paged.pack_block_table(lists, ctx)
+            dec = ent[:, 1] == 0
+            if dec.any():
+                idx = np.nonzero(dec)[0]
+                q = bf16_np(rng.standard_normal((len(idx), Hq, D), dtype=np.float32))
+                out, lse = run_decode(q, ctx[idx], bt[idx], kp, vp)
+                assert lib().amp_device_status(1) == 0
+                O, L = decode_ref(q, ctx[idx], bt[idx], kp, vp)
+                assert oracle.max_rel_err(out, O) < TOL_O
+                assert np.abs(lse - L).max() < TOL_LSE
+                n_dec += len(idx)
+            for i in np.nonzero(~dec)[0]:   # chunk lengths differ: one sequence per call
+                Lq = int(ent[i, 2])
+                q = bf16_np(rng.standard_normal((1, Hq, Lq, D), dtype=np.float32))
+                out, lse = run_prefill(q, ctx[i:i + 1], bt[i:i + 1], kp, vp)
+                assert lib().amp_device_status(1) == 0
+                O, L = prefill_ref(q, ctx[i:i + 1], bt[i:i + 1], kp, vp,
+                                   [(0, h) for h in range(Hq)])
+                assert oracle.max_rel_err(out, O) < TOL_O
+                n_pre += 1
+    finally:
+        s.close()
+    assert n_pre > 0 and n_dec > 0
