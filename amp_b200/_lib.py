@@ -38,6 +38,9 @@ SIGNATURES: dict[str, tuple] = {
     "amp_user_gemm_fp8e4m3": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32]),
     "amp_flash_attn_fwd_bf16_dev": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
                                            _i32, _i32, _i32, _f32, _vp]),
+    "amp_flash_attn_bwd_workspace_bytes": (_sz, [_i32, _i32, _i32]),
+    "amp_flash_attn_bwd_bf16_dev": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32,
+                                           _i32, _i32, _i32, _i32, _i32, _f32, _vp, _sz, _vp]),
     "amp_user_flash_attn_fwd_bf16": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
                                             _i32, _i32, _i32, _f32]),
     "amp_paged_decode_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32]),

@@ -53,3 +53,27 @@ def flash_attn_fwd(q, k, v, causal: bool = True, scale: float = 0.0):
     launch_flash_attn_bf16(q, k, v, O, lse, B, S_q, S_kv,
                            AttnCfg(Hq, Hkv, D, causal, scale))
     return O, lse
+
+
+def flash_attn_bwd(q, k, v, o, do, lse, causal: bool = True, scale: float = 0.0,
+                   workspace: torch.Tensor | None = None):
+    """Backward of flash_attn_fwd: returns (dQ, dK, dV) from the forward's q, k, v,
+    o, lse and the upstream gradient do (all [B,H,S,D] bf16 CUDA tensors; lse fp32)."""
+    B, Hq, S_q, D = q.shape
+    Hkv, S_kv = k.shape[1], k.shape[2]
+    _check(q, (B, Hq, S_q, D), "q")
+    _check(k, (B, Hkv, S_kv, D), "k")
+    _check(v, (B, Hkv, S_kv, D), "v")
+    _check(o, (B, Hq, S_q, D), "o")
+    _check(do, (B, Hq, S_q, D), "do")
+    _check(lse, (B, Hq, S_q), "lse", torch.float32)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    from ._lib import lib
+    ws_b = int(lib().amp_flash_attn_bwd_workspace_bytes(B, Hq, S_q))
+    ws = workspace if workspace is not None else torch.empty(ws_b, dtype=torch.uint8,
+                                                             device=q.device)
+    call("amp_flash_attn_bwd_bf16_dev", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+         do.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, Hq, Hkv,
+         S_q, S_kv, D, 1 if causal else 0, float(scale), ws.data_ptr(), ws.numel(),
+         torch.cuda.current_stream(q.device).cuda_stream)
+    return dq, dk, dv

@@ -1,0 +1,634 @@
+// flash_attn_bwd.cu -- FlashAttention-2 backward on tcgen05: the lse consumer.
+//
+// The reference has no backward; its forward documents lse as "required for
+// the backward pass" (kernels/flash_attn.cuh:48).  Given Q, K, V, O, dO and the
+// forward's lse (natural log):
+//   Delta = rowsum(dO * O)                                   k_fa_bwd_delta
+//   P = exp(scale Q K^T - lse),  dP = dO V^T,  dS = P * (dP - Delta)
+//   dV = P^T dO,  dK = scale dS^T Q,  dQ = scale dS K
+// in two passes shaped like the forward, so every product is one of its MMA
+// forms (SS, K-major x K-major; TS with P / dS in TMEM and an MN-major B):
+//   k_fa_bwd_dkdv  one CTA per (batch * kv head, 128-key tile).  S^T = K Q^T and
+//                  dP^T = V dO^T put keys on the TMEM lanes; P^T and dS^T go
+//                  back over them as bf16; dV += P^T dO and dK += dS^T Q
+//                  accumulate in TMEM over every query tile of every query head
+//                  that shares the kv head (GQA).
+//   k_fa_bwd_dq    one CTA per (batch * query head, 128-query tile).  S = Q K^T,
+//                  dP = dO V^T with queries on the lanes; dS back over dP;
+//                  dQ += dS K over the visible key tiles.
+// Each pass recomputes P from lse, so there are no atomics and no fp32 dQ
+// accumulator in global memory.  Both kernels: warp 0 TMA, warp 1 TMEM + MMA
+// issue, warps 2-5 the element-wise work (one TMEM lane = one row per thread).
+#include <cuda.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+
+#include "common.cuh"
+#include "runtime.h"
+#include "tc_common.cuh"
+
+namespace ampb {
+
+int fa_make_tmap_3d(CUtensorMap* m, const void* base, int64_t d, int64_t s, int64_t bh);
+
+namespace {
+
+constexpr int BT = 128;                 // rows per query / key tile
+constexpr int kThreads = 192;
+constexpr int SLAB_BYTES = 128 * 128;   // [128 rows x 128 bytes] swizzled slab
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D>
+struct BwdCfg {
+    static constexpr int SLABS = D / 64;
+    static constexpr int TILE = SLABS * SLAB_BYTES;          // 128 rows x D bf16
+    static constexpr uint32_t IDESC_SS = make_idesc(1, 1, 0, 0, BT, BT);
+    static constexpr uint32_t IDESC_TS = make_idesc(1, 1, 0, 1, BT, D);
+};
+
+struct BwdParams {
+    int B, Hq, Hkv, S_q, S_kv;
+    int causal, causal_offset;   // key j visible for query i iff j <= i + causal_offset
+    float scale, scale_log2;
+    const float* lse;            // [B*Hq][S_q], natural log (forward output)
+    const float* delta;          // [B*Hq][S_q]
+    void* dq;                    // [B*Hq][S_q][D] bf16
+    void* dk;                    // [B*Hkv][S_kv][D] bf16
+    void* dv;
+    int* status;
+};
+
+// SS product of two 128-row K-major tiles over D: acc[128 x 128] (+)= A B^T
+template <int D>
+__device__ __forceinline__ void mma_ss(uint32_t acc, uint32_t a_addr, uint32_t b_addr) {
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off = (kk >> 2) * SLAB_BYTES + (kk & 3) * 32;
+        tc_mma_f16(acc, smem_desc_sw128(a_addr + off, 16, 1024),
+                   smem_desc_sw128(b_addr + off, 16, 1024), BwdCfg<D>::IDESC_SS, kk != 0);
+    }
+}
+// TS product: acc[128 x D] (+)= T[128 x 128] (bf16 in TMEM) x B[128 rows x D] (MN-major)
+template <int D>
+__device__ __forceinline__ void mma_ts(uint32_t acc, uint32_t t_col, uint32_t b_addr,
+                                       bool accumulate) {
+#pragma unroll
+    for (int kk = 0; kk < BT / 16; ++kk)
+        tc_mma_f16_ts(acc, t_col + kk * 8, smem_desc_sw128(b_addr + kk * 16 * 128, SLAB_BYTES, 1024),
+                      BwdCfg<D>::IDESC_TS, (accumulate || kk != 0) ? 1u : 0u);
+}
+
+// ---------------------------------------------------------------- Delta
+// Delta[row] = sum_d dO[row][d] * O[row][d] in fp32; one warp per row.
+template <int D>
+__global__ void __launch_bounds__(256) k_fa_bwd_delta(const __nv_bfloat16* __restrict__ O,
+                                                      const __nv_bfloat16* __restrict__ dO,
+                                                      float* __restrict__ delta, int64_t rows) {
+    const int lane = threadIdx.x & 31;
+    for (int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); r < rows;
+         r += (int64_t)gridDim.x * 8) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int c = lane * 4; c < D; c += 128) {
+            const uint2 o = *reinterpret_cast<const uint2*>(O + r * D + c);
+            const uint2 g = *reinterpret_cast<const uint2*>(dO + r * D + c);
+            acc = fmaf(bf16_lo(o.x), bf16_lo(g.x), acc);
+            acc = fmaf(bf16_hi(o.x), bf16_hi(g.x), acc);
+            acc = fmaf(bf16_lo(o.y), bf16_lo(g.y), acc);
+            acc = fmaf(bf16_hi(o.y), bf16_hi(g.y), acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) delta[r] = acc;
+    }
+}
+
+// store one 128 x D fp32 TMEM accumulator row (this thread's lane) as bf16 * mul
+template <int D>
+__device__ __forceinline__ void store_row(uint32_t lane_addr, float mul, __nv_bfloat16* row,
+                                          bool ok) {
+    __syncwarp();
+#pragma unroll
+    for (int oc = 0; oc < D / 32; ++oc) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_addr + oc * 32, v);
+        tmem_ld_wait();
+        if (ok) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 8) {
+                uint4 w;
+                w.x = f32x2_to_bf16x2(__uint_as_float(v[e]) * mul, __uint_as_float(v[e + 1]) * mul);
+                w.y = f32x2_to_bf16x2(__uint_as_float(v[e + 2]) * mul, __uint_as_float(v[e + 3]) * mul);
+                w.z = f32x2_to_bf16x2(__uint_as_float(v[e + 4]) * mul, __uint_as_float(v[e + 5]) * mul);
+                w.w = f32x2_to_bf16x2(__uint_as_float(v[e + 6]) * mul, __uint_as_float(v[e + 7]) * mul);
+                *reinterpret_cast<uint4*>(row + oc * 32 + e) = w;
+            }
+        }
+    }
+}
+
+template <int D>
+__device__ __forceinline__ void store_zero_row(__nv_bfloat16* row) {
+#pragma unroll
+    for (int e = 0; e < D; e += 8) *reinterpret_cast<uint4*>(row + e) = make_uint4(0u, 0u, 0u, 0u);
+}
+
+// ---------------------------------------------------------------- dK, dV
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_fa_bwd_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                  const BwdParams p) {
+    using CF = BwdCfg<D>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint8_t* k_s = smem;                          // K_j
+    uint8_t* v_s = k_s + CF::TILE;                // V_j
+    uint8_t* q_s = v_s + CF::TILE;                // [2][Q_i]
+    uint8_t* o_s = q_s + 2 * CF::TILE;            // [2][dO_i]
+    float* cols = reinterpret_cast<float*>(o_s + 2 * CF::TILE);   // [2][2][128] lse2, Delta
+    uint64_t* bars = reinterpret_cast<uint64_t*>(cols + 2 * 2 * BT);
+    uint64_t* kv_full = bars;
+    uint64_t* qs_full = bars + 1;     // [2]
+    uint64_t* qs_empty = bars + 3;    // [2]
+    uint64_t* sdp_full = bars + 5;
+    uint64_t* pds_full = bars + 6;
+    uint64_t* dkv_done = bars + 7;
+    uint64_t* drain = bars + 8;
+    uint64_t* cols_ready = bars + 9;  // [2]: the 128 element-wise threads posted lse2 / Delta
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int jt = blockIdx.x, bh_kv = blockIdx.y;
+    const int b = bh_kv / p.Hkv, hk = bh_kv % p.Hkv;
+    const int G = p.Hq / p.Hkv;
+    const int k0 = jt * BT;
+    const int n_qt = (p.S_q + BT - 1) / BT;
+    int i_lo = 0;
+    if (p.causal) {   // first query tile with a query that sees a key of this tile
+        const int first_q = k0 - p.causal_offset;
+        i_lo = first_q <= 0 ? 0 : first_q / BT;
+    }
+    const int per_head = max(0, n_qt - i_lo);
+    const int steps = G * per_head;
+
+    if (threadIdx.x == 0) {
+        mbar_init(kv_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&qs_full[s], 1);
+            mbar_init(&qs_empty[s], 1);
+        }
+        mbar_init(sdp_full, 1);
+        mbar_init(pds_full, 4);
+        mbar_init(dkv_done, 1);
+        mbar_init(drain, 1);
+        mbar_init(&cols_ready[0], 128);
+        mbar_init(&cols_ready[1], 128);
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t T_S = tmem, T_dP = tmem + BT, T_dV = tmem + 2 * BT, T_dK = tmem + 2 * BT + D;
+
+    if (warp == 0) {
+        if (lane == 0 && steps > 0) {
+            tma_prefetch_desc(&tmQ);
+            tma_prefetch_desc(&tmdO);
+            mbar_arrive_expect_tx(kv_full, 2 * CF::TILE);
+#pragma unroll
+            for (int sl = 0; sl < CF::SLABS; ++sl) {
+                tma_load_3d(k_s + sl * SLAB_BYTES, &tmK, kv_full, sl * 64, k0, bh_kv);
+                tma_load_3d(v_s + sl * SLAB_BYTES, &tmV, kv_full, sl * 64, k0, bh_kv);
+            }
+            for (int t = 0; t < steps; ++t) {
+                const int s = t & 1;
+                if (!mbar_wait(&qs_empty[s], ((t >> 1) & 1) ^ 1, p.status)) break;
+                const int g = t / per_head, it = i_lo + t % per_head;
+                const int bh_q = b * p.Hq + hk * G + g;
+                mbar_arrive_expect_tx(&qs_full[s], 2 * CF::TILE);
+#pragma unroll
+                for (int sl = 0; sl < CF::SLABS; ++sl) {
+                    tma_load_3d(q_s + s * CF::TILE + sl * SLAB_BYTES, &tmQ, &qs_full[s], sl * 64,
+                                it * BT, bh_q);
+                    tma_load_3d(o_s + s * CF::TILE + sl * SLAB_BYTES, &tmdO, &qs_full[s], sl * 64,
+                                it * BT, bh_q);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && steps > 0) {
+            bool ok = mbar_wait(kv_full, 0, p.status);
+            const uint32_t ka = smem_u32(k_s), va = smem_u32(v_s);
+            for (int t = 0; ok && t < steps; ++t) {
+                const int s = t & 1;
+                if (!mbar_wait(&qs_full[s], (t >> 1) & 1, p.status)) break;
+                // P^T / dS^T of step t-1 live in T_S / T_dP: dV/dK must have read them
+                if (t > 0 && !mbar_wait(dkv_done, (t - 1) & 1, p.status)) break;
+                tc_fence_after();
+                const uint32_t qa = smem_u32(q_s + s * CF::TILE), oa = smem_u32(o_s + s * CF::TILE);
+                mma_ss<D>(T_S, ka, qa);     // S^T = K Q^T
+                mma_ss<D>(T_dP, va, oa);    // dP^T = V dO^T
+                tc_commit(sdp_full);
+                if (!mbar_wait(pds_full, t & 1, p.status)) break;
+                tc_fence_after();
+                mma_ts<D>(T_dV, T_S, oa, t != 0);    // dV += P^T dO
+                mma_ts<D>(T_dK, T_dP, qa, t != 0);   // dK += dS^T Q
+                tc_commit(&qs_empty[s]);
+                tc_commit(dkv_done);
+            }
+            tc_commit(drain);
+            mbar_wait(drain, 0, p.status);
+        }
+    } else {
+        // ---------------------------------------------------- element-wise
+        const int quad = warp & 3;
+        const int tid = threadIdx.x - 64;             // 0..127
+        const int kr = quad * 32 + lane;              // key row == TMEM lane
+        const int kj = k0 + kr;
+        const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+        const float c = p.scale_log2;
+        bool ok = true;
+        // lse2 / Delta of the next step's query tile, one query per thread
+        auto fetch = [&](int t, float& l2, float& dl) {
+            const int g = t / per_head, it = i_lo + t % per_head;
+            const int q = it * BT + tid;
+            const int64_t row = (int64_t)(b * p.Hq + hk * G + g) * p.S_q + q;
+            const float lse = q < p.S_q ? p.lse[row] : -INFINITY;
+            l2 = lse == -INFINITY ? INFINITY : lse * kLog2e;   // +inf: the column's P is 0
+            dl = q < p.S_q ? p.delta[row] : 0.0f;
+        };
+        float nl2 = 0.0f, ndl = 0.0f;
+        if (steps > 0) fetch(0, nl2, ndl);
+        for (int t = 0; t < steps; ++t) {
+            // [lse2 | Delta] of this step's query tile, one value per thread; a buffer
+            // is rewritten two steps later, after every thread has posted the step
+            // in between (so it has finished reading this one)
+            float* cl = cols + (t & 1) * 2 * BT;
+            cl[tid] = nl2;
+            cl[BT + tid] = ndl;
+            mbar_arrive(&cols_ready[t & 1]);
+            if (!mbar_wait_warp(&cols_ready[t & 1], (t >> 1) & 1, p.status)) { ok = false; break; }
+            if (t + 1 < steps) fetch(t + 1, nl2, ndl);
+            const int it = i_lo + t % per_head;
+            const int q0 = it * BT;
+            if (!mbar_wait_warp(sdp_full, t & 1, p.status)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t sv[2][32], dv[2][32];
+                __syncwarp();
+                tmem_ld_32x32b_x32(T_S + lane_base + h * 64, sv[0]);
+                tmem_ld_32x32b_x32(T_S + lane_base + h * 64 + 32, sv[1]);
+                tmem_ld_32x32b_x32(T_dP + lane_base + h * 64, dv[0]);
+                tmem_ld_32x32b_x32(T_dP + lane_base + h * 64 + 32, dv[1]);
+                tmem_ld_wait();
+                uint32_t pw[32], dw[32];
+#pragma unroll
+                for (int e = 0; e < 64; e += 2) {
+                    const int qc = h * 64 + e;            // query column within the tile
+                    const float2 l2 = *reinterpret_cast<const float2*>(cl + qc);
+                    const float2 dl = *reinterpret_cast<const float2*>(cl + BT + qc);
+                    const int q = q0 + qc;
+                    const bool v0 = kj < p.S_kv && (!p.causal || kj <= q + p.causal_offset);
+                    const bool v1 = kj < p.S_kv && (!p.causal || kj <= q + 1 + p.causal_offset);
+                    const float s0 = __uint_as_float(sv[e >> 5][e & 31]);
+                    const float s1 = __uint_as_float(sv[e >> 5][(e & 31) + 1]);
+                    const float p0 = v0 ? ex2_approx(fmaf(s0, c, -l2.x)) : 0.0f;
+                    const float p1 = v1 ? ex2_approx(fmaf(s1, c, -l2.y)) : 0.0f;
+                    const float d0 = p0 * (__uint_as_float(dv[e >> 5][e & 31]) - dl.x);
+                    const float d1 = p1 * (__uint_as_float(dv[e >> 5][(e & 31) + 1]) - dl.y);
+                    pw[e >> 1] = f32x2_to_bf16x2(p0, p1);
+                    dw[e >> 1] = f32x2_to_bf16x2(d0, d1);
+                }
+                // P^T over S^T, dS^T over dP^T (columns of this half were read above)
+                tmem_st_32x32b_x32(T_S + lane_base + h * 32, pw);
+                tmem_st_32x32b_x32(T_dP + lane_base + h * 32, dw);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(pds_full);
+        }
+        // epilogue: dK = scale * acc, dV = acc
+        __nv_bfloat16* dk_row = static_cast<__nv_bfloat16*>(p.dk) + ((int64_t)bh_kv * p.S_kv + (kj < p.S_kv ? kj : 0)) * D;
+        __nv_bfloat16* dv_row = static_cast<__nv_bfloat16*>(p.dv) + ((int64_t)bh_kv * p.S_kv + (kj < p.S_kv ? kj : 0)) * D;
+        if (steps == 0) {
+            if (kj < p.S_kv) {
+                store_zero_row<D>(dk_row);
+                store_zero_row<D>(dv_row);
+            }
+        } else if (ok && mbar_wait_warp(dkv_done, (steps - 1) & 1, p.status)) {
+            tc_fence_after();
+            store_row<D>(T_dK + lane_base, p.scale, dk_row, kj < p.S_kv);
+            store_row<D>(T_dV + lane_base, 1.0f, dv_row, kj < p.S_kv);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------- dQ
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_fa_bwd_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                const BwdParams p) {
+    using CF = BwdCfg<D>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint8_t* q_s = smem;                          // Q_i
+    uint8_t* o_s = q_s + CF::TILE;                // dO_i
+    uint8_t* k_s = o_s + CF::TILE;                // [2][K_j]
+    uint8_t* v_s = k_s + 2 * CF::TILE;            // [2][V_j]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(v_s + 2 * CF::TILE);
+    uint64_t* q_full = bars;
+    uint64_t* k_full = bars + 1;      // [2]
+    uint64_t* k_empty = bars + 3;     // [2]
+    uint64_t* v_full = bars + 5;      // [2]
+    uint64_t* v_empty = bars + 7;     // [2]
+    uint64_t* sdp_full = bars + 9;
+    uint64_t* ds_full = bars + 10;
+    uint64_t* dq_done = bars + 11;
+    uint64_t* drain = bars + 12;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_qt = (p.S_q + BT - 1) / BT;
+    const int it = n_qt - 1 - (int)blockIdx.x;   // heaviest causal tiles first
+    const int bh = blockIdx.y;
+    const int b = bh / p.Hq, h = bh % p.Hq;
+    const int bh_kv = b * p.Hkv + h / (p.Hq / p.Hkv);
+    const int q0 = it * BT;
+    int n_kv = (p.S_kv + BT - 1) / BT;
+    if (p.causal) {
+        const int last = q0 + BT - 1 + p.causal_offset;
+        n_kv = min(n_kv, last < 0 ? 0 : last / BT + 1);
+    }
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
+        }
+        mbar_init(sdp_full, 1);
+        mbar_init(ds_full, 4);
+        mbar_init(dq_done, 1);
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t T_S = tmem, T_dP = tmem + BT, T_dQ = tmem + 2 * BT;
+
+    if (warp == 0) {
+        if (lane == 0 && n_kv > 0) {
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+            mbar_arrive_expect_tx(q_full, 2 * CF::TILE);
+#pragma unroll
+            for (int sl = 0; sl < CF::SLABS; ++sl) {
+                tma_load_3d(q_s + sl * SLAB_BYTES, &tmQ, q_full, sl * 64, q0, bh);
+                tma_load_3d(o_s + sl * SLAB_BYTES, &tmdO, q_full, sl * 64, q0, bh);
+            }
+            for (int j = 0; j < n_kv; ++j) {
+                const int s = j & 1;
+                const uint32_t ph = ((j >> 1) & 1) ^ 1;
+                if (!mbar_wait(&k_empty[s], ph, p.status)) break;
+                mbar_arrive_expect_tx(&k_full[s], CF::TILE);
+#pragma unroll
+                for (int sl = 0; sl < CF::SLABS; ++sl)
+                    tma_load_3d(k_s + s * CF::TILE + sl * SLAB_BYTES, &tmK, &k_full[s], sl * 64,
+                                j * BT, bh_kv);
+                if (!mbar_wait(&v_empty[s], ph, p.status)) break;
+                mbar_arrive_expect_tx(&v_full[s], CF::TILE);
+#pragma unroll
+                for (int sl = 0; sl < CF::SLABS; ++sl)
+                    tma_load_3d(v_s + s * CF::TILE + sl * SLAB_BYTES, &tmV, &v_full[s], sl * 64,
+                                j * BT, bh_kv);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && n_kv > 0) {
+            bool ok = mbar_wait(q_full, 0, p.status);
+            const uint32_t qa = smem_u32(q_s), oa = smem_u32(o_s);
+            for (int j = 0; ok && j < n_kv; ++j) {
+                const int s = j & 1;
+                const uint32_t ph = (j >> 1) & 1;
+                if (!mbar_wait(&k_full[s], ph, p.status) || !mbar_wait(&v_full[s], ph, p.status))
+                    break;
+                // dS of step j-1 lives in T_dP: dQ must have read it
+                if (j > 0 && !mbar_wait(dq_done, (j - 1) & 1, p.status)) break;
+                tc_fence_after();
+                const uint32_t ka = smem_u32(k_s + s * CF::TILE), va = smem_u32(v_s + s * CF::TILE);
+                mma_ss<D>(T_S, qa, ka);     // S = Q K^T
+                mma_ss<D>(T_dP, oa, va);    // dP = dO V^T
+                tc_commit(&v_empty[s]);
+                tc_commit(sdp_full);
+                if (!mbar_wait(ds_full, j & 1, p.status)) break;
+                tc_fence_after();
+                mma_ts<D>(T_dQ, T_dP, ka, j != 0);   // dQ += dS K
+                tc_commit(&k_empty[s]);
+                tc_commit(dq_done);
+            }
+            tc_commit(drain);
+            mbar_wait(drain, 0, p.status);
+        }
+    } else {
+        // ---------------------------------------------------- element-wise
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;               // query row == TMEM lane
+        const int qi = q0 + r;
+        const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+        const float c = p.scale_log2;
+        const int64_t row = (int64_t)bh * p.S_q + qi;
+        const float lse = qi < p.S_q ? p.lse[row] : -INFINITY;
+        const float l2 = lse == -INFINITY ? INFINITY : lse * kLog2e;   // +inf: P = 0
+        const float dl = qi < p.S_q ? p.delta[row] : 0.0f;
+        const int vis_hi = p.causal ? min(p.S_kv - 1, qi + p.causal_offset) : p.S_kv - 1;
+        bool ok = true;
+        for (int j = 0; j < n_kv; ++j) {
+            if (!mbar_wait_warp(sdp_full, j & 1, p.status)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t sv[2][32], dv[2][32];
+                __syncwarp();
+                tmem_ld_32x32b_x32(T_S + lane_base + hh * 64, sv[0]);
+                tmem_ld_32x32b_x32(T_S + lane_base + hh * 64 + 32, sv[1]);
+                tmem_ld_32x32b_x32(T_dP + lane_base + hh * 64, dv[0]);
+                tmem_ld_32x32b_x32(T_dP + lane_base + hh * 64 + 32, dv[1]);
+                tmem_ld_wait();
+                const int kb = j * BT + hh * 64;
+                uint32_t dw[32];
+#pragma unroll
+                for (int e = 0; e < 64; e += 2) {
+                    const float s0 = __uint_as_float(sv[e >> 5][e & 31]);
+                    const float s1 = __uint_as_float(sv[e >> 5][(e & 31) + 1]);
+                    const float p0 = kb + e <= vis_hi ? ex2_approx(fmaf(s0, c, -l2)) : 0.0f;
+                    const float p1 = kb + e + 1 <= vis_hi ? ex2_approx(fmaf(s1, c, -l2)) : 0.0f;
+                    const float d0 = p0 * (__uint_as_float(dv[e >> 5][e & 31]) - dl);
+                    const float d1 = p1 * (__uint_as_float(dv[e >> 5][(e & 31) + 1]) - dl);
+                    dw[e >> 1] = f32x2_to_bf16x2(d0, d1);
+                }
+                tmem_st_32x32b_x32(T_dP + lane_base + hh * 32, dw);   // dS over dP
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(ds_full);
+        }
+        __nv_bfloat16* dq_row = static_cast<__nv_bfloat16*>(p.dq) + ((int64_t)bh * p.S_q + (qi < p.S_q ? qi : 0)) * D;
+        if (n_kv == 0) {
+            if (qi < p.S_q) store_zero_row<D>(dq_row);
+        } else if (ok && mbar_wait_warp(dq_done, (n_kv - 1) & 1, p.status)) {
+            tc_fence_after();
+            store_row<D>(T_dQ + lane_base, p.scale, dq_row, qi < p.S_q);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+template <int D>
+int launch_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+               const float* lse, void* dQ, void* dK, void* dV, float* delta, int B, int Hq,
+               int Hkv, int S_q, int S_kv, int causal, float scale, cudaStream_t st) {
+    using CF = BwdCfg<D>;
+    CUtensorMap tq, tk, tv, to;
+    int rc;
+    if ((rc = fa_make_tmap_3d(&tq, Q, D, S_q, (int64_t)B * Hq))) return rc;
+    if ((rc = fa_make_tmap_3d(&to, dO, D, S_q, (int64_t)B * Hq))) return rc;
+    if ((rc = fa_make_tmap_3d(&tk, K, D, S_kv, (int64_t)B * Hkv))) return rc;
+    if ((rc = fa_make_tmap_3d(&tv, V, D, S_kv, (int64_t)B * Hkv))) return rc;
+    int* status = nullptr;
+    if ((rc = device_status(&status))) return rc;
+    BwdParams p;
+    p.B = B;
+    p.Hq = Hq;
+    p.Hkv = Hkv;
+    p.S_q = S_q;
+    p.S_kv = S_kv;
+    p.causal = causal;
+    p.causal_offset = 0;
+    p.scale = scale;
+    p.scale_log2 = scale * kLog2e;
+    p.lse = lse;
+    p.delta = delta;
+    p.dq = dQ;
+    p.dk = dK;
+    p.dv = dV;
+    p.status = status;
+    const int64_t rows = (int64_t)B * Hq * S_q;
+    const int dgrid = (int)std::min<int64_t>((rows + 7) / 8, (int64_t)sm_count() * 16);
+    k_fa_bwd_delta<D><<<dgrid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(O),
+                                             static_cast<const __nv_bfloat16*>(dO), delta, rows);
+    AMPB_CHECK_LAUNCH("k_fa_bwd_delta");
+    constexpr int SMEM_KV = 6 * CF::TILE + 2 * 2 * BT * 4 + 1024 + 256;
+    constexpr int SMEM_Q = 6 * CF::TILE + 1024 + 256;
+    static std::atomic<uint64_t> attr_done{0};
+    int dev = 0;
+    AMPB_CHECK_CUDA(cudaGetDevice(&dev));
+    if (dev >= 64 || !(attr_done.load() >> dev & 1)) {
+        AMPB_CHECK_CUDA(cudaFuncSetAttribute(k_fa_bwd_dkdv<D>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_KV));
+        AMPB_CHECK_CUDA(cudaFuncSetAttribute(k_fa_bwd_dq<D>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_Q));
+        if (dev < 64) attr_done.fetch_or(1ull << dev);
+    }
+    k_fa_bwd_dkdv<D><<<dim3((S_kv + BT - 1) / BT, B * Hkv), kThreads, SMEM_KV, st>>>(tq, tk, tv,
+                                                                                       to, p);
+    AMPB_CHECK_LAUNCH("k_fa_bwd_dkdv");
+    k_fa_bwd_dq<D><<<dim3((S_q + BT - 1) / BT, B * Hq), kThreads, SMEM_Q, st>>>(tq, tk, tv, to, p);
+    AMPB_CHECK_LAUNCH("k_fa_bwd_dq");
+    return AMP_OK;
+}
+
+}  // namespace
+
+size_t fa_bwd_ws_bytes(int B, int Hq, int S_q) { return (size_t)B * Hq * S_q * 4 + 256; }
+
+int flash_attn_bwd_dev(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                       const float* lse, void* dQ, void* dK, void* dV, int B, int Hq, int Hkv,
+                       int S_q, int S_kv, int D, int causal, float scale, void* ws,
+                       size_t ws_bytes, cudaStream_t st) {
+    AMPB_REQUIRE(B > 0 && Hq > 0 && Hkv > 0 && S_q > 0 && S_kv > 0, AMP_ERR_INVALID,
+                 "attention sizes must be positive");
+    AMPB_REQUIRE(Hq % Hkv == 0, AMP_ERR_INVALID, "num_q_heads (%d) must be a multiple of "
+                 "num_kv_heads (%d)", Hq, Hkv);
+    AMPB_REQUIRE(Q && K && V && O && dO && lse && dQ && dK && dV && ws, AMP_ERR_INVALID,
+                 "NULL tensor");
+    AMPB_REQUIRE(aligned16(Q) && aligned16(K) && aligned16(V) && aligned16(O) && aligned16(dO) &&
+                     aligned16(dQ) && aligned16(dK) && aligned16(dV),
+                 AMP_ERR_INVALID, "tensors must be 16-byte aligned");
+    AMPB_REQUIRE(!causal || S_q == S_kv, AMP_ERR_UNSUPPORTED,
+                 "causal backward needs S_q == S_kv (top-left aligned mask)");
+    AMPB_REQUIRE((int64_t)B * Hq <= 65535, AMP_ERR_UNSUPPORTED, "B*Hq must be <= 65535");
+    AMPB_REQUIRE(ws_bytes >= fa_bwd_ws_bytes(B, Hq, S_q), AMP_ERR_INVALID,
+                 "workspace too small: %zu < %zu", ws_bytes, fa_bwd_ws_bytes(B, Hq, S_q));
+    AMPB_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 15u) == 0, AMP_ERR_INVALID,
+                 "workspace must be 16-byte aligned");
+    if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)D);
+    float* delta = static_cast<float*>(ws);
+    switch (D) {
+        case 128:
+            return launch_bwd<128>(Q, K, V, O, dO, lse, dQ, dK, dV, delta, B, Hq, Hkv, S_q, S_kv,
+                                   causal, scale, st);
+        case 64:
+            return launch_bwd<64>(Q, K, V, O, dO, lse, dQ, dK, dV, delta, B, Hq, Hkv, S_q, S_kv,
+                                  causal, scale, st);
+        default:
+            set_error(AMP_ERR_UNSUPPORTED, "flash_attn backward: head_dim %d not supported (64, 128)", D);
+            return AMP_ERR_UNSUPPORTED;
+    }
+}
+
+}  // namespace ampb
+
+using namespace ampb;
+
+extern "C" {
+
+size_t amp_flash_attn_bwd_workspace_bytes(int B, int Hq, int S_q) {
+    return fa_bwd_ws_bytes(B, Hq, S_q);
+}
+
+int amp_flash_attn_bwd_bf16_dev(const void* Q, const void* K, const void* V, const void* O,
+                                const void* dO, const float* lse, void* dQ, void* dK, void* dV,
+                                int B, int Hq, int Hkv, int S_q, int S_kv, int head_dim,
+                                int causal, float scale, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+    return flash_attn_bwd_dev(Q, K, V, O, dO, lse, dQ, dK, dV, B, Hq, Hkv, S_q, S_kv, head_dim,
+                              causal, scale, workspace, workspace_bytes, as_stream(stream));
+}
+
+}  // extern "C"

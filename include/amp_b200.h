@@ -175,6 +175,19 @@ AMP_API int amp_flash_attn_fwd_bf16_dev(const void* Q, const void* K, const void
                                         float* lse, int B, int Hq, int Hkv, int S_q, int S_kv,
                                         int head_dim, int causal, float scale, void* stream);
 
+/* FlashAttention-2 backward (AMP has none; its forward's lse is "required for the
+ * backward pass", kernels/flash_attn.cuh:48).  Inputs: the forward's Q, K, V, O
+ * and lse (natural log) and dO; outputs dQ [B,Hq,S_q,D], dK and dV [B,Hkv,S_kv,D]
+ * bf16 (a kv head's dK / dV sum over its query heads).  P is recomputed from
+ * lse.  causal needs S_q == S_kv.  Workspace: amp_flash_attn_bwd_workspace_bytes
+ * (the fp32 row sums of dO * O). */
+AMP_API size_t amp_flash_attn_bwd_workspace_bytes(int B, int Hq, int S_q);
+AMP_API int amp_flash_attn_bwd_bf16_dev(const void* Q, const void* K, const void* V,
+                                        const void* O, const void* dO, const float* lse,
+                                        void* dQ, void* dK, void* dV, int B, int Hq, int Hkv,
+                                        int S_q, int S_kv, int head_dim, int causal, float scale,
+                                        void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------
  * Attention over a paged KV cache (block tables of 16-token pages, the
  * format of Sequence::kv_page_ids / kv_page_size_tokens in the reference's

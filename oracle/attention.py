@@ -9,7 +9,8 @@ Restates the semantics of the reference's FlashAttention-2 forward
     with offset = S_kv - S_q, which the `causal_offset` argument expresses
   * O = softmax(s) V; lse = m + ln(l) = ln sum_j exp(s_ij)  (flash_attn.cu:195)
 The reference has no CPU attention path of its own; this is the oracle the
-GPU kernels are checked against, computed exactly in fp64.
+GPU kernels are checked against, computed exactly in fp64 (forward, and the
+backward that consumes its lse).
 """
 from __future__ import annotations
 
@@ -49,6 +50,45 @@ def flash_attn_fwd(q, k, v, causal: bool = True, scale: float = 0.0, causal_offs
                 O[b, h] = np.where(l > 0, (p @ v[b, hk]) / l, 0.0)
                 lse[b, h] = np.where(l[:, 0] > 0, m_safe[:, 0] + np.log(l[:, 0]), -np.inf)
     return O, lse
+
+
+def flash_attn_bwd(q, k, v, do, causal: bool = True, scale: float = 0.0, causal_offset: int = 0):
+    """Gradients of O = softmax(scale * Q K^T) V, in float64: returns (dQ, dK, dV).
+
+    The reference has no backward (its lse output is documented as "required for
+    the backward pass", kernels/flash_attn.cuh:48); this is the standard chain
+    rule the GPU backward is checked against: P = softmax(S); dV = P^T dO;
+    dP = dO V^T; dS = P * (dP - rowsum(dO * O)); dQ = scale dS K; dK = scale dS^T Q.
+    GQA: a kv head's dK / dV sum over the query heads that share it."""
+    q, k, v, do = (np.asarray(x, np.float64) for x in (q, k, v, do))
+    B, Hq, Sq, D = q.shape
+    Hkv, Skv = k.shape[1], k.shape[2]
+    group = Hq // Hkv
+    sc = scale if scale > 0 else 1.0 / np.sqrt(D)
+    dq = np.zeros_like(q)
+    dk = np.zeros_like(k)
+    dv = np.zeros_like(v)
+    if causal:
+        masked = np.arange(Skv)[None, :] > np.arange(Sq)[:, None] + causal_offset
+    for b in range(B):
+        for h in range(Hq):
+            hk = h // group
+            s = (q[b, h] @ k[b, hk].T) * sc
+            if causal:
+                s = np.where(masked, -np.inf, s)
+            m = s.max(axis=1, keepdims=True)
+            m = np.where(np.isfinite(m), m, 0.0)
+            e = np.exp(s - m)
+            l = e.sum(axis=1, keepdims=True)
+            p = np.where(l > 0, e / np.where(l > 0, l, 1.0), 0.0)
+            o = p @ v[b, hk]
+            dv[b, hk] += p.T @ do[b, h]
+            dp = do[b, h] @ v[b, hk].T
+            delta = (do[b, h] * o).sum(axis=1, keepdims=True)
+            ds = p * (dp - delta)
+            dq[b, h] = sc * (ds @ k[b, hk])
+            dk[b, hk] += sc * (ds.T @ q[b, h])
+    return dq, dk, dv
 
 
 def paged_gather(pool, block_table, ctx_len, page_size: int = 16):
