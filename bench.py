@@ -659,8 +659,95 @@ class PagedPrefillWorkload(PagedDecodeWorkload):
                                       out=self.out, lse=self.lse)
 
 
+class AttentionBwdWorkload(AttentionWorkload):
+    """FA2 backward (dQ, dK, dV from the forward's O and lse) on the same causal
+    configuration; FLOPs by the usual convention of 2.5x the forward (five
+    S x S x D products), although the two-pass kernels recompute P and dP."""
+    name = "fa2_bwd"
+    metric = "fa2_bwd_causal_TFLOPS"
+
+    def __init__(self, dist: Dist, args):
+        super().__init__(dist, args)
+        torch = self.torch
+        from amp_b200._lib import lib
+        g = torch.Generator(device=self.q.device)
+        g.manual_seed(199 + dist.rank)
+        self.do = torch.randn(self.q.shape, generator=g, device=self.q.device).to(torch.bfloat16)
+        self.att.launch_flash_attn_bf16(self.q, self.k, self.v, self.o, self.lse, 1, self.S,
+                                        self.S, self.cfg)
+        self.dq, self.dk, self.dv = (torch.empty_like(self.q) for _ in range(3))
+        self.ws = torch.empty(int(lib().amp_flash_attn_bwd_workspace_bytes(1, self.bh, self.S)),
+                              dtype=torch.uint8, device=self.q.device)
+
+    def units_per_step(self) -> float:
+        return 2.5 * super().units_per_step()
+
+    def launches_per_step(self) -> int:
+        return 3
+
+    def config(self):
+        c = super().config()
+        c["workload"] = "flash_attn2_bwd_causal"
+        c["flop_convention"] = "2.5 x 4*B*H*D*S*(S+1)/2 (five products over the visible pairs)"
+        c["parallelism"] = "single" if self.dist.world == 1 else f"(batch*head) split over {self.dist.world} GPUs"
+        return c
+
+    def kernel_table(self):
+        return [("k_fa_bwd_delta + k_fa_bwd_dkdv + k_fa_bwd_dq", self.units_per_step())]
+
+    def _call(self, q, k, v, o, do, lse, dq, dk, dv):
+        from amp_b200._lib import call
+        call("amp_flash_attn_bwd_bf16_dev", q.data_ptr(), k.data_ptr(), v.data_ptr(),
+             o.data_ptr(), do.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+             dv.data_ptr(), 1, self.bh, self.bh, self.S, self.S, self.D, 1, 0.0,
+             self.ws.data_ptr(), self.ws.numel(),
+             self.torch.cuda.current_stream(q.device).cuda_stream)
+
+    def step(self, ev=None):
+        if ev: ev[0].record()
+        self._call(self.q, self.k, self.v, self.o, self.do, self.lse, self.dq, self.dk, self.dv)
+        if ev: ev[1].record()
+
+    def e2e(self, steps: int, warmup: int):
+        torch = self.torch
+        hs = [t.cpu().pin_memory() for t in (self.q, self.k, self.v, self.o, self.do, self.lse)]
+        outs = [torch.empty_like(t).pin_memory() for t in hs[:3]]
+        dev = [torch.empty_like(t) for t in (self.q, self.k, self.v, self.o, self.do, self.lse)]
+        grads = [torch.empty_like(self.q) for _ in range(3)]
+
+        def fn():
+            for d, h in zip(dev, hs):
+                d.copy_(h, non_blocking=True)
+            self._call(*dev, *grads)
+            for h, d in zip(outs, grads):
+                h.copy_(d, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        ms = _e2e_time(torch, fn, steps, warmup)
+        h2d = sum(t.numel() * t.element_size() for t in hs)
+        d2h = sum(t.numel() * t.element_size() for t in outs)
+        return {"value": self.units_per_step() / (ms * 1e-3) / self.scale, "unit": self.unit,
+                "ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "amp_flash_attn_bwd_bf16_dev (host tensors copied in and out)"}
+
+    @classmethod
+    def cpu_reference(cls, args, budget_s: float, threads: int):
+        """No CPU backward exists in AMP: the fp64 chain-rule oracle on one head."""
+        from oracle import attention as ref
+        S, D = args.seq, 128
+        rng = np.random.default_rng(0)
+        q, k, v, do = (rng.standard_normal((1, 1, S, D)).astype(np.float32) for _ in range(4))
+        run = lambda: ref.flash_attn_bwd(q, k, v, do, True)
+        reps, dt = timed_reps(run, budget_s)
+        flops = 2.5 * 4.0 * D * S * (S + 1) / 2 * reps
+        return {"value": flops / dt / cls.scale, "unit": cls.unit, "cores": threads,
+                "kind": "port",
+                "sample": f"{reps} head(s) of S={S}, D={D} in {dt:.1f} s; fp64 numpy oracle "
+                          "(the reference has no backward)"}
+
+
 WORKLOADS = {w.name: w for w in (QuantWorkload, GemmWorkload, GemmFp8Workload,
-                                 AttentionWorkload, PagedDecodeWorkload, PagedPrefillWorkload)}
+                                 AttentionWorkload, AttentionBwdWorkload, PagedDecodeWorkload,
+                                 PagedPrefillWorkload)}
 
 
 def _e2e_time_stream(torch, fn, steps, warmup):

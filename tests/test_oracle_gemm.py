@@ -45,3 +45,24 @@ def test_restated_loop_is_bit_identical_to_reference_function(oracle_lib):
         mt = np.empty((M, N), np.float32)
         g.ref_cpu_reference_gemm_mt(A.ctypes.data, B.ctypes.data, mt.ctypes.data, M, N, K, 3)
         assert np.array_equal(mt.view(np.uint32), want.view(np.uint32))
+
+
+def test_attention_backward_oracle_matches_autograd():
+    """The fp64 chain-rule backward the GPU backward is checked against agrees with
+    torch autograd (an independent implementation) in fp64, causal and GQA."""
+    import torch
+    from oracle import attention as ref
+    rng = np.random.default_rng(0)
+    B, Hq, Hkv, S, D = 1, 4, 2, 37, 16
+    q, k, v, do = (rng.standard_normal(s) for s in
+                   ((B, Hq, S, D), (B, Hkv, S, D), (B, Hkv, S, D), (B, Hq, S, D)))
+    for causal in (True, False):
+        dq, dk, dv = ref.flash_attn_bwd(q, k, v, do, causal)
+        tq, tk, tv = (torch.tensor(x, requires_grad=True) for x in (q, k, v))
+        kk, vv = (t.repeat_interleave(Hq // Hkv, dim=1) for t in (tk, tv))
+        s = tq @ kk.transpose(-1, -2) / np.sqrt(D)
+        if causal:
+            s = s.masked_fill(torch.triu(torch.ones(S, S, dtype=torch.bool), 1), float("-inf"))
+        (torch.softmax(s, -1) @ vv).backward(torch.tensor(do))
+        for got, want in ((dq, tq.grad), (dk, tk.grad), (dv, tv.grad)):
+            assert np.abs(got - want.numpy()).max() < 1e-12
