@@ -16,6 +16,10 @@
 //   k_fa_bwd_dq    one CTA per (batch * query head, 128-query tile).  S = Q K^T,
 //                  dP = dO V^T with queries on the lanes; dS back over dP;
 //                  dQ += dS K over the visible key tiles.
+// Steps overlap: the element-wise warps write P (or P^T) first and dS after, so
+// the tensor core takes the next step's S^T while dS^T is computed (dK/dV pass:
+// dV_t, S^T_{t+1}, dK_t, dP^T_{t+1}); the dQ pass keeps two S buffers in TMEM
+// (S_{j+1}, dQ_j, dP_{j+1}).
 // Each pass recomputes P from lse, so there are no atomics and no fp32 dQ
 // accumulator in global memory.  Both kernels: warp 0 TMA, warp 1 TMEM + MMA
 // issue, warps 2-5 the element-wise work (one TMEM lane = one row per thread).
@@ -153,12 +157,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* kv_full = bars;
     uint64_t* qs_full = bars + 1;     // [2]
     uint64_t* qs_empty = bars + 3;    // [2]
-    uint64_t* sdp_full = bars + 5;
-    uint64_t* pds_full = bars + 6;
-    uint64_t* dkv_done = bars + 7;
-    uint64_t* drain = bars + 8;
-    uint64_t* cols_ready = bars + 9;  // [2]: the 128 element-wise threads posted lse2 / Delta
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+    uint64_t* s_full = bars + 5;      // S^T of the step in TMEM
+    uint64_t* dp_full = bars + 6;     // dP^T of the step in TMEM
+    uint64_t* p_full = bars + 7;      // P^T written back (4 warps)
+    uint64_t* ds_full = bars + 8;     // dS^T written back (4 warps)
+    uint64_t* dv_done = bars + 9;     // dV has read P^T: S^T may be rewritten
+    uint64_t* dk_done = bars + 10;    // dK has read dS^T: dP^T may be rewritten
+    uint64_t* drain = bars + 11;
+    uint64_t* cols_ready = bars + 12; // [2]: the 128 element-wise threads posted lse2 / Delta
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int jt = blockIdx.x, bh_kv = blockIdx.y;
@@ -180,9 +187,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&qs_full[s], 1);
             mbar_init(&qs_empty[s], 1);
         }
-        mbar_init(sdp_full, 1);
-        mbar_init(pds_full, 4);
-        mbar_init(dkv_done, 1);
+        mbar_init(s_full, 1);
+        mbar_init(dp_full, 1);
+        mbar_init(p_full, 4);
+        mbar_init(ds_full, 4);
+        mbar_init(dv_done, 1);
+        mbar_init(dk_done, 1);
         mbar_init(drain, 1);
         mbar_init(&cols_ready[0], 128);
         mbar_init(&cols_ready[1], 128);
@@ -226,24 +236,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0 && steps > 0) {
-            bool ok = mbar_wait(kv_full, 0, p.status);
+            // tensor-core order per step t:  dV_t, S^T_{t+1}, dK_t, dP^T_{t+1} -- so the
+            // next step's S^T runs while the element-wise warps compute dS^T_t
             const uint32_t ka = smem_u32(k_s), va = smem_u32(v_s);
+            auto qa = [&](int t) { return smem_u32(q_s + (t & 1) * CF::TILE); };
+            auto oa = [&](int t) { return smem_u32(o_s + (t & 1) * CF::TILE); };
+            bool ok = mbar_wait(kv_full, 0, p.status) && mbar_wait(&qs_full[0], 0, p.status);
+            if (ok) {
+                tc_fence_after();
+                mma_ss<D>(T_S, ka, qa(0));     // S^T_0 = K Q_0^T
+                tc_commit(s_full);
+                mma_ss<D>(T_dP, va, oa(0));    // dP^T_0 = V dO_0^T
+                tc_commit(dp_full);
+            }
             for (int t = 0; ok && t < steps; ++t) {
-                const int s = t & 1;
-                if (!mbar_wait(&qs_full[s], (t >> 1) & 1, p.status)) break;
-                // P^T / dS^T of step t-1 live in T_S / T_dP: dV/dK must have read them
-                if (t > 0 && !mbar_wait(dkv_done, (t - 1) & 1, p.status)) break;
+                const bool more = t + 1 < steps;
+                if (!mbar_wait(p_full, t & 1, p.status)) break;
                 tc_fence_after();
-                const uint32_t qa = smem_u32(q_s + s * CF::TILE), oa = smem_u32(o_s + s * CF::TILE);
-                mma_ss<D>(T_S, ka, qa);     // S^T = K Q^T
-                mma_ss<D>(T_dP, va, oa);    // dP^T = V dO^T
-                tc_commit(sdp_full);
-                if (!mbar_wait(pds_full, t & 1, p.status)) break;
+                mma_ts<D>(T_dV, T_S, oa(t), t != 0);    // dV += P^T dO
+                tc_commit(dv_done);
+                if (more) {
+                    if (!mbar_wait(&qs_full[(t + 1) & 1], ((t + 1) >> 1) & 1, p.status)) break;
+                    if (!mbar_wait(dv_done, t & 1, p.status)) break;   // P^T_t read
+                    tc_fence_after();
+                    mma_ss<D>(T_S, ka, qa(t + 1));
+                    tc_commit(s_full);
+                }
+                if (!mbar_wait(ds_full, t & 1, p.status)) break;
                 tc_fence_after();
-                mma_ts<D>(T_dV, T_S, oa, t != 0);    // dV += P^T dO
-                mma_ts<D>(T_dK, T_dP, qa, t != 0);   // dK += dS^T Q
-                tc_commit(&qs_empty[s]);
-                tc_commit(dkv_done);
+                mma_ts<D>(T_dK, T_dP, qa(t), t != 0);   // dK += dS^T Q
+                tc_commit(dk_done);
+                tc_commit(&qs_empty[t & 1]);
+                if (more) {
+                    if (!mbar_wait(dk_done, t & 1, p.status)) break;   // dS^T_t read
+                    tc_fence_after();
+                    mma_ss<D>(T_dP, va, oa(t + 1));
+                    tc_commit(dp_full);
+                }
             }
             tc_commit(drain);
             mbar_wait(drain, 0, p.status);
@@ -280,23 +309,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (t + 1 < steps) fetch(t + 1, nl2, ndl);
             const int it = i_lo + t % per_head;
             const int q0 = it * BT;
-            if (!mbar_wait_warp(sdp_full, t & 1, p.status)) { ok = false; break; }
+            // phase P (needs S^T only): P^T back over S^T, kept in registers as bf16
+            if (!mbar_wait_warp(s_full, t & 1, p.status)) { ok = false; break; }
             tc_fence_after();
+            uint32_t pw[2][32];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                uint32_t sv[2][32], dv[2][32];
+                uint32_t sv[2][32];
                 __syncwarp();
                 tmem_ld_32x32b_x32(T_S + lane_base + h * 64, sv[0]);
                 tmem_ld_32x32b_x32(T_S + lane_base + h * 64 + 32, sv[1]);
-                tmem_ld_32x32b_x32(T_dP + lane_base + h * 64, dv[0]);
-                tmem_ld_32x32b_x32(T_dP + lane_base + h * 64 + 32, dv[1]);
                 tmem_ld_wait();
-                uint32_t pw[32], dw[32];
 #pragma unroll
                 for (int e = 0; e < 64; e += 2) {
                     const int qc = h * 64 + e;            // query column within the tile
                     const float2 l2 = *reinterpret_cast<const float2*>(cl + qc);
-                    const float2 dl = *reinterpret_cast<const float2*>(cl + BT + qc);
                     const int q = q0 + qc;
                     const bool v0 = kj < p.S_kv && (!p.causal || kj <= q + p.causal_offset);
                     const bool v1 = kj < p.S_kv && (!p.causal || kj <= q + 1 + p.causal_offset);
@@ -304,20 +331,41 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float s1 = __uint_as_float(sv[e >> 5][(e & 31) + 1]);
                     const float p0 = v0 ? ex2_approx(fmaf(s0, c, -l2.x)) : 0.0f;
                     const float p1 = v1 ? ex2_approx(fmaf(s1, c, -l2.y)) : 0.0f;
-                    const float d0 = p0 * (__uint_as_float(dv[e >> 5][e & 31]) - dl.x);
-                    const float d1 = p1 * (__uint_as_float(dv[e >> 5][(e & 31) + 1]) - dl.y);
-                    pw[e >> 1] = f32x2_to_bf16x2(p0, p1);
+                    pw[h][e >> 1] = f32x2_to_bf16x2(p0, p1);
+                }
+                tmem_st_32x32b_x32(T_S + lane_base + h * 32, pw[h]);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+            // phase dS (needs dP^T): dS^T = P^T (dP^T - Delta) back over dP^T
+            if (!mbar_wait_warp(dp_full, t & 1, p.status)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t dv[2][32];
+                __syncwarp();
+                tmem_ld_32x32b_x32(T_dP + lane_base + h * 64, dv[0]);
+                tmem_ld_32x32b_x32(T_dP + lane_base + h * 64 + 32, dv[1]);
+                tmem_ld_wait();
+                uint32_t dw[32];
+#pragma unroll
+                for (int e = 0; e < 64; e += 2) {
+                    const float2 dl = *reinterpret_cast<const float2*>(cl + BT + h * 64 + e);
+                    const uint32_t pp = pw[h][e >> 1];
+                    const float d0 = bf16_lo(pp) * (__uint_as_float(dv[e >> 5][e & 31]) - dl.x);
+                    const float d1 = bf16_hi(pp) * (__uint_as_float(dv[e >> 5][(e & 31) + 1]) - dl.y);
                     dw[e >> 1] = f32x2_to_bf16x2(d0, d1);
                 }
-                // P^T over S^T, dS^T over dP^T (columns of this half were read above)
-                tmem_st_32x32b_x32(T_S + lane_base + h * 32, pw);
                 tmem_st_32x32b_x32(T_dP + lane_base + h * 32, dw);
             }
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(pds_full);
+            if (lane == 0) mbar_arrive(ds_full);
         }
+
         // epilogue: dK = scale * acc, dV = acc
         __nv_bfloat16* dk_row = static_cast<__nv_bfloat16*>(p.dk) + ((int64_t)bh_kv * p.S_kv + (kj < p.S_kv ? kj : 0)) * D;
         __nv_bfloat16* dv_row = static_cast<__nv_bfloat16*>(p.dv) + ((int64_t)bh_kv * p.S_kv + (kj < p.S_kv ? kj : 0)) * D;
@@ -326,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 store_zero_row<D>(dk_row);
                 store_zero_row<D>(dv_row);
             }
-        } else if (ok && mbar_wait_warp(dkv_done, (steps - 1) & 1, p.status)) {
+        } else if (ok && mbar_wait_warp(dk_done, (steps - 1) & 1, p.status)) {
             tc_fence_after();
             store_row<D>(T_dK + lane_base, p.scale, dk_row, kj < p.S_kv);
             store_row<D>(T_dV + lane_base, 1.0f, dv_row, kj < p.S_kv);
@@ -361,11 +409,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* k_empty = bars + 3;     // [2]
     uint64_t* v_full = bars + 5;      // [2]
     uint64_t* v_empty = bars + 7;     // [2]
-    uint64_t* sdp_full = bars + 9;
-    uint64_t* ds_full = bars + 10;
-    uint64_t* dq_done = bars + 11;
-    uint64_t* drain = bars + 12;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+    uint64_t* s_full = bars + 9;      // [2]: S of step j in TMEM buffer j & 1
+    uint64_t* dp_full = bars + 11;
+    uint64_t* ds_full = bars + 12;
+    uint64_t* dq_done = bars + 13;    // dQ has read dS: dP may be rewritten
+    uint64_t* drain = bars + 14;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_qt = (p.S_q + BT - 1) / BT;
@@ -388,7 +437,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&v_full[s], 1);
             mbar_init(&v_empty[s], 1);
         }
-        mbar_init(sdp_full, 1);
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
+        mbar_init(dp_full, 1);
         mbar_init(ds_full, 4);
         mbar_init(dq_done, 1);
         mbar_init(drain, 1);
@@ -403,7 +454,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t T_S = tmem, T_dP = tmem + BT, T_dQ = tmem + 2 * BT;
+    // two S buffers, so that the next step's S = Q K^T runs during this step
+    const uint32_t T_S = tmem, T_dP = tmem + 2 * BT, T_dQ = tmem + 3 * BT;
 
     if (warp == 0) {
         if (lane == 0 && n_kv > 0) {
@@ -434,26 +486,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0 && n_kv > 0) {
-            bool ok = mbar_wait(q_full, 0, p.status);
+            // tensor-core order per step j:  S_{j+1}, dQ_j, dP_{j+1}
             const uint32_t qa = smem_u32(q_s), oa = smem_u32(o_s);
-            for (int j = 0; ok && j < n_kv; ++j) {
-                const int s = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(&k_full[s], ph, p.status) || !mbar_wait(&v_full[s], ph, p.status))
-                    break;
-                // dS of step j-1 lives in T_dP: dQ must have read it
-                if (j > 0 && !mbar_wait(dq_done, (j - 1) & 1, p.status)) break;
+            auto ka = [&](int j) { return smem_u32(k_s + (j & 1) * CF::TILE); };
+            auto va = [&](int j) { return smem_u32(v_s + (j & 1) * CF::TILE); };
+            bool ok = mbar_wait(q_full, 0, p.status) && mbar_wait(&k_full[0], 0, p.status) &&
+                      mbar_wait(&v_full[0], 0, p.status);
+            if (ok) {
                 tc_fence_after();
-                const uint32_t ka = smem_u32(k_s + s * CF::TILE), va = smem_u32(v_s + s * CF::TILE);
-                mma_ss<D>(T_S, qa, ka);     // S = Q K^T
-                mma_ss<D>(T_dP, oa, va);    // dP = dO V^T
-                tc_commit(&v_empty[s]);
-                tc_commit(sdp_full);
+                mma_ss<D>(T_S, qa, ka(0));     // S_0 = Q K_0^T
+                tc_commit(&s_full[0]);
+                mma_ss<D>(T_dP, oa, va(0));    // dP_0 = dO V_0^T
+                tc_commit(&v_empty[0]);
+                tc_commit(dp_full);
+            }
+            for (int j = 0; ok && j < n_kv; ++j) {
+                const bool more = j + 1 < n_kv;
+                const int n1 = (j + 1) & 1;
+                const uint32_t ph1 = ((j + 1) >> 1) & 1;
+                if (more) {   // S buffer n1 held S_{j-1}, read before ds_full(j-1)
+                    if (!mbar_wait(&k_full[n1], ph1, p.status)) break;
+                    tc_fence_after();
+                    mma_ss<D>(T_S + n1 * BT, qa, ka(j + 1));
+                    tc_commit(&s_full[n1]);
+                }
                 if (!mbar_wait(ds_full, j & 1, p.status)) break;
                 tc_fence_after();
-                mma_ts<D>(T_dQ, T_dP, ka, j != 0);   // dQ += dS K
-                tc_commit(&k_empty[s]);
+                mma_ts<D>(T_dQ, T_dP, ka(j), j != 0);   // dQ += dS K
                 tc_commit(dq_done);
+                tc_commit(&k_empty[j & 1]);
+                if (more) {
+                    if (!mbar_wait(&v_full[n1], ph1, p.status)) break;
+                    if (!mbar_wait(dq_done, j & 1, p.status)) break;   // dS_j read
+                    tc_fence_after();
+                    mma_ss<D>(T_dP, oa, va(j + 1));
+                    tc_commit(&v_empty[n1]);
+                    tc_commit(dp_full);
+                }
             }
             tc_commit(drain);
             mbar_wait(drain, 0, p.status);
@@ -472,27 +541,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int vis_hi = p.causal ? min(p.S_kv - 1, qi + p.causal_offset) : p.S_kv - 1;
         bool ok = true;
         for (int j = 0; j < n_kv; ++j) {
-            if (!mbar_wait_warp(sdp_full, j & 1, p.status)) { ok = false; break; }
+            // phase P (needs S only), kept in registers as bf16
+            if (!mbar_wait_warp(&s_full[j & 1], (j >> 1) & 1, p.status)) { ok = false; break; }
             tc_fence_after();
+            const uint32_t sb = T_S + (j & 1) * BT;
+            uint32_t pw[2][32];
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-                uint32_t sv[2][32], dv[2][32];
+                uint32_t sv[2][32];
                 __syncwarp();
-                tmem_ld_32x32b_x32(T_S + lane_base + hh * 64, sv[0]);
-                tmem_ld_32x32b_x32(T_S + lane_base + hh * 64 + 32, sv[1]);
-                tmem_ld_32x32b_x32(T_dP + lane_base + hh * 64, dv[0]);
-                tmem_ld_32x32b_x32(T_dP + lane_base + hh * 64 + 32, dv[1]);
+                tmem_ld_32x32b_x32(sb + lane_base + hh * 64, sv[0]);
+                tmem_ld_32x32b_x32(sb + lane_base + hh * 64 + 32, sv[1]);
                 tmem_ld_wait();
                 const int kb = j * BT + hh * 64;
-                uint32_t dw[32];
 #pragma unroll
                 for (int e = 0; e < 64; e += 2) {
                     const float s0 = __uint_as_float(sv[e >> 5][e & 31]);
                     const float s1 = __uint_as_float(sv[e >> 5][(e & 31) + 1]);
                     const float p0 = kb + e <= vis_hi ? ex2_approx(fmaf(s0, c, -l2)) : 0.0f;
                     const float p1 = kb + e + 1 <= vis_hi ? ex2_approx(fmaf(s1, c, -l2)) : 0.0f;
-                    const float d0 = p0 * (__uint_as_float(dv[e >> 5][e & 31]) - dl);
-                    const float d1 = p1 * (__uint_as_float(dv[e >> 5][(e & 31) + 1]) - dl);
+                    pw[hh][e >> 1] = f32x2_to_bf16x2(p0, p1);
+                }
+            }
+            // phase dS (needs dP): dS = P (dP - Delta) back over dP
+            if (!mbar_wait_warp(dp_full, j & 1, p.status)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t dv[2][32];
+                __syncwarp();
+                tmem_ld_32x32b_x32(T_dP + lane_base + hh * 64, dv[0]);
+                tmem_ld_32x32b_x32(T_dP + lane_base + hh * 64 + 32, dv[1]);
+                tmem_ld_wait();
+                uint32_t dw[32];
+#pragma unroll
+                for (int e = 0; e < 64; e += 2) {
+                    const uint32_t pp = pw[hh][e >> 1];
+                    const float d0 = bf16_lo(pp) * (__uint_as_float(dv[e >> 5][e & 31]) - dl);
+                    const float d1 = bf16_hi(pp) * (__uint_as_float(dv[e >> 5][(e & 31) + 1]) - dl);
                     dw[e >> 1] = f32x2_to_bf16x2(d0, d1);
                 }
                 tmem_st_32x32b_x32(T_dP + lane_base + hh * 32, dw);   // dS over dP
@@ -502,6 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(ds_full);
         }
+
         __nv_bfloat16* dq_row = static_cast<__nv_bfloat16*>(p.dq) + ((int64_t)bh * p.S_q + (qi < p.S_q ? qi : 0)) * D;
         if (n_kv == 0) {
             if (qi < p.S_q) store_zero_row<D>(dq_row);
