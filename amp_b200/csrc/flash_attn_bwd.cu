@@ -21,8 +21,10 @@
 // dV_t, S^T_{t+1}, dK_t, dP^T_{t+1}); the dQ pass keeps two S buffers in TMEM
 // (S_{j+1}, dQ_j, dP_{j+1}).
 // Each pass recomputes P from lse, so there are no atomics and no fp32 dQ
-// accumulator in global memory.  Both kernels: warp 0 TMA, warp 1 TMEM + MMA
-// issue, warps 2-5 the element-wise work (one TMEM lane = one row per thread).
+// accumulator in global memory.  Both kernels: 384 threads; warp 0 TMA, warp 1
+// TMEM + MMA issue (warps 2-3 only lend their registers, setmaxnreg 72 / 216);
+// warps 4-11 the element-wise work, two warps per TMEM lane quadrant (one row
+// per thread), each taking one 64-column half of the 128-column tile.
 #include <cuda.h>
 
 #include <algorithm>
@@ -40,7 +42,10 @@ int fa_make_tmap_3d(CUtensorMap* m, const void* base, int64_t d, int64_t s, int6
 namespace {
 
 constexpr int BT = 128;                 // rows per query / key tile
-constexpr int kThreads = 192;
+constexpr int kThreads = 384;      // 3 warpgroups
+// Register split: 128 * 72 + 256 * 216 == 384 * 168, the launch's allocation
+// (__launch_bounds__(384, 1) compiles for exactly 168).
+constexpr int kRegCtl = 72, kRegEw = 216;
 constexpr int SLAB_BYTES = 128 * 128;   // [128 rows x 128 bytes] swizzled slab
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -74,13 +79,17 @@ __device__ __forceinline__ void mma_ss(uint32_t acc, uint32_t a_addr, uint32_t b
                    smem_desc_sw128(b_addr + off, 16, 1024), BwdCfg<D>::IDESC_SS, kk != 0);
     }
 }
-// TS product: acc[128 x D] (+)= T[128 x 128] (bf16 in TMEM) x B[128 rows x D] (MN-major)
+// TS product: acc[128 x D] (+)= T[128 x 128] (bf16 in TMEM) x B[128 rows x D] (MN-major).
+// T is packed two bf16 per column in two halves: its columns 0-63 at TMEM
+// columns [t_col, t_col + 32), 64-127 at [t_col + 96, t_col + 128) -- where the
+// two element-wise warps of a lane quadrant write them (see the element-wise code).
 template <int D>
 __device__ __forceinline__ void mma_ts(uint32_t acc, uint32_t t_col, uint32_t b_addr,
                                        bool accumulate) {
 #pragma unroll
     for (int kk = 0; kk < BT / 16; ++kk)
-        tc_mma_f16_ts(acc, t_col + kk * 8, smem_desc_sw128(b_addr + kk * 16 * 128, SLAB_BYTES, 1024),
+        tc_mma_f16_ts(acc, t_col + kk * 8 + (kk >= BT / 32 ? BT / 2 : 0),
+                      smem_desc_sw128(b_addr + kk * 16 * 128, SLAB_BYTES, 1024),
                       BwdCfg<D>::IDESC_TS, (accumulate || kk != 0) ? 1u : 0u);
 }
 
@@ -108,13 +117,15 @@ __global__ void __launch_bounds__(256) k_fa_bwd_delta(const __nv_bfloat16* __res
     }
 }
 
-// store one 128 x D fp32 TMEM accumulator row (this thread's lane) as bf16 * mul
+// store columns [half * D/2, half * D/2 + D/2) of one 128 x D fp32 TMEM
+// accumulator row (this thread's lane) as bf16 * mul
 template <int D>
 __device__ __forceinline__ void store_row(uint32_t lane_addr, float mul, __nv_bfloat16* row,
-                                          bool ok) {
+                                          bool ok, int half) {
     __syncwarp();
 #pragma unroll
-    for (int oc = 0; oc < D / 32; ++oc) {
+    for (int ocl = 0; ocl < D / 64; ++ocl) {
+        const int oc = half * (D / 64) + ocl;
         uint32_t v[32];
         tmem_ld_32x32b_x32(lane_addr + oc * 32, v);
         tmem_ld_wait();
@@ -133,9 +144,10 @@ __device__ __forceinline__ void store_row(uint32_t lane_addr, float mul, __nv_bf
 }
 
 template <int D>
-__device__ __forceinline__ void store_zero_row(__nv_bfloat16* row) {
+__device__ __forceinline__ void store_zero_row(__nv_bfloat16* row, int half) {
 #pragma unroll
-    for (int e = 0; e < D; e += 8) *reinterpret_cast<uint4*>(row + e) = make_uint4(0u, 0u, 0u, 0u);
+    for (int e = half * (D / 2); e < (half + 1) * (D / 2); e += 8)
+        *reinterpret_cast<uint4*>(row + e) = make_uint4(0u, 0u, 0u, 0u);
 }
 
 // ---------------------------------------------------------------- dK, dV
@@ -159,12 +171,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* qs_empty = bars + 3;    // [2]
     uint64_t* s_full = bars + 5;      // S^T of the step in TMEM
     uint64_t* dp_full = bars + 6;     // dP^T of the step in TMEM
-    uint64_t* p_full = bars + 7;      // P^T written back (4 warps)
-    uint64_t* ds_full = bars + 8;     // dS^T written back (4 warps)
+    uint64_t* p_full = bars + 7;      // P^T written back (8 warps)
+    uint64_t* ds_full = bars + 8;     // dS^T written back (8 warps)
     uint64_t* dv_done = bars + 9;     // dV has read P^T: S^T may be rewritten
     uint64_t* dk_done = bars + 10;    // dK has read dS^T: dP^T may be rewritten
     uint64_t* drain = bars + 11;
-    uint64_t* cols_ready = bars + 12; // [2]: the 128 element-wise threads posted lse2 / Delta
+    uint64_t* cols_ready = bars + 12; // [2]: the 256 element-wise threads posted the step
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -189,13 +201,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(s_full, 1);
         mbar_init(dp_full, 1);
-        mbar_init(p_full, 4);
-        mbar_init(ds_full, 4);
+        mbar_init(p_full, 8);
+        mbar_init(ds_full, 8);
         mbar_init(dv_done, 1);
         mbar_init(dk_done, 1);
         mbar_init(drain, 1);
-        mbar_init(&cols_ready[0], 128);
-        mbar_init(&cols_ready[1], 128);
+        mbar_init(&cols_ready[0], 256);
+        mbar_init(&cols_ready[1], 256);
         fence_barrier_init();
         fence_proxy_async_smem();
     }
@@ -209,6 +221,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
     const uint32_t T_S = tmem, T_dP = tmem + BT, T_dV = tmem + 2 * BT, T_dK = tmem + 2 * BT + D;
 
+    if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegCtl));
     if (warp == 0) {
         if (lane == 0 && steps > 0) {
             tma_prefetch_desc(&tmQ);
@@ -277,64 +291,81 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_commit(drain);
             mbar_wait(drain, 0, p.status);
         }
+    }
     } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegEw));
         // ---------------------------------------------------- element-wise
-        const int quad = warp & 3;
-        const int tid = threadIdx.x - 64;             // 0..127
+        // Two warps per lane quadrant: `half` takes query columns [64 half, 64 half + 64)
+        // of the tile.  P^T / dS^T of half 0 are packed into TMEM columns [0, 32) of
+        // their region, of half 1 into [96, 128), so each half overwrites only columns
+        // it has already read itself (mma_ts reads that layout).
+        const int quad = warp & 3, half = (warp - 4) >> 2;
+        const int tid = threadIdx.x - 128;            // 0..255
         const int kr = quad * 32 + lane;              // key row == TMEM lane
         const int kj = k0 + kr;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-        const float c = p.scale_log2;
+        const uint32_t src_col = half * 64, dst_col = half ? 96 : 0;
+        const uint64_t c2 = f2pack(p.scale_log2, p.scale_log2);
         bool ok = true;
-        // lse2 / Delta of the next step's query tile, one query per thread
-        auto fetch = [&](int t, float& l2, float& dl) {
+        // -lse2 / -Delta of query `tid` of step t's tile (threads tid < 128)
+        auto fetch = [&](int t, float& nl2, float& ndl) {
             const int g = t / per_head, it = i_lo + t % per_head;
             const int q = it * BT + tid;
             const int64_t row = (int64_t)(b * p.Hq + hk * G + g) * p.S_q + q;
             const float lse = q < p.S_q ? p.lse[row] : -INFINITY;
-            l2 = lse == -INFINITY ? INFINITY : lse * kLog2e;   // +inf: the column's P is 0
-            dl = q < p.S_q ? p.delta[row] : 0.0f;
+            nl2 = lse == -INFINITY ? -INFINITY : -lse * kLog2e;   // -inf: the column's P is 0
+            ndl = q < p.S_q ? -p.delta[row] : 0.0f;
         };
         float nl2 = 0.0f, ndl = 0.0f;
-        if (steps > 0) fetch(0, nl2, ndl);
+        if (steps > 0 && tid < BT) fetch(0, nl2, ndl);
         for (int t = 0; t < steps; ++t) {
-            // [lse2 | Delta] of this step's query tile, one value per thread; a buffer
-            // is rewritten two steps later, after every thread has posted the step
-            // in between (so it has finished reading this one)
+            // [-lse2 | -Delta] of this step's query tile; a buffer is rewritten two
+            // steps later, after all 256 threads have posted the step in between (so
+            // every thread has finished reading this one)
             float* cl = cols + (t & 1) * 2 * BT;
-            cl[tid] = nl2;
-            cl[BT + tid] = ndl;
+            if (tid < BT) {
+                cl[tid] = nl2;
+                cl[BT + tid] = ndl;
+            }
             mbar_arrive(&cols_ready[t & 1]);
             if (!mbar_wait_warp(&cols_ready[t & 1], (t >> 1) & 1, p.status)) { ok = false; break; }
-            if (t + 1 < steps) fetch(t + 1, nl2, ndl);
-            const int it = i_lo + t % per_head;
-            const int q0 = it * BT;
-            // phase P (needs S^T only): P^T back over S^T, kept in registers as bf16
+            if (t + 1 < steps && tid < BT) fetch(t + 1, nl2, ndl);
+            // key kj sees query q iff kj <= q + causal_offset: this half's columns
+            // e < lo are masked (q = q0 + e)
+            const int q0 = (i_lo + t % per_head) * BT + half * 64;
+            int lo = 0;
+            if (kj >= p.S_kv) lo = 64;
+            else if (p.causal) lo = min(64, max(0, kj - p.causal_offset - q0));
+            const bool dense = __all_sync(0xffffffffu, lo == 0);
+            const float* hcl = cl + half * 64;
+            // phase P (needs S^T only): P^T = exp2(S^T c - lse2), kept as bf16 pairs
             if (!mbar_wait_warp(s_full, t & 1, p.status)) { ok = false; break; }
             tc_fence_after();
-            uint32_t pw[2][32];
+            uint32_t sv[2][32];
+            __syncwarp();
+            tmem_ld_32x32b_x32(T_S + lane_base + src_col, sv[0]);
+            tmem_ld_32x32b_x32(T_S + lane_base + src_col + 32, sv[1]);
+            tmem_ld_wait();
+            uint32_t pw[32];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t sv[2][32];
-                __syncwarp();
-                tmem_ld_32x32b_x32(T_S + lane_base + h * 64, sv[0]);
-                tmem_ld_32x32b_x32(T_S + lane_base + h * 64 + 32, sv[1]);
-                tmem_ld_wait();
+            for (int e = 0; e < 64; e += 4) {
+                const float4 l4 = *reinterpret_cast<const float4*>(hcl + e);
 #pragma unroll
-                for (int e = 0; e < 64; e += 2) {
-                    const int qc = h * 64 + e;            // query column within the tile
-                    const float2 l2 = *reinterpret_cast<const float2*>(cl + qc);
-                    const int q = q0 + qc;
-                    const bool v0 = kj < p.S_kv && (!p.causal || kj <= q + p.causal_offset);
-                    const bool v1 = kj < p.S_kv && (!p.causal || kj <= q + 1 + p.causal_offset);
-                    const float s0 = __uint_as_float(sv[e >> 5][e & 31]);
-                    const float s1 = __uint_as_float(sv[e >> 5][(e & 31) + 1]);
-                    const float p0 = v0 ? ex2_approx(fmaf(s0, c, -l2.x)) : 0.0f;
-                    const float p1 = v1 ? ex2_approx(fmaf(s1, c, -l2.y)) : 0.0f;
-                    pw[h][e >> 1] = f32x2_to_bf16x2(p0, p1);
+                for (int u = 0; u < 4; u += 2) {
+                    const int ee = e + u;
+                    const uint64_t x2 = ffma2(f2pack(__uint_as_float(sv[ee >> 5][ee & 31]),
+                                                     __uint_as_float(sv[ee >> 5][(ee & 31) + 1])),
+                                              c2, u ? f2pack(l4.z, l4.w) : f2pack(l4.x, l4.y));
+                    float x0, x1;
+                    f2unpack(x2, x0, x1);
+                    if (!dense) {
+                        x0 = ee >= lo ? x0 : -INFINITY;
+                        x1 = ee + 1 >= lo ? x1 : -INFINITY;
+                    }
+                    pw[ee >> 1] = f32x2_to_bf16x2(ex2_approx(x0), ex2_approx(x1));
                 }
-                tmem_st_32x32b_x32(T_S + lane_base + h * 32, pw[h]);
             }
+            tmem_st_32x32b_x32(T_S + lane_base + dst_col, pw);
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
@@ -342,42 +373,45 @@ __global__ void __launch_bounds__(kThreads, 1)
             // phase dS (needs dP^T): dS^T = P^T (dP^T - Delta) back over dP^T
             if (!mbar_wait_warp(dp_full, t & 1, p.status)) { ok = false; break; }
             tc_fence_after();
+            __syncwarp();
+            tmem_ld_32x32b_x32(T_dP + lane_base + src_col, sv[0]);
+            tmem_ld_32x32b_x32(T_dP + lane_base + src_col + 32, sv[1]);
+            tmem_ld_wait();
+            uint32_t dw[32];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t dv[2][32];
-                __syncwarp();
-                tmem_ld_32x32b_x32(T_dP + lane_base + h * 64, dv[0]);
-                tmem_ld_32x32b_x32(T_dP + lane_base + h * 64 + 32, dv[1]);
-                tmem_ld_wait();
-                uint32_t dw[32];
+            for (int e = 0; e < 64; e += 4) {
+                const float4 d4 = *reinterpret_cast<const float4*>(hcl + BT + e);
 #pragma unroll
-                for (int e = 0; e < 64; e += 2) {
-                    const float2 dl = *reinterpret_cast<const float2*>(cl + BT + h * 64 + e);
-                    const uint32_t pp = pw[h][e >> 1];
-                    const float d0 = bf16_lo(pp) * (__uint_as_float(dv[e >> 5][e & 31]) - dl.x);
-                    const float d1 = bf16_hi(pp) * (__uint_as_float(dv[e >> 5][(e & 31) + 1]) - dl.y);
-                    dw[e >> 1] = f32x2_to_bf16x2(d0, d1);
+                for (int u = 0; u < 4; u += 2) {
+                    const int ee = e + u;
+                    const uint32_t pp = pw[ee >> 1];
+                    const uint64_t g2 = fadd2(f2pack(__uint_as_float(sv[ee >> 5][ee & 31]),
+                                                     __uint_as_float(sv[ee >> 5][(ee & 31) + 1])),
+                                              u ? f2pack(d4.z, d4.w) : f2pack(d4.x, d4.y));
+                    float d0, d1;
+                    f2unpack(fmul2(f2pack(bf16_lo(pp), bf16_hi(pp)), g2), d0, d1);
+                    dw[ee >> 1] = f32x2_to_bf16x2(d0, d1);
                 }
-                tmem_st_32x32b_x32(T_dP + lane_base + h * 32, dw);
             }
+            tmem_st_32x32b_x32(T_dP + lane_base + dst_col, dw);
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(ds_full);
         }
 
-        // epilogue: dK = scale * acc, dV = acc
+        // epilogue: dK = scale * acc, dV = acc (each half stores half of the columns)
         __nv_bfloat16* dk_row = static_cast<__nv_bfloat16*>(p.dk) + ((int64_t)bh_kv * p.S_kv + (kj < p.S_kv ? kj : 0)) * D;
         __nv_bfloat16* dv_row = static_cast<__nv_bfloat16*>(p.dv) + ((int64_t)bh_kv * p.S_kv + (kj < p.S_kv ? kj : 0)) * D;
         if (steps == 0) {
             if (kj < p.S_kv) {
-                store_zero_row<D>(dk_row);
-                store_zero_row<D>(dv_row);
+                store_zero_row<D>(dk_row, half);
+                store_zero_row<D>(dv_row, half);
             }
         } else if (ok && mbar_wait_warp(dk_done, (steps - 1) & 1, p.status)) {
             tc_fence_after();
-            store_row<D>(T_dK + lane_base, p.scale, dk_row, kj < p.S_kv);
-            store_row<D>(T_dV + lane_base, 1.0f, dv_row, kj < p.S_kv);
+            store_row<D>(T_dK + lane_base, p.scale, dk_row, kj < p.S_kv, half);
+            store_row<D>(T_dV + lane_base, 1.0f, dv_row, kj < p.S_kv, half);
         }
     }
 
@@ -440,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&s_full[0], 1);
         mbar_init(&s_full[1], 1);
         mbar_init(dp_full, 1);
-        mbar_init(ds_full, 4);
+        mbar_init(ds_full, 8);
         mbar_init(dq_done, 1);
         mbar_init(drain, 1);
         fence_barrier_init();
@@ -457,6 +491,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // two S buffers, so that the next step's S = Q K^T runs during this step
     const uint32_t T_S = tmem, T_dP = tmem + 2 * BT, T_dQ = tmem + 3 * BT;
 
+    if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegCtl));
     if (warp == 0) {
         if (lane == 0 && n_kv > 0) {
             tma_prefetch_desc(&tmK);
@@ -527,62 +563,72 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_commit(drain);
             mbar_wait(drain, 0, p.status);
         }
+    }
     } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegEw));
         // ---------------------------------------------------- element-wise
-        const int quad = warp & 3;
+        // Two warps per lane quadrant: `half` takes key columns [64 half, 64 half + 64);
+        // dS of half 0 is packed into TMEM columns [0, 32) of the dP region, of half 1
+        // into [96, 128) (the layout mma_ts reads).
+        const int quad = warp & 3, half = (warp - 4) >> 2;
         const int r = quad * 32 + lane;               // query row == TMEM lane
         const int qi = q0 + r;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-        const float c = p.scale_log2;
+        const uint32_t src_col = half * 64, dst_col = half ? 96 : 0;
+        const uint64_t c2 = f2pack(p.scale_log2, p.scale_log2);
         const int64_t row = (int64_t)bh * p.S_q + qi;
         const float lse = qi < p.S_q ? p.lse[row] : -INFINITY;
-        const float l2 = lse == -INFINITY ? INFINITY : lse * kLog2e;   // +inf: P = 0
-        const float dl = qi < p.S_q ? p.delta[row] : 0.0f;
+        const float nl2 = lse == -INFINITY ? -INFINITY : -lse * kLog2e;   // -inf: P = 0
+        const float ndl = qi < p.S_q ? -p.delta[row] : 0.0f;
+        const uint64_t nl2x2 = f2pack(nl2, nl2), ndlx2 = f2pack(ndl, ndl);
         const int vis_hi = p.causal ? min(p.S_kv - 1, qi + p.causal_offset) : p.S_kv - 1;
         bool ok = true;
         for (int j = 0; j < n_kv; ++j) {
-            // phase P (needs S only), kept in registers as bf16
+            // this half's key columns e > hi are masked
+            const int hi = vis_hi - (j * BT + half * 64);
+            const bool dense = __all_sync(0xffffffffu, hi >= 63);
+            // phase P (needs S only), kept in registers as bf16 pairs
             if (!mbar_wait_warp(&s_full[j & 1], (j >> 1) & 1, p.status)) { ok = false; break; }
             tc_fence_after();
             const uint32_t sb = T_S + (j & 1) * BT;
-            uint32_t pw[2][32];
+            uint32_t sv[2][32];
+            __syncwarp();
+            tmem_ld_32x32b_x32(sb + lane_base + src_col, sv[0]);
+            tmem_ld_32x32b_x32(sb + lane_base + src_col + 32, sv[1]);
+            tmem_ld_wait();
+            uint32_t pw[32];
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                uint32_t sv[2][32];
-                __syncwarp();
-                tmem_ld_32x32b_x32(sb + lane_base + hh * 64, sv[0]);
-                tmem_ld_32x32b_x32(sb + lane_base + hh * 64 + 32, sv[1]);
-                tmem_ld_wait();
-                const int kb = j * BT + hh * 64;
-#pragma unroll
-                for (int e = 0; e < 64; e += 2) {
-                    const float s0 = __uint_as_float(sv[e >> 5][e & 31]);
-                    const float s1 = __uint_as_float(sv[e >> 5][(e & 31) + 1]);
-                    const float p0 = kb + e <= vis_hi ? ex2_approx(fmaf(s0, c, -l2)) : 0.0f;
-                    const float p1 = kb + e + 1 <= vis_hi ? ex2_approx(fmaf(s1, c, -l2)) : 0.0f;
-                    pw[hh][e >> 1] = f32x2_to_bf16x2(p0, p1);
+            for (int e = 0; e < 64; e += 2) {
+                const uint64_t x2 = ffma2(f2pack(__uint_as_float(sv[e >> 5][e & 31]),
+                                                 __uint_as_float(sv[e >> 5][(e & 31) + 1])),
+                                          c2, nl2x2);
+                float x0, x1;
+                f2unpack(x2, x0, x1);
+                if (!dense) {
+                    x0 = e <= hi ? x0 : -INFINITY;
+                    x1 = e + 1 <= hi ? x1 : -INFINITY;
                 }
+                pw[e >> 1] = f32x2_to_bf16x2(ex2_approx(x0), ex2_approx(x1));
             }
             // phase dS (needs dP): dS = P (dP - Delta) back over dP
             if (!mbar_wait_warp(dp_full, j & 1, p.status)) { ok = false; break; }
             tc_fence_after();
+            __syncwarp();
+            tmem_ld_32x32b_x32(T_dP + lane_base + src_col, sv[0]);
+            tmem_ld_32x32b_x32(T_dP + lane_base + src_col + 32, sv[1]);
+            tmem_ld_wait();
+            uint32_t dw[32];
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                uint32_t dv[2][32];
-                __syncwarp();
-                tmem_ld_32x32b_x32(T_dP + lane_base + hh * 64, dv[0]);
-                tmem_ld_32x32b_x32(T_dP + lane_base + hh * 64 + 32, dv[1]);
-                tmem_ld_wait();
-                uint32_t dw[32];
-#pragma unroll
-                for (int e = 0; e < 64; e += 2) {
-                    const uint32_t pp = pw[hh][e >> 1];
-                    const float d0 = bf16_lo(pp) * (__uint_as_float(dv[e >> 5][e & 31]) - dl);
-                    const float d1 = bf16_hi(pp) * (__uint_as_float(dv[e >> 5][(e & 31) + 1]) - dl);
-                    dw[e >> 1] = f32x2_to_bf16x2(d0, d1);
-                }
-                tmem_st_32x32b_x32(T_dP + lane_base + hh * 32, dw);   // dS over dP
+            for (int e = 0; e < 64; e += 2) {
+                const uint32_t pp = pw[e >> 1];
+                const uint64_t g2 = fadd2(f2pack(__uint_as_float(sv[e >> 5][e & 31]),
+                                                 __uint_as_float(sv[e >> 5][(e & 31) + 1])),
+                                          ndlx2);
+                float d0, d1;
+                f2unpack(fmul2(f2pack(bf16_lo(pp), bf16_hi(pp)), g2), d0, d1);
+                dw[e >> 1] = f32x2_to_bf16x2(d0, d1);
             }
+            tmem_st_32x32b_x32(T_dP + lane_base + dst_col, dw);   // dS over dP
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
@@ -591,10 +637,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
         __nv_bfloat16* dq_row = static_cast<__nv_bfloat16*>(p.dq) + ((int64_t)bh * p.S_q + (qi < p.S_q ? qi : 0)) * D;
         if (n_kv == 0) {
-            if (qi < p.S_q) store_zero_row<D>(dq_row);
+            if (qi < p.S_q) store_zero_row<D>(dq_row, half);
         } else if (ok && mbar_wait_warp(dq_done, (n_kv - 1) & 1, p.status)) {
             tc_fence_after();
-            store_row<D>(T_dQ + lane_base, p.scale, dq_row, qi < p.S_q);
+            store_row<D>(T_dQ + lane_base, p.scale, dq_row, qi < p.S_q, half);
         }
     }
 

@@ -264,6 +264,32 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
+// ----------------------------------------------------------------- f32x2
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes).
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 // ----------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor (sm_100 "version 1" format) for a 128-byte
 // swizzled canonical layout.  Fields: start address >> 4 in bits [0,14),
