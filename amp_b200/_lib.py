@@ -34,6 +34,10 @@ SIGNATURES: dict[str, tuple] = {
     "amp_gemm_fp8e4m3_dev": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _vp]),
     "amp_gemm_fp8e4m3_ex_dev": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _vp, _i32, _i32,
                                        _i32, _vp]),
+    "amp_gemm_bf16_allgather_dev": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp, C.c_uint, _i32,
+                                           _i32, _i32, _vp]),
+    "amp_gemm_fp8e4m3_allgather_dev": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _vp,
+                                              C.c_uint, _i32, _i32, _i32, _vp]),
     "amp_user_gemm_bf16": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32]),
     "amp_user_gemm_fp8e4m3": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32]),
     "amp_flash_attn_fwd_bf16_dev": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
@@ -58,6 +62,7 @@ SIGNATURES: dict[str, tuple] = {
     "amp_peer_handle_bytes": (_i32, []),
     "amp_peer_mailbox_create": (_i32, [_vp, _vp]),
     "amp_peer_mailbox_open": (_i32, [_vp, _vp]),
+    "amp_peer_buffer_create": (_i32, [_sz, _vp, _vp]),
     "amp_peer_mailbox_close": (_i32, [_vp]),
     "amp_peer_mailbox_free": (_i32, [_vp]),
     "amp_peer_allreduce_max_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, C.c_uint, _vp]),

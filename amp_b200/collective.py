@@ -128,8 +128,10 @@ class PeerMailboxes:
         own = C.c_void_p()
         call("amp_peer_mailbox_create", C.byref(own), handle)
         self.own = own.value
-        handles = [None] * g.world
-        dist.all_gather_object(handles, bytes(handle), group=g.group)
+        handles = [bytes(handle)]
+        if g.world > 1:
+            handles = [None] * g.world
+            dist.all_gather_object(handles, bytes(handle), group=g.group)
         ptrs, self._opened = [], []
         for r, hb in enumerate(handles):
             if r == g.rank:
@@ -158,3 +160,72 @@ class PeerMailboxes:
         barrier(self.g)                 # every peer has unmapped this rank's mailbox
         call("amp_peer_mailbox_free", self.own)
         self.own, self._opened = None, []
+
+
+_TYPESTR = {torch.bfloat16: "<i2", torch.float32: "<f4", torch.uint8: "|u1"}
+
+
+class _CudaArray:
+    """Zero-copy view of a raw device pointer (__cuda_array_interface__)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3}
+
+
+class PeerBuffer:
+    """A [rows, cols] output replicated on every rank of `g`, which the other
+    ranks write into directly over NVLink (CUDA IPC): the C of the all-gather
+    GEMM.  `tensor` is this rank's copy, `table` the device array of every
+    rank's pointer that the kernels take, `mailboxes` the completion mailboxes.
+
+    Collective: every rank constructs it, and closes it, at the same point."""
+
+    def __init__(self, g: CommGroup, rows: int, cols: int, dtype=torch.bfloat16,
+                 mailboxes: "PeerMailboxes | None" = None):
+        from ._lib import call, lib
+        if dtype not in _TYPESTR:
+            raise ValueError(f"unsupported peer buffer dtype {dtype}")
+        self.g, self.shape, self.dtype = g, (rows, cols), dtype
+        esz = torch.tensor([], dtype=dtype).element_size()
+        n = int(lib().amp_peer_handle_bytes())
+        handle = (C.c_ubyte * n)()
+        own = C.c_void_p()
+        call("amp_peer_buffer_create", rows * cols * esz, C.byref(own), handle)
+        self.own = own.value
+        handles = [bytes(handle)]
+        if g.world > 1:
+            handles = [None] * g.world
+            dist.all_gather_object(handles, bytes(handle), group=g.group)
+        ptrs, self._opened = [], []
+        for r in range(g.world):
+            if r == g.rank:
+                ptrs.append(self.own)
+                continue
+            p = C.c_void_p()
+            call("amp_peer_mailbox_open", (C.c_ubyte * n).from_buffer_copy(handles[r]), C.byref(p))
+            ptrs.append(p.value)
+            self._opened.append(p.value)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.table = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+        # torch reads bf16 through the array interface as int16 and reinterprets it;
+        # the view does not own the memory, so it must not outlive close()
+        raw = torch.as_tensor(_CudaArray(self.own, (rows, cols), _TYPESTR[dtype]), device=dev)
+        self.tensor = raw.view(dtype) if dtype == torch.bfloat16 else raw
+        self._own_mb = mailboxes is None
+        self.mailboxes = mailboxes if mailboxes is not None else PeerMailboxes(g)
+
+    def close(self) -> None:
+        from ._lib import call
+        if self.own is None:
+            return
+        torch.cuda.synchronize()
+        barrier(self.g)                 # nobody writes any more
+        for p in self._opened:
+            call("amp_peer_mailbox_close", p)
+        barrier(self.g)                 # every peer has unmapped this rank's buffer
+        self.tensor = None
+        call("amp_peer_mailbox_free", self.own)
+        self.own, self._opened = None, []
+        if self._own_mb:
+            self.mailboxes.close()

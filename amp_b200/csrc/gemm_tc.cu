@@ -26,12 +26,24 @@
 //               next tile's MMAs overlap this tile's stores.
 // Tiles are visited in groups of 16 M-tiles (a ~2K-row band) so that the
 // CTAs running at the same time share A rows and B columns in L2.
+//
+// All-gather mode (N-sharded GEMM on the GPUs of one node, the reference's
+// launch + ncclAllGather of C, include/collective.hpp:87-89): rank r computes
+// its column block C[:, r*N : (r+1)*N] and the epilogue stores every chunk
+// straight into the replicated C of every rank -- its own and, over NVLink,
+// each peer's (CUDA IPC mappings) -- so the exchange overlaps the MMAs of the
+// next tiles.  When a CTA's epilogue warps have stored their last tile they
+// fence at system scope and count themselves done; the last warp on the GPU
+// posts this launch's sequence number to every rank's mailbox and waits
+// (bounded) until every rank has posted it, so the kernel ends only once
+// every peer's stores into this rank's C are visible.
 #include <cuda.h>
 
 #include <cfloat>
 #include <mutex>
 
 #include "common.cuh"
+#include "peer.cuh"
 #include "runtime.h"
 #include "tc_common.cuh"
 
@@ -48,6 +60,10 @@ constexpr int A_STAGE_BYTES = BM * SLAB;           // 16 KiB
 constexpr int B_STAGE_BYTES = BN * SLAB;           // 32 KiB (BK rows x 256 cols x es)
 constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+// all-gather mode: per epilogue warp a [32 rows x 128 B] staging tile, so that
+// the stores to the other ranks go out as whole 128-byte row segments
+constexpr int AG_STAGE_BYTES = 4 * 32 * 128;
+constexpr int SMEM_BYTES_AG = SMEM_BYTES + AG_STAGE_BYTES;
 constexpr uint32_t TMEM_COLS = 512;
 
 enum ScaleMode : int { kNoScale = 0, kTensorScale = 1, kRowColScale = 2 };
@@ -62,7 +78,18 @@ struct TcParams {
     const float* scale_c;   // E4M3 output: dequantisation scale of C (device float)
     float* amax;            // optional: max |C| before output conversion (device float)
     int* status;
+    // all-gather mode (peers != nullptr): C of every rank, [M][ldc] each; this
+    // rank's block starts at column col_base
+    void* const* peers;
+    int world, rank, ldc, col_base;
+    unsigned long long* const* mbox;
+    unsigned seq;
+    unsigned* done;         // epilogue warps finished (zeroed before the launch)
 };
+
+// Epilogue warps of the all-gather GEMM that have stored their last tile; one
+// counter per device (one all-gather GEMM in flight per device).
+__device__ unsigned g_allgather_done;
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
     const int per_group = kGroupM * num_n;
@@ -74,7 +101,7 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm
     tn = local / gm;
 }
 
-template <bool kFP8, typename OutT>
+template <bool kFP8, typename OutT, bool kAllGather>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const TcParams p) {
@@ -185,6 +212,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         const int quad = warp & 3;             // TMEM lanes [32*quad, 32*quad + 32)
         const int row_in_tile = quad * 32 + lane;
+        uint4* ag_stage = reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES + 256) +
+                          (warp - 2) * 32 * 8;   // all-gather mode only
         float amx = 0.0f;                      // this thread's max |C| (NaN ignored)
         int i = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
@@ -216,6 +245,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const int col0 = tn * BN + c * 32;
                 if (col0 >= p.N) continue;  // warp-uniform
+                // all-gather mode: chunk groups of 128 bytes a row that lie inside N go
+                // through the staging tile (all lanes, rows past M included)
+                constexpr int CPG = 128 / (32 * (int)sizeof(OutT));   // chunks per group
+                const bool staged = kAllGather && (tn * BN + (c / CPG + 1) * CPG * 32 <= p.N);
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * sa;
@@ -224,60 +257,113 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] *= __shfl_sync(0xffffffffu, sbv, j);
                 }
-                if (!row_ok) continue;
-                if (p.amax) {
+                if (p.amax && row_ok) {
                     const int nv = p.N - col0;
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
                         if (j < nv) amx = fmaxf(amx, fabsf(v[j]));
                 }
-                OutT* out = static_cast<OutT*>(p.C) + (int64_t)row * p.N + col0;
-                const bool full_chunk = col0 + 32 <= p.N &&
-                                        ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
-                if constexpr (sizeof(OutT) == 1) {
-                    uint32_t w8[8];
+                if constexpr (kAllGather && sizeof(OutT) != 1) {
+                    if (staged) {
+                        // this row's 32 values into 16-byte columns [slot0, slot0 + Q) of the
+                        // warp's staging row, swizzled by row so neither side conflicts
+                        constexpr int Q = 32 * (int)sizeof(OutT) / 16;
+                        const int slot0 = (c % CPG) * Q;
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4)
-                        w8[j >> 2] = f32x2_to_e4m3x2(__fmul_rn(v[j], inv_c), __fmul_rn(v[j + 1], inv_c)) |
-                                     (f32x2_to_e4m3x2(__fmul_rn(v[j + 2], inv_c),
-                                                      __fmul_rn(v[j + 3], inv_c)) << 16);
-                    if (full_chunk) {
-                        reinterpret_cast<uint4*>(out)[0] = make_uint4(w8[0], w8[1], w8[2], w8[3]);
-                        reinterpret_cast<uint4*>(out)[1] = make_uint4(w8[4], w8[5], w8[6], w8[7]);
-                    } else {
-                        uint8_t* o8 = reinterpret_cast<uint8_t*>(out);
+                        for (int k = 0; k < Q; ++k) {
+                            uint4 w;
+                            if constexpr (sizeof(OutT) == 4) {
+                                w = make_uint4(__float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]),
+                                               __float_as_uint(v[4 * k + 2]), __float_as_uint(v[4 * k + 3]));
+                            } else {
+                                w.x = f32x2_to_bf16x2(v[8 * k], v[8 * k + 1]);
+                                w.y = f32x2_to_bf16x2(v[8 * k + 2], v[8 * k + 3]);
+                                w.z = f32x2_to_bf16x2(v[8 * k + 4], v[8 * k + 5]);
+                                w.w = f32x2_to_bf16x2(v[8 * k + 6], v[8 * k + 7]);
+                            }
+                            ag_stage[lane * 8 + ((slot0 + k) ^ (lane & 7))] = w;
+                        }
+                        if (c % CPG == CPG - 1) {
+                            __syncwarp();
+                            // 32 rows x 128 B to every rank's C (this rank last): each store
+                            // instruction writes 4 whole row segments
+                            const int gcol = p.col_base + tn * BN + (c - CPG + 1) * 32;
+                            const int row0 = tm * BM + quad * 32;
+                            for (int i = 1; i <= p.world; ++i) {
+                                uint8_t* base = static_cast<uint8_t*>(p.peers[(p.rank + i) % p.world]);
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)   // constant indices: w8 stays in registers
-                            if (col0 + j < p.N) o8[j] = (uint8_t)(w8[j >> 2] >> (8 * (j & 3)));
+                                for (int it = 0; it < 8; ++it) {
+                                    const int idx = it * 32 + lane, r8 = idx >> 3, c16 = idx & 7;
+                                    if (row0 + r8 < p.M)
+                                        *reinterpret_cast<uint4*>(
+                                            base + ((int64_t)(row0 + r8) * p.ldc + gcol) * sizeof(OutT) +
+                                            c16 * 16) = ag_stage[r8 * 8 + (c16 ^ (r8 & 7))];
+                                }
+                            }
+                            __syncwarp();
+                        }
+                        continue;
                     }
-                } else if constexpr (sizeof(OutT) == 4) {
-                    if (full_chunk) {
+                }
+                if (!row_ok) continue;
+                auto store_to = [&](OutT* out) {
+                    const bool full_chunk = col0 + 32 <= p.N &&
+                                            ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
+                    if constexpr (sizeof(OutT) == 1) {
+                        uint32_t w8[8];
 #pragma unroll
                         for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4*>(out + j) =
-                                make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                    } else {
+                            w8[j >> 2] = f32x2_to_e4m3x2(__fmul_rn(v[j], inv_c), __fmul_rn(v[j + 1], inv_c)) |
+                                         (f32x2_to_e4m3x2(__fmul_rn(v[j + 2], inv_c),
+                                                          __fmul_rn(v[j + 3], inv_c)) << 16);
+                        if (full_chunk) {
+                            reinterpret_cast<uint4*>(out)[0] = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+                            reinterpret_cast<uint4*>(out)[1] = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+                        } else {
+                            uint8_t* o8 = reinterpret_cast<uint8_t*>(out);
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)   // constant indices: v stays in registers
-                            if (col0 + j < p.N) out[j] = v[j];
-                    }
-                } else {
-                    if (full_chunk) {
+                            for (int j = 0; j < 32; ++j)   // constant indices: w8 stays in registers
+                                if (col0 + j < p.N) o8[j] = (uint8_t)(w8[j >> 2] >> (8 * (j & 3)));
+                        }
+                    } else if constexpr (sizeof(OutT) == 4) {
+                        if (full_chunk) {
 #pragma unroll
-                        for (int j = 0; j < 32; j += 8) {
-                            uint4 w;
-                            w.x = f32x2_to_bf16x2(v[j], v[j + 1]);
-                            w.y = f32x2_to_bf16x2(v[j + 2], v[j + 3]);
-                            w.z = f32x2_to_bf16x2(v[j + 4], v[j + 5]);
-                            w.w = f32x2_to_bf16x2(v[j + 6], v[j + 7]);
-                            *reinterpret_cast<uint4*>(out + j) = w;
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<float4*>(out + j) =
+                                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)   // constant indices: v stays in registers
+                                if (col0 + j < p.N) out[j] = v[j];
                         }
                     } else {
-                        uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
+                        if (full_chunk) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < p.N)
-                                o16[j] = (uint16_t)(f32x2_to_bf16x2(v[j], 0.0f) & 0xffffu);
+                            for (int j = 0; j < 32; j += 8) {
+                                uint4 w;
+                                w.x = f32x2_to_bf16x2(v[j], v[j + 1]);
+                                w.y = f32x2_to_bf16x2(v[j + 2], v[j + 3]);
+                                w.z = f32x2_to_bf16x2(v[j + 4], v[j + 5]);
+                                w.w = f32x2_to_bf16x2(v[j + 6], v[j + 7]);
+                                *reinterpret_cast<uint4*>(out + j) = w;
+                            }
+                        } else {
+                            uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (col0 + j < p.N)
+                                    o16[j] = (uint16_t)(f32x2_to_bf16x2(v[j], 0.0f) & 0xffffu);
+                        }
+                    }
+                };
+                if constexpr (!kAllGather) {
+                    store_to(static_cast<OutT*>(p.C) + (int64_t)row * p.N + col0);
+                } else {
+                    // every rank's C, this rank last (peers first, spread over the links)
+                    for (int i = 1; i <= p.world; ++i) {
+                        const int d = (p.rank + i) % p.world;
+                        store_to(static_cast<OutT*>(p.peers[d]) + (int64_t)row * p.ldc + p.col_base +
+                                 col0);
                     }
                 }
             }
@@ -285,6 +371,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.amax) {   // non-negative floats order like their bit patterns
             const float m = warp_max(amx);
             if (lane == 0) atomicMax(reinterpret_cast<unsigned*>(p.amax), __float_as_uint(m));
+        }
+        if constexpr (kAllGather) {
+            // this warp's stores (local and remote) are visible system-wide before it
+            // counts itself done; the last of the 4 * gridDim.x warps signals the peers
+            __threadfence_system();
+            __syncwarp();
+            unsigned last = 0;
+            if (lane == 0) last = atomicAdd(p.done, 1u) == 4u * gridDim.x - 1u;
+            if (__shfl_sync(0xffffffffu, last, 0)) {
+                __shared__ unsigned got[kMaxPeers];
+                __threadfence_system();
+                mailbox_exchange(p.mbox, p.rank, p.world, p.seq, 1u, got, p.status);
+            }
         }
     }
 
@@ -341,13 +440,20 @@ int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int 
     return AMP_OK;
 }
 
+struct AllGather {
+    void* const* peers = nullptr;              // device array of `world` C pointers
+    int world = 1, rank = 0;
+    unsigned long long* const* mbox = nullptr; // device array of `world` mailboxes
+    unsigned seq = 0;
+};
+
 template <bool kFP8, typename OutT>
 int launch_tc(const void* A, const void* B, void* C, int M, int N, int K, const float* sa,
               const float* sb, int mode, cudaStream_t st, const float* sc = nullptr,
-              float* amax = nullptr) {
+              float* amax = nullptr, const AllGather* ag = nullptr) {
     const int es = kFP8 ? 1 : 2;
     AMPB_REQUIRE(M > 0 && N > 0 && K > 0, AMP_ERR_INVALID, "GEMM sizes must be positive");
-    AMPB_REQUIRE(A && B && C, AMP_ERR_INVALID, "NULL operand");
+    AMPB_REQUIRE(A && B && (C || ag), AMP_ERR_INVALID, "NULL operand");
     AMPB_REQUIRE((int64_t)K * es % 16 == 0 && (int64_t)N * es % 16 == 0, AMP_ERR_UNSUPPORTED,
                  "tensor-core GEMM needs K and N to be multiples of %d (got K=%d N=%d)", 16 / es,
                  K, N);
@@ -373,19 +479,47 @@ int launch_tc(const void* A, const void* B, void* C, int M, int N, int K, const 
     p.scale_c = sc;
     p.amax = amax;
     p.status = status;
+    p.peers = nullptr;
+    p.world = 1;
+    p.rank = 0;
+    p.ldc = N;
+    p.col_base = 0;
+    p.mbox = nullptr;
+    p.seq = 0;
+    p.done = nullptr;
+    if (ag) {
+        AMPB_REQUIRE(ag->peers && ag->mbox, AMP_ERR_INVALID, "all-gather needs C and mailbox tables");
+        AMPB_REQUIRE(ag->world >= 1 && ag->world <= kMaxPeers && ag->rank >= 0 &&
+                         ag->rank < ag->world, AMP_ERR_INVALID, "rank %d / world %d outside [0, %d)",
+                     ag->rank, ag->world, kMaxPeers);
+        AMPB_REQUIRE(ag->seq != 0, AMP_ERR_INVALID, "sequence numbers start at 1");
+        AMPB_REQUIRE((int64_t)N * ag->world <= INT32_MAX, AMP_ERR_UNSUPPORTED, "C too wide");
+        void* done = nullptr;
+        AMPB_CHECK_CUDA(cudaGetSymbolAddress(&done, g_allgather_done));
+        AMPB_CHECK_CUDA(cudaMemsetAsync(done, 0, sizeof(unsigned), st));
+        p.peers = ag->peers;
+        p.world = ag->world;
+        p.rank = ag->rank;
+        p.ldc = N * ag->world;
+        p.col_base = N * ag->rank;
+        p.mbox = ag->mbox;
+        p.seq = ag->seq;
+        p.done = static_cast<unsigned*>(done);
+    }
     if (amax) AMPB_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st));
-    auto kern = k_gemm_tc<kFP8, OutT>;
-    static uint64_t attr_done = 0;  // one bit per device ordinal (< 64)
+    auto kern = ag ? k_gemm_tc<kFP8, OutT, true> : k_gemm_tc<kFP8, OutT, false>;
+    static uint64_t attr_done[2] = {0, 0};  // one bit per device ordinal (< 64) and mode
     int dev = 0;
     AMPB_CHECK_CUDA(cudaGetDevice(&dev));
-    if (dev >= 64 || !(attr_done >> dev & 1)) {
-        AMPB_CHECK_CUDA(
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-        if (dev < 64) attr_done |= 1ull << dev;
+    uint64_t& done_bits = attr_done[ag ? 1 : 0];
+    if (dev >= 64 || !(done_bits >> dev & 1)) {
+        AMPB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             ag ? SMEM_BYTES_AG : SMEM_BYTES));
+        if (dev < 64) done_bits |= 1ull << dev;
     }
     const int total = p.num_m * p.num_n;
     const int grid = total < sm_count() ? total : sm_count();
-    kern<<<grid, kThreads, SMEM_BYTES, st>>>(tmA, tmB, p);
+    kern<<<grid, kThreads, ag ? SMEM_BYTES_AG : SMEM_BYTES, st>>>(tmA, tmB, p);
     AMPB_CHECK_LAUNCH("k_gemm_tc");
     return AMP_OK;
 }
@@ -401,19 +535,21 @@ int gemm_bf16_dev(const void* A, const void* B, void* C, int c_is_bf16, int M, i
 
 int gemm_fp8_dev(const void* A, const void* B, const float* sa, const float* sb, int mode,
                  void* C, int c_dtype, int M, int N, int K, cudaStream_t st,
-                 const float* scale_c = nullptr, float* amax_c = nullptr) {
+                 const float* scale_c = nullptr, float* amax_c = nullptr,
+                 const AllGather* ag = nullptr) {
     AMPB_REQUIRE(mode == kTensorScale || mode == kRowColScale, AMP_ERR_INVALID,
                  "FP8 scale mode must be 1 (per tensor) or 2 (per row of A / column of B)");
     AMPB_REQUIRE(sa && sb, AMP_ERR_INVALID, "FP8 GEMM needs both scale pointers");
     switch (c_dtype) {
         case AMP_DTYPE_F32:
-            return launch_tc<true, float>(A, B, C, M, N, K, sa, sb, mode, st, nullptr, amax_c);
+            return launch_tc<true, float>(A, B, C, M, N, K, sa, sb, mode, st, nullptr, amax_c, ag);
         case AMP_DTYPE_BF16:
             return launch_tc<true, __nv_bfloat16>(A, B, C, M, N, K, sa, sb, mode, st, nullptr,
-                                                  amax_c);
+                                                  amax_c, ag);
         case AMP_DTYPE_E4M3:
             AMPB_REQUIRE(scale_c, AMP_ERR_INVALID, "E4M3 output needs scale_c");
-            return launch_tc<true, uint8_t>(A, B, C, M, N, K, sa, sb, mode, st, scale_c, amax_c);
+            return launch_tc<true, uint8_t>(A, B, C, M, N, K, sa, sb, mode, st, scale_c, amax_c,
+                                            ag);
         default:
             set_error(AMP_ERR_INVALID, "C dtype must be AMP_DTYPE_F32, _BF16 or _E4M3");
             return AMP_ERR_INVALID;
@@ -440,6 +576,45 @@ int amp_gemm_fp8e4m3_dev(const uint8_t* A, const uint8_t* B, const float* scale_
                  "C dtype must be AMP_DTYPE_F32 or AMP_DTYPE_BF16");
     return gemm_fp8_dev(A, B, scale_a, scale_b, scale_mode, C, c_dtype, M, N, K,
                         as_stream(stream));
+}
+
+// N-sharded GEMM with the all-gather of C fused into the epilogue (see the
+// all-gather mode above).  B is this rank's [K, N] column block; C_peers and
+// mailboxes are DEVICE arrays of `world` pointers (this rank's own at [rank]),
+// every C being [M, N * world] row-major; seq is the mailbox sequence number of
+// this exchange (the same on every rank, never 0, one more per exchange).
+int amp_gemm_bf16_allgather_dev(const void* A, const void* B, void* const* C_peers, int c_dtype,
+                                int rank, int world, void* const* mailboxes, unsigned seq, int M,
+                                int N, int K, void* stream) {
+    AMPB_REQUIRE(c_dtype == AMP_DTYPE_F32 || c_dtype == AMP_DTYPE_BF16, AMP_ERR_INVALID,
+                 "C dtype must be AMP_DTYPE_F32 or AMP_DTYPE_BF16");
+    AllGather ag;
+    ag.peers = C_peers;
+    ag.world = world;
+    ag.rank = rank;
+    ag.mbox = reinterpret_cast<unsigned long long* const*>(mailboxes);
+    ag.seq = seq;
+    if (c_dtype == AMP_DTYPE_BF16)
+        return launch_tc<false, __nv_bfloat16>(A, B, nullptr, M, N, K, nullptr, nullptr, kNoScale,
+                                               as_stream(stream), nullptr, nullptr, &ag);
+    return launch_tc<false, float>(A, B, nullptr, M, N, K, nullptr, nullptr, kNoScale,
+                                   as_stream(stream), nullptr, nullptr, &ag);
+}
+
+int amp_gemm_fp8e4m3_allgather_dev(const uint8_t* A, const uint8_t* B, const float* scale_a,
+                                   const float* scale_b, int scale_mode, void* const* C_peers,
+                                   int c_dtype, int rank, int world, void* const* mailboxes,
+                                   unsigned seq, int M, int N, int K, void* stream) {
+    AMPB_REQUIRE(c_dtype == AMP_DTYPE_F32 || c_dtype == AMP_DTYPE_BF16, AMP_ERR_INVALID,
+                 "C dtype must be AMP_DTYPE_F32 or AMP_DTYPE_BF16");
+    AllGather ag;
+    ag.peers = C_peers;
+    ag.world = world;
+    ag.rank = rank;
+    ag.mbox = reinterpret_cast<unsigned long long* const*>(mailboxes);
+    ag.seq = seq;
+    return gemm_fp8_dev(A, B, scale_a, scale_b, scale_mode, nullptr, c_dtype, M, N, K,
+                        as_stream(stream), nullptr, nullptr, &ag);
 }
 
 int amp_gemm_fp8e4m3_ex_dev(const uint8_t* A, const uint8_t* B, const float* scale_a,

@@ -10,6 +10,8 @@
 //   amp_peer_mailbox_create   cudaMalloc + zero + cudaIpcGetMemHandle
 //   amp_peer_mailbox_open     cudaIpcOpenMemHandle of a peer's mailbox
 //   amp_peer_mailbox_close / _free
+//   amp_peer_buffer_create    the same for a buffer of any size (opened, closed
+//                             and freed with the mailbox calls)
 //
 // A mailbox is [2][kMaxPeers] 64-bit words.  Rank r posts (seq << 32 | value)
 // into slot [seq & 1][r] of every rank's mailbox with st.release.sys and
@@ -83,6 +85,26 @@ int amp_peer_mailbox_create(void** mailbox, void* handle_out) {
     }
     memcpy(handle_out, &h, sizeof(h));
     *mailbox = p;
+    return AMP_OK;
+}
+
+// A device buffer of `bytes` (zeroed) that the other processes of the node can
+// map with amp_peer_mailbox_open and write into directly: the replicated output
+// of the all-gather GEMM.  Freed with amp_peer_mailbox_free.
+int amp_peer_buffer_create(size_t bytes, void** buffer, void* handle_out) {
+    AMPB_REQUIRE(buffer && handle_out && bytes > 0, AMP_ERR_INVALID, "bad peer buffer arguments");
+    void* p = nullptr;
+    AMPB_CHECK_CUDA(cudaMalloc(&p, bytes));
+    AMPB_CHECK_CUDA(cudaMemset(p, 0, bytes));
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        set_error(AMP_ERR_UNSUPPORTED, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+        return AMP_ERR_UNSUPPORTED;
+    }
+    memcpy(handle_out, &h, sizeof(h));
+    *buffer = p;
     return AMP_OK;
 }
 

@@ -5,6 +5,9 @@
   matmul_bf16_sharded    N-split GEMM: rank r computes C[:, r*N/p:(r+1)*N/p]
                          from all of A and its B column slab, then C is
                          all-gathered and laid out row-major (optional)
+  matmul_allgather       the same with the all-gather fused into the GEMM
+                         epilogue: every rank's block is stored straight into
+                         every rank's C over NVLink (bf16 or FP8 operands)
   flash_attn_sharded     (batch*head)-split attention; O / lse gathered (optional)
 """
 from __future__ import annotations
@@ -12,7 +15,9 @@ from __future__ import annotations
 import torch
 
 from . import attention, fp8, gemm
-from .collective import CommGroup, gather_columns, gather_heads, global_amax, head_range
+from ._lib import call
+from .collective import (CommGroup, PeerBuffer, gather_columns, gather_heads, global_amax,
+                         head_range)
 
 
 def quantize_e4m3_sharded(x_shard: torch.Tensor, g: CommGroup | None = None, mailboxes=None):
@@ -37,6 +42,46 @@ def matmul_bf16_sharded(A: torch.Tensor, B_slab: torch.Tensor, g: CommGroup | No
     C = torch.empty(M, Np, dtype=out_dtype, device=A.device)
     gemm.launch_matmul_bf16(A, B_slab, C, M, Np, K)
     return gather_columns(g, C) if gather else C
+
+
+def matmul_allgather(A: torch.Tensor, B_slab: torch.Tensor, out: PeerBuffer,
+                     scale_a=None, scale_b=None) -> torch.Tensor:
+    """C = A @ B on the node with the all-gather fused into the GEMM: A [M, K] on
+    every rank, B_slab [K, N/p] this rank's column block, `out` a [M, N] PeerBuffer
+    (bf16 or fp32).  bf16 operands, or E4M3 codes (uint8 / float8_e4m3fn) with
+    per-row scale_a [M] and per-column scale_b [N/p] (or 1-element tensors).
+    Returns out.tensor, complete on every rank once the stream reaches it."""
+    g = out.g
+    M, K = A.shape
+    Np = B_slab.shape[1]
+    if tuple(out.shape) != (M, Np * g.world):
+        raise ValueError(f"out is {tuple(out.shape)}, expected {(M, Np * g.world)}")
+    if out.dtype not in gemm.AMP_DTYPE:
+        raise ValueError("out must be bfloat16 or float32")
+    for t, shape, nm in ((A, (M, K), "A"), (B_slab, (K, Np), "B_slab")):
+        if not t.is_cuda or not t.is_contiguous() or tuple(t.shape) != shape:
+            raise ValueError(f"{nm}: expected a contiguous CUDA tensor of shape {shape}")
+    stream = torch.cuda.current_stream(A.device).cuda_stream
+    seq = out.mailboxes.next_seq()
+    if A.dtype == torch.bfloat16:
+        if B_slab.dtype != torch.bfloat16:
+            raise ValueError("A and B_slab must have the same type")
+        call("amp_gemm_bf16_allgather_dev", A.data_ptr(), B_slab.data_ptr(), out.table.data_ptr(),
+             gemm.AMP_DTYPE[out.dtype], g.rank, g.world, out.mailboxes.table.data_ptr(), seq,
+             M, Np, K, stream)
+    elif A.dtype in (torch.uint8, torch.float8_e4m3fn):
+        if B_slab.dtype not in (torch.uint8, torch.float8_e4m3fn):
+            raise ValueError("A and B_slab must both hold E4M3 codes")
+        rowcol = scale_a.numel() == M and M != 1 or scale_b.numel() == Np and Np != 1
+        n_a, n_b, mode = (M, Np, 2) if rowcol else (1, 1, 1)
+        sa = gemm._scale_tensor(scale_a, n_a, A.device, "scale_a")
+        sb = gemm._scale_tensor(scale_b, n_b, A.device, "scale_b")
+        call("amp_gemm_fp8e4m3_allgather_dev", A.data_ptr(), B_slab.data_ptr(), sa.data_ptr(),
+             sb.data_ptr(), mode, out.table.data_ptr(), gemm.AMP_DTYPE[out.dtype], g.rank,
+             g.world, out.mailboxes.table.data_ptr(), seq, M, Np, K, stream)
+    else:
+        raise ValueError(f"unsupported operand type {A.dtype}")
+    return out.tensor
 
 
 def flash_attn_sharded(q, k, v, causal: bool = True, g: CommGroup | None = None,

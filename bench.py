@@ -324,8 +324,15 @@ class GemmWorkload:
             self.B = b.to(torch.bfloat16).contiguous()
         del a, b
         self.C = torch.empty(S, self.Np, dtype=torch.bfloat16, device=dev)
-        self.Cfull = (torch.empty(p, S, self.Np, dtype=torch.bfloat16, device=dev)
-                      if p > 1 else None)
+        # N > 1: the all-gather is fused into the GEMM epilogue (stores into every
+        # rank's C over NVLink) unless --gather nccl asks for launch + NCCL all-gather
+        self.peer = None
+        self.Cfull = None
+        if p > 1 and args.gather == "peer":
+            from amp_b200.collective import CommGroup, PeerBuffer
+            self.peer = PeerBuffer(CommGroup.current(), S, S, torch.bfloat16)
+        elif p > 1:
+            self.Cfull = torch.empty(p, S, self.Np, dtype=torch.bfloat16, device=dev)
 
     def units_per_step(self) -> float:
         return 2.0 * self.S * self.S * self.Np
@@ -341,14 +348,21 @@ class GemmWorkload:
                                       if self.fp8 else ""),
                 "l2": "operands (2 x %d MiB) exceed L2; L2 flushed before every step"
                       % (self.S * self.S * (1 if self.fp8 else 2) >> 20),
-                "parallelism": f"N-split over {p} GPUs + NCCL all-gather of C" if p > 1
+                "parallelism": (f"N-split over {p} GPUs, all-gather of C fused into the GEMM "
+                                "epilogue (stores into every rank's C over NVLink)"
+                                if self.peer is not None else
+                                f"N-split over {p} GPUs + NCCL all-gather of C") if p > 1
                 else "single"}
 
     def kernel_table(self):
         return [(f"k_gemm_tc<{'e4m3' if self.fp8 else 'bf16'}>", self.units_per_step())]
 
     def _launch(self):
-        if self.fp8:
+        if self.peer is not None:
+            from amp_b200 import sharded
+            sharded.matmul_allgather(self.A, self.B, self.peer, self.sa if self.fp8 else None,
+                                     self.sb if self.fp8 else None)
+        elif self.fp8:
             self.gemm.launch_matmul_fp8e4m3(self.A, self.B, self.C, self.S, self.Np, self.S,
                                             self.sa, self.sb)
         else:
@@ -358,8 +372,13 @@ class GemmWorkload:
         if ev: ev[0].record()
         self._launch()
         if ev: ev[1].record()
-        if self.dist.world > 1:
+        if self.Cfull is not None:
             self.dist.pg.all_gather_into_tensor(self.Cfull, self.C)
+
+    def close(self):
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def e2e(self, steps: int, warmup: int):
         torch = self.torch
@@ -917,6 +936,8 @@ def main():
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="N>1 GEMM: all-gather fused into the epilogue (peer) or NCCL after it")
     args = ap.parse_args()
     if args.impl == "reference":
         args.steps = args.steps or 5

@@ -150,6 +150,24 @@ AMP_API int amp_gemm_fp8e4m3_dev(const uint8_t* A, const uint8_t* B, const float
                                  const float* scale_b, int scale_mode, void* C, int c_dtype,
                                  int M, int N, int K, void* stream);
 
+/* N-sharded GEMM with the all-gather of C fused into the epilogue; replaces
+ * AMP's per-rank launch + ncclAllGather of C (include/collective.hpp:87-89,
+ * src/collective.cpp:155-160).  B is this rank's [K, N] column block; every
+ * rank holds C [M, N * world] row-major (amp_peer_buffer_create), and this
+ * rank's epilogue stores its block C[:, rank*N : (rank+1)*N] into all of them
+ * over NVLink.  C_peers / mailboxes: DEVICE arrays of `world` pointers (own at
+ * [rank]); seq: the mailbox sequence number of this call (the same on every
+ * rank, never 0, one more per exchange).  On return of the stream work every
+ * rank's C is complete.  The next call into the same C may start only after
+ * every rank has finished reading it.  One call in flight per device. */
+AMP_API int amp_gemm_bf16_allgather_dev(const void* A, const void* B, void* const* C_peers,
+                                        int c_dtype, int rank, int world, void* const* mailboxes,
+                                        unsigned seq, int M, int N, int K, void* stream);
+AMP_API int amp_gemm_fp8e4m3_allgather_dev(const uint8_t* A, const uint8_t* B,
+                                           const float* scale_a, const float* scale_b,
+                                           int scale_mode, void* const* C_peers, int c_dtype,
+                                           int rank, int world, void* const* mailboxes,
+                                           unsigned seq, int M, int N, int K, void* stream);
 /* FP8 GEMM with output-side quantisation (AMP's GemmDesc d_scale_c / d_amax_c,
  * include/gemm_vendor.hpp:55-56, which it hands to cuBLASLt):
  *   v = scale_a * scale_b * (A8 . B8)  (fp32 accumulate)
@@ -266,6 +284,10 @@ AMP_API size_t amp_peer_mailbox_bytes(void);
 AMP_API int amp_peer_handle_bytes(void);
 AMP_API int amp_peer_mailbox_create(void** mailbox, void* handle_out);
 AMP_API int amp_peer_mailbox_open(const void* handle, void** mailbox);
+/* A zeroed device buffer of `bytes` that the other ranks open with
+ * amp_peer_mailbox_open (close / free with the mailbox calls): the replicated
+ * output C of the all-gather GEMMs below. */
+AMP_API int amp_peer_buffer_create(size_t bytes, void** buffer, void* handle_out);
 AMP_API int amp_peer_mailbox_close(void* mailbox);
 AMP_API int amp_peer_mailbox_free(void* mailbox);
 /* all-reduce(max) of one float per rank through the mailboxes (device in/out). */

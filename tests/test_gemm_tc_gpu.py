@@ -177,3 +177,27 @@ def test_fp8_output_quantisation_and_amax(M, N, K, rowcol, cuda, amp_lib):
 def ctypes_float(x):
     import ctypes
     return ctypes.c_float(float(x))
+
+
+def test_allgather_gemm_single_rank(cuda):
+    """The fused all-gather GEMM on a group of one: the epilogue writes into the
+    rank's own replicated C and the kernel's completion exchange posts to itself."""
+    from amp_b200 import sharded
+    from amp_b200._lib import lib
+    from amp_b200.collective import CommGroup, PeerBuffer
+    M, N, K = 384, 512, 320
+    g = torch.Generator(device="cuda").manual_seed(21)
+    A = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    B = torch.randn(K, N, generator=g, device="cuda").to(torch.bfloat16)
+    ref = torch.empty(M, N, dtype=torch.float32, device="cuda")
+    gemm.launch_matmul_bf16(A, B, ref, M, N, K)
+    for dtype in (torch.bfloat16, torch.float32):
+        pb = PeerBuffer(CommGroup(), M, N, dtype)
+        try:
+            for _ in range(3):
+                C = sharded.matmul_allgather(A, B, pb)
+                torch.cuda.synchronize()
+                assert torch.equal(C.float(), ref.to(dtype).float())
+            assert lib().amp_device_status(1) == 0
+        finally:
+            pb.close()

@@ -70,6 +70,30 @@ def _rank_main(rank, world, port, q):
         C_ref = torch.empty(512, 1024, dtype=torch.bfloat16, device=dev)
         gemm.launch_matmul_bf16(A, B, C_ref, 512, 1024, 256)
         assert torch.equal(C, C_ref)
+        # the same with the all-gather fused into the GEMM epilogue (stores into every
+        # rank's C over NVLink); a barrier between calls, so nobody still reads C
+        from amp_b200.collective import PeerBuffer
+        pb = PeerBuffer(CommGroup.current(), 512, 1024, torch.bfloat16)
+        try:
+            for _ in range(3):
+                Cf = sharded.matmul_allgather(A, B[:, rank * w:(rank + 1) * w].contiguous(), pb)
+                torch.cuda.synchronize()
+                assert torch.equal(Cf, C_ref)
+                dist.barrier()
+            # FP8 operands, per-row / per-column scales, into the same buffer
+            a8 = (A.float() / 4).to(torch.float8_e4m3fn).view(torch.uint8).contiguous()
+            b8 = (B.float() / 4).to(torch.float8_e4m3fn).view(torch.uint8).contiguous()
+            sa = torch.rand(512, generator=g, device=dev) + 0.5
+            sb = torch.rand(1024, generator=g, device=dev) + 0.5
+            C8_ref = torch.empty(512, 1024, dtype=torch.bfloat16, device=dev)
+            gemm.launch_matmul_fp8e4m3(a8, b8, C8_ref, 512, 1024, 256, sa, sb)
+            C8 = sharded.matmul_allgather(a8, b8[:, rank * w:(rank + 1) * w].contiguous(), pb,
+                                          sa, sb[rank * w:(rank + 1) * w].contiguous())
+            torch.cuda.synchronize()
+            assert torch.equal(C8, C8_ref)
+            assert lib().amp_device_status(1) == 0
+        finally:
+            pb.close()
         # (batch*head)-split attention + gather
         qa, ka, va = (torch.randn(2, 4, 256, 128, generator=g, device=dev).to(torch.bfloat16)
                       for _ in range(3))
