@@ -42,6 +42,9 @@ SIGNATURES: dict[str, tuple] = {
     "amp_user_gemm_fp8e4m3": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32]),
     "amp_flash_attn_fwd_bf16_dev": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
                                            _i32, _i32, _i32, _f32, _vp]),
+    "amp_flash_attn_fwd_allgather_dev": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp,
+                                                C.c_uint, _i32, _i32, _i32, _i32, _i32, _i32,
+                                                _i32, _f32, _vp]),
     "amp_flash_attn_bwd_workspace_bytes": (_sz, [_i32, _i32, _i32]),
     "amp_flash_attn_bwd_bf16_dev": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32,
                                            _i32, _i32, _i32, _i32, _i32, _f32, _vp, _sz, _vp]),

@@ -30,11 +30,20 @@
 //              rescaled (tcgen05.ld/st) only when a row maximum grows by more
 //              than 2^8; otherwise the stale maximum is kept.
 //              Epilogue: O / l to bf16, lse = (m + log2 l) * ln 2.
+//
+// All-gather mode ((batch*head)-sharded attention on the GPUs of one node: the
+// reference's launch + ncclAllGather of O / lse, include/collective.hpp:87-89):
+// each softmax warp stages its 32 output rows in the tile's Q buffer (free once
+// the tile's last MMA has completed) and writes them -- contiguous in O -- to
+// every rank's O, then its lse values; when all softmax warps on the GPU are
+// done (system-scope fence + counter), the last one exchanges this launch's
+// sequence number with every rank through the peer mailboxes (bounded wait).
 #include <cuda.h>
 
 #include <cmath>
 
 #include "common.cuh"
+#include "peer.cuh"
 #include "runtime.h"
 #include "tc_common.cuh"
 
@@ -68,7 +77,19 @@ struct FaParams {
     const int* block_table;
     const int* ctx_lens;
     int max_pages, num_pages;
+    // all-gather mode: every rank's O ([bh_total][S_q][D] bf16) and lse; this
+    // launch's (batch*head) 0 is global index bh_base
+    void* const* o_peers;
+    float* const* lse_peers;
+    int world, rank, bh_base;
+    unsigned long long* const* mbox;
+    unsigned seq;
+    unsigned* done;
 };
+
+// Softmax warps of the all-gather attention that have stored their rows; one
+// counter per device (one all-gather attention launch in flight per device).
+__device__ unsigned g_fa_allgather_done;
 
 constexpr int kPageTokens = 16;
 
@@ -94,7 +115,7 @@ struct FaCfg {
     static constexpr uint32_t O_COL = 2 * BKV;            // S0 | S1 | O0 | O1
 };
 
-template <int D, bool kPaged>
+template <int D, bool kPaged, bool kAllGather = false>
 __global__ void __launch_bounds__(kThreads, 1)
     k_flash_fwd(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
            const __grid_constant__ CUtensorMap tmV, const FaParams p) {
@@ -389,15 +410,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
             const bool row_ok = qi < p.S_q;
-            __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.O) +
-                                  ((int64_t)bh * p.S_q + (row_ok ? qi : 0)) * D;
-            __syncwarp();
+            const float lse_v =
+                l_run > 0.0f ? (m_run + lg2_approx(l_run)) * 0.69314718055994531f : -INFINITY;
+            if constexpr (!kAllGather) {
+                __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.O) +
+                                      ((int64_t)bh * p.S_q + (row_ok ? qi : 0)) * D;
+                __syncwarp();
 #pragma unroll
-            for (int oc = 0; oc < D / 32; ++oc) {
-                uint32_t o[32];
-                tmem_ld_32x32b_x32(lane_base + o_col + oc * 32, o);
-                tmem_ld_wait();
-                if (row_ok) {
+                for (int oc = 0; oc < D / 32; ++oc) {
+                    uint32_t o[32];
+                    tmem_ld_32x32b_x32(lane_base + o_col + oc * 32, o);
+                    tmem_ld_wait();
+                    if (row_ok) {
+#pragma unroll
+                        for (int e = 0; e < 32; e += 8) {
+                            uint4 w;
+                            w.x = f32x2_to_bf16x2(__uint_as_float(o[e]) * inv_l, __uint_as_float(o[e + 1]) * inv_l);
+                            w.y = f32x2_to_bf16x2(__uint_as_float(o[e + 2]) * inv_l, __uint_as_float(o[e + 3]) * inv_l);
+                            w.z = f32x2_to_bf16x2(__uint_as_float(o[e + 4]) * inv_l, __uint_as_float(o[e + 5]) * inv_l);
+                            w.w = f32x2_to_bf16x2(__uint_as_float(o[e + 6]) * inv_l, __uint_as_float(o[e + 7]) * inv_l);
+                            *reinterpret_cast<uint4*>(orow + oc * 32 + e) = w;
+                        }
+                    }
+                }
+                if (row_ok && p.lse) p.lse[(int64_t)bh * p.S_q + qi] = lse_v;
+            } else {
+                // stage this warp's 32 rows (D * 2 bytes each, 16-byte slots swizzled by
+                // row) in the tile's Q buffer: every MMA that read it has completed
+                constexpr int SLOTS = D * 2 / 16;
+                uint4* st = reinterpret_cast<uint4*>(q_s + t * CF::TILE) + quad * 32 * SLOTS;
+                fence_proxy_async_smem();
+                __syncwarp();
+#pragma unroll
+                for (int oc = 0; oc < D / 32; ++oc) {
+                    uint32_t o[32];
+                    tmem_ld_32x32b_x32(lane_base + o_col + oc * 32, o);
+                    tmem_ld_wait();
 #pragma unroll
                     for (int e = 0; e < 32; e += 8) {
                         uint4 w;
@@ -405,13 +453,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                         w.y = f32x2_to_bf16x2(__uint_as_float(o[e + 2]) * inv_l, __uint_as_float(o[e + 3]) * inv_l);
                         w.z = f32x2_to_bf16x2(__uint_as_float(o[e + 4]) * inv_l, __uint_as_float(o[e + 5]) * inv_l);
                         w.w = f32x2_to_bf16x2(__uint_as_float(o[e + 6]) * inv_l, __uint_as_float(o[e + 7]) * inv_l);
-                        *reinterpret_cast<uint4*>(orow + oc * 32 + e) = w;
+                        const int slot = oc * 4 + (e >> 3);
+                        st[lane * SLOTS + ((slot & ~7) | ((slot ^ lane) & 7))] = w;
                     }
                 }
+                __syncwarp();
+                // the warp's rows are contiguous in O: whole 512-byte stores to every rank
+                const int row0 = q0 + t * BQ + quad * 32;
+                const int nrows = max(0, min(32, p.S_q - row0));
+                const int64_t grow = (int64_t)(p.bh_base + bh) * p.S_q + row0;
+                for (int i = 1; i <= p.world; ++i) {
+                    const int d = (p.rank + i) % p.world;
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o_peers[d]) +
+                                                          grow * D);
+                    for (int idx = lane; idx < nrows * SLOTS; idx += 32) {
+                        const int rr = idx / SLOTS, slot = idx % SLOTS;
+                        dst[idx] = st[rr * SLOTS + ((slot & ~7) | ((slot ^ rr) & 7))];
+                    }
+                    if (row_ok && p.lse_peers) p.lse_peers[d][grow + lane] = lse_v;
+                }
             }
-            if (row_ok && p.lse)
-                p.lse[(int64_t)bh * p.S_q + qi] =
-                    l_run > 0.0f ? (m_run + lg2_approx(l_run)) * 0.69314718055994531f : -INFINITY;
+        }
+    }
+    if constexpr (kAllGather) {
+        if (warp >= 4) {
+            // this warp's stores are visible system-wide before it counts itself done;
+            // the last of the 8 softmax warps of every CTA signals the other ranks
+            __threadfence_system();
+            __syncwarp();
+            unsigned last = 0;
+            if (lane == 0)
+                last = atomicAdd(p.done, 1u) == 8u * gridDim.x * gridDim.y - 1u;
+            if (__shfl_sync(0xffffffffu, last, 0)) {
+                __shared__ unsigned got[kMaxPeers];
+                __threadfence_system();
+                mailbox_exchange(p.mbox, p.rank, p.world, p.seq, 1u, got, p.status);
+            }
         }
     }
 
@@ -429,10 +506,18 @@ struct PagedKV {
     int max_pages = 0, num_pages = 0;
 };
 
+struct FaAllGather {
+    void* const* o_peers = nullptr;
+    float* const* lse_peers = nullptr;
+    int world = 1, rank = 0, bh_base = 0;
+    unsigned long long* const* mbox = nullptr;
+    unsigned seq = 0;
+};
+
 template <int D, bool kPaged>
 int launch_fa(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq,
               int Hkv, int S_q, int S_kv, int causal, int causal_offset, float scale,
-              const PagedKV& pkv, cudaStream_t st) {
+              const PagedKV& pkv, cudaStream_t st, const FaAllGather* ag = nullptr) {
     CUtensorMap tq, tk, tv;
     int rc;
     if ((rc = fa_make_tmap_3d(&tq, Q, D, S_q, (int64_t)B * Hq))) return rc;
@@ -461,7 +546,31 @@ int launch_fa(const void* Q, const void* K, const void* V, void* O, float* lse, 
     p.ctx_lens = pkv.ctx_lens;
     p.max_pages = pkv.max_pages;
     p.num_pages = pkv.num_pages;
-    auto kern = k_flash_fwd<D, kPaged>;
+    p.o_peers = nullptr;
+    p.lse_peers = nullptr;
+    p.world = 1;
+    p.rank = 0;
+    p.bh_base = 0;
+    p.mbox = nullptr;
+    p.seq = 0;
+    p.done = nullptr;
+    auto kern = k_flash_fwd<D, kPaged, false>;
+    if constexpr (!kPaged) {
+        if (ag) {
+            void* done = nullptr;
+            AMPB_CHECK_CUDA(cudaGetSymbolAddress(&done, g_fa_allgather_done));
+            AMPB_CHECK_CUDA(cudaMemsetAsync(done, 0, sizeof(unsigned), st));
+            p.o_peers = ag->o_peers;
+            p.lse_peers = ag->lse_peers;
+            p.world = ag->world;
+            p.rank = ag->rank;
+            p.bh_base = ag->bh_base;
+            p.mbox = ag->mbox;
+            p.seq = ag->seq;
+            p.done = static_cast<unsigned*>(done);
+            kern = k_flash_fwd<D, kPaged, true>;
+        }
+    }
     AMPB_CHECK_CUDA(
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FaCfg<D>::SMEM));
     dim3 grid((S_q + 2 * BQ - 1) / (2 * BQ), B * Hq);
@@ -524,24 +633,24 @@ int fa_encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims
 
 int flash_attn_fwd_dev(const void* Q, const void* K, const void* V, void* O, float* lse, int B,
                        int Hq, int Hkv, int S_q, int S_kv, int D, int causal, int causal_offset,
-                       float scale, cudaStream_t st) {
+                       float scale, cudaStream_t st, const FaAllGather* ag = nullptr) {
     AMPB_REQUIRE(B > 0 && Hq > 0 && Hkv > 0 && S_q > 0 && S_kv > 0, AMP_ERR_INVALID,
                  "attention sizes must be positive");
     AMPB_REQUIRE(Hq % Hkv == 0, AMP_ERR_INVALID, "num_q_heads (%d) must be a multiple of "
                  "num_kv_heads (%d)", Hq, Hkv);
-    AMPB_REQUIRE(Q && K && V && O, AMP_ERR_INVALID, "NULL tensor");
-    AMPB_REQUIRE(aligned16(Q) && aligned16(K) && aligned16(V) && aligned16(O), AMP_ERR_INVALID,
-                 "Q, K, V, O must be 16-byte aligned");
+    AMPB_REQUIRE(Q && K && V && (O || ag), AMP_ERR_INVALID, "NULL tensor");
+    AMPB_REQUIRE(aligned16(Q) && aligned16(K) && aligned16(V) && (ag || aligned16(O)),
+                 AMP_ERR_INVALID, "Q, K, V, O must be 16-byte aligned");
     AMPB_REQUIRE((int64_t)B * Hq <= 65535, AMP_ERR_UNSUPPORTED, "B*Hq must be <= 65535");
     if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)D);
     const PagedKV none;
     switch (D) {
         case 128:
             return launch_fa<128, false>(Q, K, V, O, lse, B, Hq, Hkv, S_q, S_kv, causal,
-                                         causal_offset, scale, none, st);
+                                         causal_offset, scale, none, st, ag);
         case 64:
             return launch_fa<64, false>(Q, K, V, O, lse, B, Hq, Hkv, S_q, S_kv, causal,
-                                        causal_offset, scale, none, st);
+                                        causal_offset, scale, none, st, ag);
         default:
             set_error(AMP_ERR_UNSUPPORTED, "flash_attn: head_dim %d not supported (64, 128)", D);
             return AMP_ERR_UNSUPPORTED;
@@ -598,6 +707,34 @@ extern "C" int amp_flash_attn_fwd_bf16_dev(const void* Q, const void* K, const v
                                            int head_dim, int causal, float scale, void* stream) {
     return flash_attn_fwd_dev(Q, K, V, O, lse, B, Hq, Hkv, S_q, S_kv, head_dim, causal, 0, scale,
                               as_stream(stream));
+}
+
+// (batch*head)-sharded attention with the all-gather of O and lse fused into the
+// epilogue.  Q, K, V hold this rank's B*Hq (B*Hkv) slice; O_peers / lse_peers
+// are DEVICE arrays of `world` pointers to every rank's full O [bh_total][S_q][D]
+// and lse [bh_total][S_q] (lse_peers may be NULL); this rank's batch*head 0 is
+// global index bh_base.  Mailboxes and seq as for amp_gemm_bf16_allgather_dev.
+extern "C" int amp_flash_attn_fwd_allgather_dev(const void* Q, const void* K, const void* V,
+                                                void* const* O_peers, float* const* lse_peers,
+                                                int rank, int world, int bh_base,
+                                                void* const* mailboxes, unsigned seq, int B,
+                                                int Hq, int Hkv, int S_q, int S_kv, int head_dim,
+                                                int causal, float scale, void* stream) {
+    AMPB_REQUIRE(O_peers && mailboxes, AMP_ERR_INVALID, "all-gather needs O and mailbox tables");
+    AMPB_REQUIRE(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world, AMP_ERR_INVALID,
+                 "rank %d / world %d outside [0, %d)", rank, world, kMaxPeers);
+    AMPB_REQUIRE(seq != 0, AMP_ERR_INVALID, "sequence numbers start at 1");
+    AMPB_REQUIRE(bh_base >= 0, AMP_ERR_INVALID, "bh_base must be >= 0");
+    FaAllGather ag;
+    ag.o_peers = O_peers;
+    ag.lse_peers = lse_peers;
+    ag.world = world;
+    ag.rank = rank;
+    ag.bh_base = bh_base;
+    ag.mbox = reinterpret_cast<unsigned long long* const*>(mailboxes);
+    ag.seq = seq;
+    return flash_attn_fwd_dev(Q, K, V, nullptr, nullptr, B, Hq, Hkv, S_q, S_kv, head_dim, causal,
+                              0, scale, as_stream(stream), &ag);
 }
 
 // Host-pointer form (plugin convention): all tensors in host memory; device

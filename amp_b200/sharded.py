@@ -9,6 +9,8 @@
                          epilogue: every rank's block is stored straight into
                          every rank's C over NVLink (bf16 or FP8 operands)
   flash_attn_sharded     (batch*head)-split attention; O / lse gathered (optional)
+  flash_attn_allgather   the same with the all-gather of O / lse fused into the
+                         attention epilogue (stores into every rank's O over NVLink)
 """
 from __future__ import annotations
 
@@ -102,3 +104,36 @@ def flash_attn_sharded(q, k, v, causal: bool = True, g: CommGroup | None = None,
         return o, lse
     return (gather_heads(g, o[0]).reshape(B, Hq, S, D),
             gather_heads(g, lse[0]).reshape(B, Hq, S))
+
+
+def flash_attn_allgather(q, k, v, causal: bool, o_out: PeerBuffer, lse_out: PeerBuffer | None = None,
+                         scale: float = 0.0):
+    """(batch*head)-split attention with the all-gather fused into the epilogue.
+    q/k/v [B, H, S, D] on every rank (Hq == Hkv); o_out a [B*H*S, D] bf16 PeerBuffer,
+    lse_out an optional [B*H, S] fp32 PeerBuffer sharing o_out's mailboxes.  Returns
+    (O [B, H, S, D], lse [B, H, S] or None), complete on every rank once the stream
+    reaches them."""
+    g = o_out.g
+    B, Hq, S, D = q.shape
+    Hkv = k.shape[1]
+    if Hq != Hkv:
+        raise ValueError("the batch*head split keeps kv heads with their query group: "
+                         "use Hq == Hkv or shard along batch")
+    if tuple(o_out.shape) != (B * Hq * S, D) or o_out.dtype != torch.bfloat16:
+        raise ValueError(f"o_out must be a ({B * Hq * S}, {D}) bfloat16 PeerBuffer")
+    if lse_out is not None:
+        if tuple(lse_out.shape) != (B * Hq, S) or lse_out.dtype != torch.float32:
+            raise ValueError(f"lse_out must be a ({B * Hq}, {S}) float32 PeerBuffer")
+        if lse_out.mailboxes is not o_out.mailboxes:
+            raise ValueError("lse_out must share o_out's mailboxes")
+    lo, hi = head_range(B * Hq, g)
+    qs = q.reshape(B * Hq, S, D)[lo:hi].contiguous()
+    ks = k.reshape(B * Hkv, S, D)[lo:hi].contiguous()
+    vs = v.reshape(B * Hkv, S, D)[lo:hi].contiguous()
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    call("amp_flash_attn_fwd_allgather_dev", qs.data_ptr(), ks.data_ptr(), vs.data_ptr(),
+         o_out.table.data_ptr(), lse_out.table.data_ptr() if lse_out is not None else None,
+         g.rank, g.world, lo, o_out.mailboxes.table.data_ptr(), o_out.mailboxes.next_seq(),
+         1, hi - lo, hi - lo, S, S, D, int(causal), float(scale), stream)
+    o = o_out.tensor.view(B, Hq, S, D)
+    return o, (lse_out.tensor.view(B, Hq, S) if lse_out is not None else None)

@@ -437,6 +437,7 @@ class GemmFp8Workload(GemmWorkload):
 
 class AttentionWorkload:
     name = "fa2_fwd"
+    fused_gather = True
     metric = "fa2_fwd_causal_TFLOPS"
     unit = "TFLOP/s"
     scale = 1e12
@@ -463,8 +464,17 @@ class AttentionWorkload:
         self.o = torch.empty_like(self.q)
         self.lse = torch.empty(1, self.bh, self.S, dtype=torch.float32, device=dev)
         self.cfg = attention.AttnCfg(self.bh, self.bh, self.D, True, 0.0)
-        self.o_all = (torch.empty(p, self.bh, self.S, self.D, dtype=torch.bfloat16, device=dev)
-                      if p > 1 else None)
+        # N > 1: the all-gather of O and lse is fused into the attention epilogue
+        # (stores into every rank's O over NVLink) unless --gather nccl
+        self.peer_o = self.peer_l = self.o_all = None
+        if p > 1 and self.fused_gather and args.gather == "peer":
+            from amp_b200.collective import CommGroup, PeerBuffer
+            cg = CommGroup.current()
+            self.peer_o = PeerBuffer(cg, self.B * self.H * self.S, self.D, torch.bfloat16)
+            self.peer_l = PeerBuffer(cg, self.B * self.H, self.S, torch.float32,
+                                     mailboxes=self.peer_o.mailboxes)
+        elif p > 1:
+            self.o_all = torch.empty(p, self.bh, self.S, self.D, dtype=torch.bfloat16, device=dev)
 
     def units_per_step(self) -> float:
         # causal: 2 matmuls x 2 flop x D per (query, visible key) pair
@@ -480,7 +490,10 @@ class AttentionWorkload:
                 "flop_convention": "4*B*H*D*S*(S+1)/2 (visible pairs)",
                 "l2": "Q/K/V %d MiB each exceed L2; L2 flushed before every step"
                       % (self.B * self.H * self.S * self.D * 2 >> 20),
-                "parallelism": f"(batch*head) split over {p} GPUs + NCCL all-gather of O"
+                "parallelism": (f"(batch*head) split over {p} GPUs, all-gather of O and lse fused "
+                                "into the attention epilogue (stores into every rank's O over "
+                                "NVLink)" if self.peer_o is not None else
+                                f"(batch*head) split over {p} GPUs + NCCL all-gather of O")
                 if p > 1 else "single"}
 
     def kernel_table(self):
@@ -488,11 +501,26 @@ class AttentionWorkload:
 
     def step(self, ev=None):
         if ev: ev[0].record()
-        self.att.launch_flash_attn_bf16(self.q, self.k, self.v, self.o, self.lse, 1, self.S,
-                                        self.S, self.cfg)
+        if self.peer_o is not None:
+            from amp_b200._lib import call
+            call("amp_flash_attn_fwd_allgather_dev", self.q.data_ptr(), self.k.data_ptr(),
+                 self.v.data_ptr(), self.peer_o.table.data_ptr(), self.peer_l.table.data_ptr(),
+                 self.dist.rank, self.dist.world, self.dist.rank * self.bh,
+                 self.peer_o.mailboxes.table.data_ptr(), self.peer_o.mailboxes.next_seq(), 1,
+                 self.bh, self.bh, self.S, self.S, self.D, 1, 0.0,
+                 self.torch.cuda.current_stream(self.q.device).cuda_stream)
+        else:
+            self.att.launch_flash_attn_bf16(self.q, self.k, self.v, self.o, self.lse, 1, self.S,
+                                            self.S, self.cfg)
         if ev: ev[1].record()
-        if self.dist.world > 1:
+        if self.o_all is not None:
             self.dist.pg.all_gather_into_tensor(self.o_all, self.o[0])
+
+    def close(self):
+        for b in (self.peer_l, self.peer_o):
+            if b is not None:
+                b.close()
+        self.peer_l = self.peer_o = None
 
     def e2e(self, steps: int, warmup: int):
         torch = self.torch
@@ -684,6 +712,7 @@ class AttentionBwdWorkload(AttentionWorkload):
     S x S x D products), although the two-pass kernels recompute P and dP."""
     name = "fa2_bwd"
     metric = "fa2_bwd_causal_TFLOPS"
+    fused_gather = False
 
     def __init__(self, dist: Dist, args):
         super().__init__(dist, args)

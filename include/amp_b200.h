@@ -192,6 +192,20 @@ AMP_API int amp_gemm_fp8e4m3_ex_dev(const uint8_t* A, const uint8_t* B, const fl
 AMP_API int amp_flash_attn_fwd_bf16_dev(const void* Q, const void* K, const void* V, void* O,
                                         float* lse, int B, int Hq, int Hkv, int S_q, int S_kv,
                                         int head_dim, int causal, float scale, void* stream);
+/* (batch*head)-sharded attention with the all-gather of O and lse fused into
+ * the epilogue; replaces the per-rank launch + ncclAllGather of O / lse
+ * (include/collective.hpp:87-89).  Q, K, V hold this rank's slice (B*Hq and
+ * B*Hkv heads); O_peers / lse_peers are DEVICE arrays of `world` pointers to
+ * every rank's full O [bh_total][S_q][head_dim] bf16 and lse [bh_total][S_q]
+ * fp32 (amp_peer_buffer_create; lse_peers may be NULL); this rank's
+ * batch*head 0 is global index bh_base.  Mailboxes / seq / reuse rules as for
+ * amp_gemm_bf16_allgather_dev. */
+AMP_API int amp_flash_attn_fwd_allgather_dev(const void* Q, const void* K, const void* V,
+                                             void* const* O_peers, float* const* lse_peers,
+                                             int rank, int world, int bh_base,
+                                             void* const* mailboxes, unsigned seq, int B, int Hq,
+                                             int Hkv, int S_q, int S_kv, int head_dim, int causal,
+                                             float scale, void* stream);
 
 /* FlashAttention-2 backward (AMP has none; its forward's lse is "required for the
  * backward pass", kernels/flash_attn.cuh:48).  Inputs: the forward's Q, K, V, O

@@ -90,3 +90,28 @@ def test_rejects_head_dim_96(cuda, amp_lib):
     q, k, v = make_qkv(1, 2, 2, 128, 128, 96, seed=1)
     with pytest.raises(AmpError, match="head_dim"):
         run(q, k, v, True)
+
+
+@pytest.mark.parametrize("S,D", [(512, 128), (200, 128), (300, 64)])
+def test_allgather_attention_single_rank(S, D, cuda):
+    """The fused all-gather attention on a group of one: the epilogue's staged rows
+    land in the rank's own O / lse exactly as the plain kernel writes them."""
+    from amp_b200 import sharded
+    from amp_b200._lib import lib
+    from amp_b200.collective import CommGroup, PeerBuffer
+    B, H = 2, 3
+    g = torch.Generator(device="cuda").manual_seed(S + D)
+    q, k, v = (torch.randn(B, H, S, D, generator=g, device="cuda").to(torch.bfloat16)
+               for _ in range(3))
+    o_ref, l_ref = attention.flash_attn_fwd(q, k, v, True)
+    po = PeerBuffer(CommGroup(), B * H * S, D, torch.bfloat16)
+    pl = PeerBuffer(CommGroup(), B * H, S, torch.float32, mailboxes=po.mailboxes)
+    try:
+        for _ in range(2):
+            o, l = sharded.flash_attn_allgather(q, k, v, True, po, pl)
+            torch.cuda.synchronize()
+            assert torch.equal(o, o_ref) and torch.equal(l, l_ref)
+        assert lib().amp_device_status(1) == 0
+    finally:
+        pl.close()
+        po.close()

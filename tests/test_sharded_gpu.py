@@ -100,6 +100,22 @@ def _rank_main(rank, world, port, q):
         O, L = sharded.flash_attn_sharded(qa, ka, va, True)
         O_ref, L_ref = attention.flash_attn_fwd(qa, ka, va, True)
         assert torch.equal(O, O_ref) and torch.equal(L, L_ref)
+        # the same with the all-gather fused into the attention epilogue; S = 200
+        # leaves a partial last query tile
+        po = PeerBuffer(CommGroup.current(), 2 * 4 * 200, 128, torch.bfloat16)
+        pl = PeerBuffer(CommGroup.current(), 2 * 4, 200, torch.float32, mailboxes=po.mailboxes)
+        try:
+            qb, kb, vb = (t[:, :, :200].contiguous() for t in (qa, ka, va))
+            Ob_ref, Lb_ref = attention.flash_attn_fwd(qb, kb, vb, True)
+            for _ in range(2):
+                Of, Lf = sharded.flash_attn_allgather(qb, kb, vb, True, po, pl)
+                torch.cuda.synchronize()
+                assert torch.equal(Of, Ob_ref) and torch.equal(Lf, Lb_ref)
+                dist.barrier()
+            assert lib().amp_device_status(1) == 0
+        finally:
+            pl.close()
+            po.close()
         torch.cuda.synchronize()
         q.put((rank, "ok"))
     except Exception as e:
