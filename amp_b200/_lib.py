@@ -59,6 +59,7 @@ SIGNATURES: dict[str, tuple] = {
     "amp_paged_pack_block_table": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
     "amp_paged_pool_bytes": (_sz, [_i32, _i32, _i32]),
     "amp_gemm_fp32_dev": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp]),
+    "amp_gemm_fp32_3xtf32_dev": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "amp_gemm_fp32_tile_dev": (_i32, [_i32, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "amp_user_gemm_fp32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32]),
     "amp_peer_mailbox_bytes": (_sz, []),

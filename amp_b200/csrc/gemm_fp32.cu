@@ -12,10 +12,16 @@
 //
 // Accumulation is fp32 FFMA in k order within a thread, so results differ
 // from the CPU reference only by fp32 rounding of the summation order.
+//
+// This is the fp32 GEMM of the plugin contract.  A faster tensor-core form
+// (three TF32 products of a hi/lo split, amp_gemm_fp32_3xtf32_dev in
+// gemm_tc.cu) is opt-in only: its fp32 accumulation inside the tensor core
+// loses more than AMP's validator allows on its own harness inputs.
 #include "common.cuh"
 #include "runtime.h"
 
 namespace ampb {
+
 namespace {
 
 // Reads H consecutive floats at p and H at p + OFF into dst[0..2H) with the

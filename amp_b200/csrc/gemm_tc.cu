@@ -39,6 +39,7 @@
 // every peer's stores into this rank's C are visible.
 #include <cuda.h>
 
+#include <algorithm>
 #include <cfloat>
 #include <mutex>
 
@@ -395,6 +396,231 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ------------------------------------------------------------------ fp32 as 3 x TF32
+// C = A B in fp32 on the tensor cores (kind::tf32).  Each operand is split as
+// x = hi + lo with hi = x with its low 13 mantissa bits cleared (exactly a TF32
+// value) and lo = x - hi (exact in fp32, |lo| < 2^-10 |x|), and
+//   A B ~= hi(A) hi(B) + hi(A) lo(B) + lo(A) hi(B)
+// -- the dropped lo(A) lo(B) term and the TF32 reading of lo are ~2^-20 of
+// each product, so the result keeps fp32-level accuracy (the plugin's bound is
+// 1e-3 relative).  k_tf32_split writes hi and lo of A; k_tf32_split_t those of
+// B transposed to [N, K], so both operands are K-major (for MN-major 32-bit
+// operands the MMA wants a different shared-memory swizzle).  The GEMM streams
+// hi and lo tiles of A and B through one ring and issues three MMAs per K=8 step.
+constexpr uint32_t kTf32HiMask = 0xFFFFE000u;
+
+__global__ void __launch_bounds__(256) k_tf32_split(const float* __restrict__ x, int64_t n,
+                                                    float* __restrict__ hi, float* __restrict__ lo) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 4; i += stride) {
+        const float4 v = reinterpret_cast<const float4*>(x)[i];
+        float4 h, l;
+        h.x = __uint_as_float(__float_as_uint(v.x) & kTf32HiMask); l.x = v.x - h.x;
+        h.y = __uint_as_float(__float_as_uint(v.y) & kTf32HiMask); l.y = v.y - h.y;
+        h.z = __uint_as_float(__float_as_uint(v.z) & kTf32HiMask); l.z = v.z - h.z;
+        h.w = __uint_as_float(__float_as_uint(v.w) & kTf32HiMask); l.w = v.w - h.w;
+        reinterpret_cast<float4*>(hi)[i] = h;
+        reinterpret_cast<float4*>(lo)[i] = l;
+    }
+    for (int64_t i = n / 4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const float h = __uint_as_float(__float_as_uint(x[i]) & kTf32HiMask);
+        hi[i] = h;
+        lo[i] = x[i] - h;
+    }
+}
+
+// B [K, N] -> hi(B)^T, lo(B)^T [N, K]: 32 x 32 tiles through shared memory
+__global__ void __launch_bounds__(256) k_tf32_split_t(const float* __restrict__ b, int K, int N,
+                                                      float* __restrict__ hi_t,
+                                                      float* __restrict__ lo_t) {
+    __shared__ float tile[32][33];
+    const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8 threads
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+        const int k = k0 + ty + i, n = n0 + tx;
+        tile[ty + i][tx] = (k < K && n < N) ? b[(int64_t)k * N + n] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+        const int n = n0 + ty + i, k = k0 + tx;
+        if (n < N && k < K) {
+            const float v = tile[tx][ty + i];
+            const float h = __uint_as_float(__float_as_uint(v) & kTf32HiMask);
+            hi_t[(int64_t)n * K + k] = h;
+            lo_t[(int64_t)n * K + k] = v - h;
+        }
+    }
+}
+
+__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0;"
+        " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+template <int TBN>
+struct Tf32Cfg {
+    static constexpr int BK = SLAB / 4;                    // 32 K elements a stage
+    static constexpr int A_BYTES = BM * SLAB;              // [128 rows x 32 K] 16 KiB
+    static constexpr int B_BYTES = TBN * SLAB;             // [TBN rows x 32 K]
+    static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int STAGES = (200 * 1024) / STAGE;
+    static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
+    static constexpr uint32_t IDESC = make_idesc(2, 2, 0, 0, BM, TBN);   // TF32, both K-major
+};
+
+template <int TBN>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+                  const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
+                  float* __restrict__ C, int M, int N, int K, int* status) {
+    using CF = Tf32Cfg<TBN>;
+    constexpr int ST = CF::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * CF::STAGE);
+    uint64_t* empty = full + ST;
+    uint64_t* tfull = empty + ST;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_m = (M + BM - 1) / BM, num_n = (N + TBN - 1) / TBN;
+    const int num_kb = (K + CF::BK - 1) / CF::BK;
+    const int total = num_m * num_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 2 * TBN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                int tm, tn;
+                tile_coords(t, num_m, num_n, tm, tn);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1, status)) { ok = false; break; }
+                    uint8_t* st = smem + s * CF::STAGE;
+                    mbar_arrive_expect_tx(&full[s], CF::STAGE);
+                    tma_load_2d(st, &tmAh, &full[s], kb * CF::BK, tm * BM);
+                    tma_load_2d(st + CF::A_BYTES, &tmAl, &full[s], kb * CF::BK, tm * BM);
+                    tma_load_2d(st + 2 * CF::A_BYTES, &tmBh, &full[s], kb * CF::BK, tn * TBN);
+                    tma_load_2d(st + 2 * CF::A_BYTES + CF::B_BYTES, &tmBl, &full[s], kb * CF::BK,
+                                tn * TBN);
+                    if (++s == ST) { s = 0; ph ^= 1; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            int i = 0;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
+                const int acc = i & 1;
+                if (!mbar_wait(&tempty[acc], ((i >> 1) & 1) ^ 1, status)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * TBN;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&full[s], ph, status)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t ah = smem_u32(smem + s * CF::STAGE), al = ah + CF::A_BYTES;
+                    const uint32_t bh = ah + 2 * CF::A_BYTES, bl = bh + CF::B_BYTES;
+#pragma unroll
+                    for (int k = 0; k < SLAB / 32; ++k) {   // K = 8 (32 bytes) per MMA
+                        const uint64_t dah = smem_desc_sw128(ah + k * 32, 16, 1024);
+                        const uint64_t dal = smem_desc_sw128(al + k * 32, 16, 1024);
+                        const uint64_t dbh = smem_desc_sw128(bh + k * 32, 16, 1024);
+                        const uint64_t dbl = smem_desc_sw128(bl + k * 32, 16, 1024);
+                        // the two small cross terms first, then the large one
+                        tc_mma_tf32(d_tmem, dal, dbh, CF::IDESC, (kb | k) != 0);
+                        tc_mma_tf32(d_tmem, dah, dbl, CF::IDESC, 1);
+                        tc_mma_tf32(d_tmem, dah, dbh, CF::IDESC, 1);
+                    }
+                    tc_commit(&empty[s]);
+                    if (++s == ST) { s = 0; ph ^= 1; }
+                }
+                if (ok) tc_commit(&tfull[acc]);
+            }
+            tc_commit(drain);
+            mbar_wait(drain, 0, status);
+        }
+    } else {
+        const int quad = warp & 3;
+        const int row_in_tile = quad * 32 + lane;
+        int i = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
+            const int acc = i & 1;
+            int tm, tn;
+            tile_coords(t, num_m, num_n, tm, tn);
+            if (!mbar_wait_warp(&tfull[acc], (i >> 1) & 1, status)) break;
+            tc_fence_after();
+            const int row = tm * BM + row_in_tile;
+            const bool row_ok = row < M;
+            for (int c = 0; c < TBN / 32; ++c) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * TBN + c * 32, r);
+                tmem_ld_wait();
+                if (c == TBN / 32 - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[acc]);
+                }
+                const int col0 = tn * TBN + c * 32;
+                if (col0 >= N || !row_ok) continue;
+                float* out = C + (int64_t)row * N + col0;
+                if (col0 + 32 <= N && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        *reinterpret_cast<float4*>(out + j) =
+                            make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                        __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)   // constant indices: r stays in registers
+                        if (col0 + j < N) out[j] = __uint_as_float(r[j]);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 2 * TBN);
+    }
+}
+
 // ------------------------------------------------------------------ host side
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -430,8 +656,10 @@ int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int 
     cuuint64_t strides[1] = {(cuuint64_t)(cols * es)};
     cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(m, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
-                     2, const_cast<void*>(base), dims, strides, box, estr,
+    const CUtensorMapDataType dt = es == 4   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : es == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                             : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     AMPB_REQUIRE(r == CUDA_SUCCESS, AMP_ERR_INVALID,
@@ -556,11 +784,68 @@ int gemm_fp8_dev(const void* A, const void* B, const float* sa, const float* sb,
     }
 }
 
+// fp32 GEMM on the tensor cores (3 x TF32), opt-in.  Needs K and N multiples of 4 and
+// 16-byte aligned operands (TMA: the row pitch of A and of B^T is K * 4 bytes,
+// of C N * 4); the split operands live in library scratch
+// (staging slots 8 and 9), so calls on one device must be ordered.
+bool gemm_fp32_tc_eligible(const float* A, const float* B, const float* C, int M, int N, int K) {
+    return M >= 1 && N >= 1 && K >= 1 && K % 4 == 0 && N % 4 == 0 && aligned16(A) &&
+           aligned16(B) && aligned16(C);
+}
+
+int gemm_fp32_tc_dev(const float* A, const float* B, float* C, int M, int N, int K,
+                     cudaStream_t st) {
+    AMPB_REQUIRE(gemm_fp32_tc_eligible(A, B, C, M, N, K), AMP_ERR_UNSUPPORTED,
+                 "3xTF32 GEMM needs K, N multiples of 4 and 16-byte aligned operands");
+    const int64_t na = (int64_t)M * K, nb = (int64_t)K * N;
+    void *sa = nullptr, *sb = nullptr;
+    int rc;
+    if ((rc = staging_get(8, (size_t)na * 8, &sa))) return rc;
+    if ((rc = staging_get(9, (size_t)nb * 8, &sb))) return rc;
+    float* ah = static_cast<float*>(sa);
+    float* al = ah + na;
+    float* bh = static_cast<float*>(sb);
+    float* bl = bh + nb;
+    const int sgrid_a = (int)std::min<int64_t>((na / 4 + 255) / 256 + 1, (int64_t)sm_count() * 16);
+    k_tf32_split<<<sgrid_a, 256, 0, st>>>(A, na, ah, al);
+    AMPB_CHECK_LAUNCH("k_tf32_split");
+    k_tf32_split_t<<<dim3((N + 31) / 32, (K + 31) / 32), 256, 0, st>>>(B, K, N, bh, bl);
+    AMPB_CHECK_LAUNCH("k_tf32_split_t");
+    // 128-column tiles while they fill the machine, 64-column tiles otherwise
+    const int tbn = (int64_t)((M + BM - 1) / BM) * ((N + 127) / 128) >= sm_count() ? 128 : 64;
+    CUtensorMap tAh, tAl, tBh, tBl;
+    if ((rc = make_tmap(&tAh, ah, M, K, 4, BM)) || (rc = make_tmap(&tAl, al, M, K, 4, BM)) ||
+        (rc = make_tmap(&tBh, bh, N, K, 4, tbn)) || (rc = make_tmap(&tBl, bl, N, K, 4, tbn)))
+        return rc;
+    int* status = nullptr;
+    if ((rc = device_status(&status))) return rc;
+    auto go = [&](auto kern, int smem) {
+        AMPB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        const int64_t total = (int64_t)((M + BM - 1) / BM) * ((N + tbn - 1) / tbn);
+        const int grid = (int)std::min<int64_t>(total, sm_count());
+        kern<<<grid, kThreads, smem, st>>>(tAh, tAl, tBh, tBl, C, M, N, K, status);
+        AMPB_CHECK_LAUNCH("k_gemm_tf32x3");
+        return AMP_OK;
+    };
+    if (tbn == 128) return go(k_gemm_tf32x3<128>, Tf32Cfg<128>::SMEM);
+    return go(k_gemm_tf32x3<64>, Tf32Cfg<64>::SMEM);
+}
+
 }  // namespace ampb
 
 using namespace ampb;
 
 extern "C" {
+
+// C = A B for fp32 row-major operands as three TF32 products on the tensor cores
+// (see gemm_fp32_tc_dev).  Opt-in: the tensor core's fp32 accumulation makes the
+// error grow with K (max_rel_err 1.9e-4 / 6e-4 / 1.5e-3 at 1024 / 2048 / 4096
+// cubed for U[-1,1] inputs, against 3e-5 .. 1.7e-4 for amp_gemm_fp32_dev).
+int amp_gemm_fp32_3xtf32_dev(const float* A, const float* B, float* C, int M, int N, int K,
+                             void* stream) {
+    AMPB_REQUIRE(M >= 1 && N >= 1 && K >= 1 && A && B && C, AMP_ERR_INVALID, "bad GEMM arguments");
+    return gemm_fp32_tc_dev(A, B, C, M, N, K, as_stream(stream));
+}
 
 int amp_gemm_bf16_dev(const void* A, const void* B, void* C, int c_dtype, int M, int N, int K,
                       void* stream) {

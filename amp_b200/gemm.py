@@ -56,6 +56,19 @@ def matmul_fp32(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
     return C
 
 
+def matmul_fp32_3xtf32(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
+    """C = A @ B for fp32 operands on the tensor cores (three TF32 products),
+    opt-in: faster than matmul_fp32 at large sizes, with an error that grows with
+    K (see amp_gemm_fp32_3xtf32_dev)."""
+    M, K = A.shape
+    N = B.shape[1]
+    _check(A, torch.float32, (M, K), "A")
+    _check(B, torch.float32, (K, N), "B")
+    C = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    call("amp_gemm_fp32_3xtf32_dev", A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, _stream(A))
+    return C
+
+
 AMP_DTYPE = {torch.float32: 0, torch.bfloat16: 1}
 
 

@@ -131,6 +131,15 @@ AMP_API int amp_gemm_fp32_dev(const float* A, const float* B, float* C, int M, i
 AMP_API int amp_gemm_fp32_tile_dev(int bm, int bn, int bk, const float* A, const float* B,
                                    float* C, int M, int N, int K, void* stream);
 
+/* fp32 C = A B (row-major) on the tensor cores as three TF32 products of a
+ * hi/lo split of each operand, opt-in: ~5x the FFMA kernel's rate at 4096^3, but
+ * the tensor core's fp32 accumulation makes the error grow with K (max_rel_err
+ * 1.9e-4 at 1024^3 for U[-1,1] inputs; AMP's validator inputs in [-10, 10] fail
+ * its 1e-3 bar), so amp_gemm_fp32_dev / the plugin stay on FFMA.  K and N must be
+ * multiples of 4 and the operands 16-byte aligned; uses library scratch (calls on
+ * one device must be ordered). */
+AMP_API int amp_gemm_fp32_3xtf32_dev(const float* A, const float* B, float* C, int M, int N,
+                                     int K, void* stream);
 /* ------------------------------------------------------------------------
  * Tensor-core GEMM (tcgen05), row-major C[M,N] = A[M,K] * B[K,N].
  * bf16: replaces AMP::launch_matmul_bf16 (kernels/matmul.cuh:103-105,

@@ -111,3 +111,20 @@ def test_parity_dump_tool_schema_and_values(tmp_path, cuda, amp_lib):
         assert set(t) == {"bm", "bn", "bk", "gflops", "latency_ms", "max_rel_err_vs_cpu", "output"}
         # parity_check.py's rule: |a-b|/max(1,|b|) < 1e-3 (dump values carry 6 digits)
         assert oracle.max_rel_err(np.asarray(t["output"]).reshape(96, 96), ref) < TOL
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 1024, 1024), (300, 200, 516), (7, 1000, 64)])
+def test_3xtf32_opt_in_path(M, N, K, cuda, amp_lib):
+    """The opt-in tensor-core fp32 GEMM (three TF32 products): within the 1e-3 bar
+    on U[-1,1] inputs at these sizes; ragged M/N and tiles past the edges included."""
+    A, B = workloads.gemm_fp32_inputs(M, N, K, seed=3)
+    C = gemm.matmul_fp32_3xtf32(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())
+    torch.cuda.synchronize()
+    assert oracle.max_rel_err(C.cpu().numpy(), oracle.gemm_f64(A, B)) < 5e-4
+
+
+def test_3xtf32_rejects_shapes_tma_cannot_load(cuda, amp_lib):
+    A = torch.zeros(8, 6, device="cuda")
+    B = torch.zeros(6, 8, device="cuda")
+    with pytest.raises(AmpError):
+        gemm.matmul_fp32_3xtf32(A, B)
