@@ -46,6 +46,17 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Device helpers
 // ---------------------------------------------------------------------------
 
+// Programmatic dependent launch (kernels launched with launch_pdl): `pdl_wait`
+// blocks until the kernel before this one in the stream has completed and its
+// memory is visible -- called first thing, before this kernel reads or writes
+// anything the previous one touches; `pdl_trigger` lets the next kernel's CTAs
+// start launching (they wait in their own pdl_wait) while this grid finishes.
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Streaming 128-bit global load that bypasses L1 allocation (read-once data).
 __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
     uint4 v;

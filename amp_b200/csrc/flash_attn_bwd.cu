@@ -99,6 +99,8 @@ template <int D>
 __global__ void __launch_bounds__(256) k_fa_bwd_delta(const __nv_bfloat16* __restrict__ O,
                                                       const __nv_bfloat16* __restrict__ dO,
                                                       float* __restrict__ delta, int64_t rows) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     for (int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); r < rows;
          r += (int64_t)gridDim.x * 8) {
@@ -156,6 +158,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     k_fa_bwd_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                   const BwdParams p) {
+    pdl_wait();
+    pdl_trigger();
     using CF = BwdCfg<D>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -429,6 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     k_fa_bwd_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                 const BwdParams p) {
+    pdl_wait();
+    pdl_trigger();
     using CF = BwdCfg<D>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -683,9 +689,9 @@ int launch_bwd(const void* Q, const void* K, const void* V, const void* O, const
     p.status = status;
     const int64_t rows = (int64_t)B * Hq * S_q;
     const int dgrid = (int)std::min<int64_t>((rows + 7) / 8, (int64_t)sm_count() * 16);
-    k_fa_bwd_delta<D><<<dgrid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(O),
-                                             static_cast<const __nv_bfloat16*>(dO), delta, rows);
-    AMPB_CHECK_LAUNCH("k_fa_bwd_delta");
+    AMPB_CHECK_CUDA(launch_pdl(k_fa_bwd_delta<D>, dim3(dgrid), dim3(256), 0, st,
+                               static_cast<const __nv_bfloat16*>(O),
+                               static_cast<const __nv_bfloat16*>(dO), delta, rows));
     constexpr int SMEM_KV = 6 * CF::TILE + 2 * 2 * BT * 4 + 1024 + 256;
     constexpr int SMEM_Q = 6 * CF::TILE + 1024 + 256;
     static std::atomic<uint64_t> attr_done{0};
@@ -698,11 +704,10 @@ int launch_bwd(const void* Q, const void* K, const void* V, const void* O, const
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_Q));
         if (dev < 64) attr_done.fetch_or(1ull << dev);
     }
-    k_fa_bwd_dkdv<D><<<dim3((S_kv + BT - 1) / BT, B * Hkv), kThreads, SMEM_KV, st>>>(tq, tk, tv,
-                                                                                       to, p);
-    AMPB_CHECK_LAUNCH("k_fa_bwd_dkdv");
-    k_fa_bwd_dq<D><<<dim3((S_q + BT - 1) / BT, B * Hq), kThreads, SMEM_Q, st>>>(tq, tk, tv, to, p);
-    AMPB_CHECK_LAUNCH("k_fa_bwd_dq");
+    AMPB_CHECK_CUDA(launch_pdl(k_fa_bwd_dkdv<D>, dim3((S_kv + BT - 1) / BT, B * Hkv),
+                               dim3(kThreads), SMEM_KV, st, tq, tk, tv, to, p));
+    AMPB_CHECK_CUDA(launch_pdl(k_fa_bwd_dq<D>, dim3((S_q + BT - 1) / BT, B * Hq), dim3(kThreads),
+                               SMEM_Q, st, tq, tk, tv, to, p));
     return AMP_OK;
 }
 

@@ -55,6 +55,8 @@ __device__ __forceinline__ float block_max(float f) {
 __global__ void __launch_bounds__(kThreads) k_amax_partials(const uint16_t* __restrict__ x,
                                                             int64_t n, float* __restrict__ parts,
                                                             int vec_ok) {
+    pdl_wait();
+    pdl_trigger();
     uint32_t m = 0;
     const int64_t nthr = (int64_t)gridDim.x * kThreads;
     const int64_t tid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
@@ -112,6 +114,8 @@ __global__ void __launch_bounds__(kThreads) k_quant_encode(
     const uint16_t* __restrict__ x, int64_t n, const float* __restrict__ parts, int nparts,
     const float* __restrict__ amax_in, uint8_t* __restrict__ q, float* __restrict__ scale_out,
     float* __restrict__ amax_out, int vec_ok) {
+    pdl_wait();
+    pdl_trigger();
     float amax;
     if (amax_in) {
         amax = *amax_in;
@@ -165,6 +169,8 @@ __device__ __forceinline__ void dec16_store(uint4 v, float s, uint16_t* dst) {
 __global__ void __launch_bounds__(kThreads) k_dequant(const uint8_t* __restrict__ q, int64_t n,
                                                      const float* __restrict__ scale,
                                                      uint16_t* __restrict__ y, int vec_ok) {
+    pdl_wait();
+    pdl_trigger();
     const float s = *scale;
     const int64_t nthr = (int64_t)gridDim.x * kThreads;
     const int64_t tid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
@@ -200,6 +206,8 @@ inline int grid_for(int64_t work_items) {
 __global__ void __launch_bounds__(kThreads) k_amax_fold_exchange(
     const float* __restrict__ parts, int nparts, float* amax_out,
     unsigned long long* const* mbox, int rank, int world, unsigned seq, int* status) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ unsigned got[kMaxPeers];
     float m = 0.0f;
     for (int i = threadIdx.x; i < nparts; i += kThreads) m = fmaxf(m, parts[i]);
@@ -218,8 +226,8 @@ int launch_amax(const void* x, int64_t n, float* parts, int* nparts_out, cudaStr
     const int vec = aligned16(x);
     const int grid = grid_for(vec ? (n >> 3) : n);
     *nparts_out = grid;
-    k_amax_partials<<<grid, kThreads, 0, st>>>(static_cast<const uint16_t*>(x), n, parts, vec);
-    AMPB_CHECK_LAUNCH("k_amax_partials");
+    AMPB_CHECK_CUDA(launch_pdl(k_amax_partials, dim3(grid), dim3(kThreads), 0, st,
+                               static_cast<const uint16_t*>(x), n, parts, vec));
     return AMP_OK;
 }
 
@@ -229,17 +237,17 @@ int launch_encode(const void* x, int64_t n, const float* parts, int nparts, cons
                   uint8_t* q, float* scale_out, float* amax_out, cudaStream_t st) {
     const int vec = aligned16(x) && aligned16(q);
     const int grid = grid_deep(vec ? (n >> 4) : n, kEncodeBlocksPerSM);
-    k_quant_encode<<<grid, kThreads, 0, st>>>(static_cast<const uint16_t*>(x), n, parts, nparts,
-                                              amax_in, q, scale_out, amax_out, vec);
-    AMPB_CHECK_LAUNCH("k_quant_encode");
+    AMPB_CHECK_CUDA(launch_pdl(k_quant_encode, dim3(grid), dim3(kThreads), 0, st,
+                               static_cast<const uint16_t*>(x), n, parts, nparts, amax_in, q,
+                               scale_out, amax_out, vec));
     return AMP_OK;
 }
 
 int launch_dequant(const uint8_t* q, int64_t n, const float* scale, void* y, cudaStream_t st) {
     const int vec = aligned16(q) && aligned16(y);
     const int grid = grid_deep(vec ? (n >> 4) : n, kDequantBlocksPerSM);
-    k_dequant<<<grid, kThreads, 0, st>>>(q, n, scale, static_cast<uint16_t*>(y), vec);
-    AMPB_CHECK_LAUNCH("k_dequant");
+    AMPB_CHECK_CUDA(launch_pdl(k_dequant, dim3(grid), dim3(kThreads), 0, st, q, n, scale,
+                               static_cast<uint16_t*>(y), vec));
     return AMP_OK;
 }
 

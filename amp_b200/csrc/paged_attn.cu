@@ -198,6 +198,8 @@ __device__ void page_prefix(const DecodeParams& p, int* out, int* scratch, bool 
 
 // Large batches: the prefix sums once, in global memory, before the decode.
 __global__ void __launch_bounds__(1024) k_paged_plan(const DecodeParams p) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ int scratch[33];
     page_prefix<1024>(p, p.pref, scratch, true);
 }
@@ -207,6 +209,8 @@ __global__ void __launch_bounds__(kThreads) k_paged_decode(const __grid_constant
                                                            const __grid_constant__ CUtensorMap tmV,
                                                            const DecodeParams p) {
     static_assert(G >= 1 && G <= 8, "one n8 tile holds the GQA group");
+    pdl_wait();
+    pdl_trigger();
     constexpr int D = 128;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t c = blockIdx.x;
@@ -453,6 +457,8 @@ constexpr int kCombineWarps = 8;
 template <int D>
 __global__ void __launch_bounds__(kCombineWarps * 32) k_paged_combine(const DecodeParams p) {
     static_assert(D == 128, "one float4 per lane covers D");
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[kCombineWarps];
     __shared__ float o_s[kCombineWarps][D];
     __shared__ float l_s[kCombineWarps];
@@ -573,8 +579,7 @@ int paged_decode_dev(const void* q, const void* k_pool, const void* v_pool, cons
     p.n_cta = 0;   // set per kernel below, from its occupancy
     p.plan_in_kernel = B <= kSmemSeqs;
     if (!p.plan_in_kernel) {
-        k_paged_plan<<<1, 1024, 0, st>>>(p);
-        AMPB_CHECK_LAUNCH("k_paged_plan");
+        AMPB_CHECK_CUDA(launch_pdl(k_paged_plan, dim3(1), dim3(1024), 0, st, p));
     }
     // persistent grid: as many CTAs as are resident at once (per device and
     // group size, from the occupancy calculator), never more than the pages need
@@ -593,7 +598,7 @@ int paged_decode_dev(const void* q, const void* k_pool, const void* v_pool, cons
         const int64_t total_pages = (int64_t)Hkv * B * p.max_ctx_pages;
         const int64_t by_size = (total_pages + kMinPages - 1) / kMinPages;
         p.n_cta = (int)std::max<int64_t>(1, std::min<int64_t>(resident.load(), by_size));
-        kern<<<p.n_cta, kThreads, kDecodeSmem, st>>>(tmK, tmV, p);
+        AMPB_CHECK_CUDA(launch_pdl(kern, dim3(p.n_cta), dim3(kThreads), kDecodeSmem, st, tmK, tmV, p));
         return AMP_OK;
     };
     static std::atomic<int> res1[32], res2[32], res4[32], res8[32];
@@ -608,8 +613,7 @@ int paged_decode_dev(const void* q, const void* k_pool, const void* v_pool, cons
     }
     if (rc) return rc;
     AMPB_CHECK_LAUNCH("k_paged_decode");
-    k_paged_combine<128><<<B * Hq, kCombineWarps * 32, 0, st>>>(p);
-    AMPB_CHECK_LAUNCH("k_paged_combine");
+    AMPB_CHECK_CUDA(launch_pdl(k_paged_combine<128>, dim3(B * Hq), dim3(kCombineWarps * 32), 0, st, p));
     return AMP_OK;
 }
 

@@ -2,6 +2,8 @@
 #pragma once
 #include <cstddef>
 
+#include <cuda_runtime.h>
+
 namespace ampb {
 
 // Returns a device buffer of at least `bytes` for staging slot `slot` on the
@@ -12,5 +14,24 @@ int staging_get(int slot, size_t bytes, void** out);
 // Per-device status word written by kernels whose bounded waits expired
 // (AMP_DEV_ERR_TIMEOUT); allocated and zeroed on first use.
 int device_status(int** out);
+
+// Launch with programmatic stream serialization: the kernel may start while the
+// previous kernel in the stream drains; it must call pdl_wait() (common.cuh)
+// before touching that kernel's data.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
 
 }  // namespace ampb
