@@ -581,17 +581,13 @@ int launch_fa(const void* Q, const void* K, const void* V, void* O, float* lse, 
 
 }  // namespace
 
-namespace {
-int fa_encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
-              const cuuint64_t* strides, const cuuint32_t* box);
-}  // namespace
 
 // [bh][s][d] bf16 tensor as a 3-D TMA map, box [1][128][64], 128-byte swizzle.
 int fa_make_tmap_3d(CUtensorMap* m, const void* base, int64_t d, int64_t s, int64_t bh) {
     cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)s, (cuuint64_t)bh};
     cuuint64_t strides[2] = {(cuuint64_t)(d * 2), (cuuint64_t)(s * d * 2)};
     cuuint32_t box[3] = {64, 128, 1};
-    return fa_encode(m, base, 3, dims, strides, box);
+    return encode_tmap(m, base, 2, 3, dims, strides, box);
 }
 
 // Paged pool [pages][hkv][16][d] bf16 as a 4-D TMA map, box = one page of one
@@ -602,34 +598,9 @@ int fa_make_tmap_pool(CUtensorMap* m, const void* base, int64_t d, int64_t hkv, 
     cuuint64_t strides[3] = {(cuuint64_t)(d * 2), (cuuint64_t)(kPageTokens * d * 2),
                              (cuuint64_t)(hkv * kPageTokens * d * 2)};
     cuuint32_t box[4] = {64, (cuuint32_t)kPageTokens, 1, 1};
-    return fa_encode(m, base, 4, dims, strides, box);
+    return encode_tmap(m, base, 2, 4, dims, strides, box);
 }
 
-namespace {
-int fa_encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
-              const cuuint64_t* strides, const cuuint32_t* box) {
-    using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                       const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                       const cuuint32_t*, CUtensorMapInterleave,
-                                       CUtensorMapSwizzle, CUtensorMapL2promotion,
-                                       CUtensorMapFloatOOBfill);
-    static EncodeTiledFn enc = nullptr;
-    if (!enc) {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        AMPB_CHECK_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
-        AMPB_REQUIRE(q == cudaDriverEntryPointSuccess && fn, AMP_ERR_UNSUPPORTED,
-                     "cuTensorMapEncodeTiled not available");
-        enc = (EncodeTiledFn)fn;
-    }
-    cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims,
-                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    AMPB_REQUIRE(r == CUDA_SUCCESS, AMP_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-    return AMP_OK;
-}
-}  // namespace
 
 int flash_attn_fwd_dev(const void* Q, const void* K, const void* V, void* O, float* lse, int B,
                        int Hq, int Hkv, int S_q, int S_kv, int D, int causal, int causal_offset,

@@ -622,50 +622,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host side
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-int get_encode_fn(EncodeTiledFn* out) {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    static cudaError_t err = cudaSuccess;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-        if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = (EncodeTiledFn)p;
-    });
-    if (!fn) {
-        if (err != cudaSuccess) return cuda_status(err, "cudaGetDriverEntryPoint");
-        set_error(AMP_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled not available from the driver");
-        return AMP_ERR_UNSUPPORTED;
-    }
-    *out = fn;
-    return AMP_OK;
-}
-
 // Row-major [rows, cols] matrix of `es`-byte elements, box [box_rows, 128 bytes], 128B swizzle.
 int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int es,
               int box_rows) {
-    EncodeTiledFn enc;
-    int rc = get_encode_fn(&enc);
-    if (rc) return rc;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(cols * es)};
     cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    const CUtensorMapDataType dt = es == 4   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
-                                   : es == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                             : CU_TENSOR_MAP_DATA_TYPE_UINT8;
-    CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    AMPB_REQUIRE(r == CUDA_SUCCESS, AMP_ERR_INVALID,
-                 "cuTensorMapEncodeTiled failed (%d) for a %lld x %lld matrix", (int)r,
-                 (long long)rows, (long long)cols);
-    return AMP_OK;
+    return encode_tmap(m, base, es, 2, dims, strides, box);
 }
 
 struct AllGather {

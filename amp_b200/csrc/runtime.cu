@@ -42,6 +42,41 @@ int sm_count() {
     return cache[dev];
 }
 
+namespace {
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+}  // namespace
+
+int encode_tmap(CUtensorMap* m, const void* base, int es, int rank, const cuuint64_t* dims,
+                const cuuint64_t* strides, const cuuint32_t* box) {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    static cudaError_t err = cudaSuccess;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+        if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = (EncodeTiledFn)p;
+    });
+    if (!fn) {
+        if (err != cudaSuccess) return cuda_status(err, "cudaGetDriverEntryPoint");
+        set_error(AMP_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled not available from the driver");
+        return AMP_ERR_UNSUPPORTED;
+    }
+    const CUtensorMapDataType dt = es == 4   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : es == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                             : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    const CUresult r = fn(m, dt, (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    AMPB_REQUIRE(r == CUDA_SUCCESS, AMP_ERR_INVALID,
+                 "cuTensorMapEncodeTiled failed (%d) for a rank-%d tensor", (int)r, rank);
+    return AMP_OK;
+}
+
 // Grow-only per-device staging buffers for the host-pointer entry points, so
 // that repeated amp_user_* calls do not pay cudaMalloc/cudaFree each time.
 namespace {

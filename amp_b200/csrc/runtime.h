@@ -2,6 +2,7 @@
 #pragma once
 #include <cstddef>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace ampb {
@@ -14,6 +15,12 @@ int staging_get(int slot, size_t bytes, void** out);
 // Per-device status word written by kernels whose bounded waits expired
 // (AMP_DEV_ERR_TIMEOUT); allocated and zeroed on first use.
 int device_status(int** out);
+
+// cuTensorMapEncodeTiled from the driver (looked up once, thread-safe) applied
+// with the library's fixed options: bf16 / fp32 / u8 elements (es 2 / 4 / 1),
+// no interleave, 128-byte swizzle, 256-byte L2 promotion, zero out-of-bounds fill.
+int encode_tmap(CUtensorMap* m, const void* base, int es, int rank, const cuuint64_t* dims,
+                const cuuint64_t* strides, const cuuint32_t* box);
 
 // Launch with programmatic stream serialization: the kernel may start while the
 // previous kernel in the stream drains; it must call pdl_wait() (common.cuh)
