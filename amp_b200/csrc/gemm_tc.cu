@@ -40,6 +40,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cfloat>
 #include <mutex>
 
@@ -699,14 +700,14 @@ int launch_tc(const void* A, const void* B, void* C, int M, int N, int K, const 
     }
     if (amax) AMPB_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st));
     auto kern = ag ? k_gemm_tc<kFP8, OutT, true> : k_gemm_tc<kFP8, OutT, false>;
-    static uint64_t attr_done[2] = {0, 0};  // one bit per device ordinal (< 64) and mode
+    static std::atomic<uint64_t> attr_done[2];  // one bit per device ordinal (< 64) and mode
     int dev = 0;
     AMPB_CHECK_CUDA(cudaGetDevice(&dev));
-    uint64_t& done_bits = attr_done[ag ? 1 : 0];
-    if (dev >= 64 || !(done_bits >> dev & 1)) {
+    std::atomic<uint64_t>& done_bits = attr_done[ag ? 1 : 0];
+    if (dev >= 64 || !(done_bits.load() >> dev & 1)) {
         AMPB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              ag ? SMEM_BYTES_AG : SMEM_BYTES));
-        if (dev < 64) done_bits |= 1ull << dev;
+        if (dev < 64) done_bits.fetch_or(1ull << dev);
     }
     const int total = p.num_m * p.num_n;
     const int grid = total < sm_count() ? total : sm_count();
@@ -783,7 +784,15 @@ int gemm_fp32_tc_dev(const float* A, const float* B, float* C, int M, int N, int
     int* status = nullptr;
     if ((rc = device_status(&status))) return rc;
     auto go = [&](auto kern, int smem) {
-        AMPB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        static std::atomic<uint64_t> attr_done[2];   // one bit per device ordinal and tile width
+        int dev = 0;
+        AMPB_CHECK_CUDA(cudaGetDevice(&dev));
+        std::atomic<uint64_t>& bits = attr_done[tbn == 128 ? 1 : 0];
+        if (dev >= 64 || !(bits.load() >> dev & 1)) {
+            AMPB_CHECK_CUDA(
+                cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            if (dev < 64) bits.fetch_or(1ull << dev);
+        }
         const int64_t total = (int64_t)((M + BM - 1) / BM) * ((N + tbn - 1) / tbn);
         const int grid = (int)std::min<int64_t>(total, sm_count());
         kern<<<grid, kThreads, smem, st>>>(tAh, tAl, tBh, tBl, C, M, N, K, status);
