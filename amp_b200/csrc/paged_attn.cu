@@ -475,40 +475,58 @@ __global__ void __launch_bounds__(kCombineWarps * 32) k_paged_combine(const Deco
         n_rows = (int)min((int64_t)p.rows, (sl.owner(fb + pages - 1) - sl.owner(fb) + 1) * kCWarps);
     }
     const int64_t row0 = (int64_t)bh * p.rows;
-    // M = max over the rows' maxima
-    float M = -INFINITY;
-    for (int r = threadIdx.x; r < n_rows; r += kCombineWarps * 32) M = fmaxf(M, p.part_ml[(row0 + r) * 2]);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    if (lane == 0) red[warp] = M;
-    __syncthreads();
-    M = red[0];
-#pragma unroll
-    for (int w = 1; w < kCombineWarps; ++w) M = fmaxf(M, red[w]);
-    // this warp's rows
+    // One pass: each warp folds its rows (every kCombineWarps-th) into a running
+    // (max, sum, O) with the online rescale, four rows loaded ahead; the warps'
+    // states merge through shared memory.
+    float Mw = -INFINITY, Lw = 0.0f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float L = 0.0f;
-#pragma unroll 4
-    for (int r = warp; r < n_rows; r += kCombineWarps) {
-        const float2 ml = *reinterpret_cast<const float2*>(p.part_ml + (row0 + r) * 2);
-        const float4 v = *reinterpret_cast<const float4*>(p.part_o + (row0 + r) * D + 4 * lane);
-        const float a = (ml.x == -INFINITY) ? 0.0f : ex2_approx(ml.x - M);
-        L += a * ml.y;
-        acc.x += a * v.x;
-        acc.y += a * v.y;
-        acc.z += a * v.z;
-        acc.w += a * v.w;
+    for (int r0 = warp; r0 < n_rows; r0 += 4 * kCombineWarps) {
+        float2 ml[4];
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int r = r0 + u * kCombineWarps;
+            if (r < n_rows) {
+                ml[u] = *reinterpret_cast<const float2*>(p.part_ml + (row0 + r) * 2);
+                v[u] = *reinterpret_cast<const float4*>(p.part_o + (row0 + r) * D + 4 * lane);
+            } else {
+                ml[u] = make_float2(-INFINITY, 0.0f);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (ml[u].x == -INFINITY) continue;   // warp-uniform: a row that saw no page
+            if (ml[u].x > Mw) {
+                const float sc = (Mw == -INFINITY) ? 0.0f : ex2_approx(Mw - ml[u].x);
+                Lw *= sc;
+                acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+                Mw = ml[u].x;
+            }
+            const float a = ex2_approx(ml[u].x - Mw);
+            Lw += a * ml[u].y;
+            acc.x += a * v[u].x;
+            acc.y += a * v[u].y;
+            acc.z += a * v[u].z;
+            acc.w += a * v[u].w;
+        }
     }
     *reinterpret_cast<float4*>(&o_s[warp][4 * lane]) = acc;
-    if (lane == 0) l_s[warp] = L;
+    if (lane == 0) {
+        l_s[warp] = Lw;
+        red[warp] = Mw;
+    }
     __syncthreads();
     if (threadIdx.x < D) {
         const int d = threadIdx.x;
+        float M = red[0];
+#pragma unroll
+        for (int w = 1; w < kCombineWarps; ++w) M = fmaxf(M, red[w]);
         float O = 0.0f, Lt = 0.0f;
 #pragma unroll
         for (int w = 0; w < kCombineWarps; ++w) {
-            O += o_s[w][d];
-            Lt += l_s[w];
+            const float sc = (red[w] == -INFINITY) ? 0.0f : ex2_approx(red[w] - M);
+            O += sc * o_s[w][d];
+            Lt += sc * l_s[w];
         }
         p.out[(int64_t)bh * D + d] = __float2bfloat16_rn(Lt > 0.0f ? O / Lt : 0.0f);
         if (d == 0 && p.lse) {
