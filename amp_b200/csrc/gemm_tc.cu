@@ -397,6 +397,341 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ------------------------------------------------------------------ 2-SM tiles
+// A cluster of two CTAs (a pair) computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2: each CTA loads its 128 rows of A and its 128 columns
+// of B, and holds its 128 rows of the accumulator in its own TMEM, so each SM
+// streams two thirds of the operand bytes of a 128 x 256 single-SM tile.  Only
+// the leader (cluster rank 0) issues MMAs; both CTAs' TMA loads count on the
+// leader's full barriers; the leader's commits arrive on both CTAs' barriers
+// (tcgen05.commit multicast); the peer's epilogue releases the accumulator on the
+// leader's barrier.  No TMA load uses multicast.
+constexpr int STAGES2 = 6;
+constexpr int STAGE2_BYTES = A_STAGE_BYTES + (BN / 2) * SLAB;   // 16 KiB A + 16 KiB B
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+// shared::cluster address of this CTA's object `p` in the CTA of cluster rank `r`
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t r) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(r));
+    return a;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+                 : "memory");
+}
+// bounded wait with cluster-scope acquire (arrivals come from the other CTA too)
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* status) {
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t n = 0;
+    while (true) {
+        uint32_t ok;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;"
+            " selp.u32 %0, 1, 0, p; }"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if ((++n & 1023u) == 0) {
+            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+                atomicExch(status, AMP_DEV_ERR_TIMEOUT);
+                return false;
+            }
+            if (*reinterpret_cast<volatile int*>(status) != AMP_DEV_OK) return false;
+        }
+    }
+}
+// this CTA's box, completion counted on the barrier at cluster address `bar`
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* m, uint32_t bar,
+                                                 int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+template <bool kFP8>
+__device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+    if constexpr (kFP8)
+        asm volatile(
+            "{ .reg .pred p; setp.ne.b32 p, %4, 0;"
+            " tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    else
+        asm volatile(
+            "{ .reg .pred p; setp.ne.b32 p, %4, 0;"
+            " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+            : "memory");
+}
+// arrive on the barrier at this offset in both CTAs of the pair once the pair's
+// MMAs issued so far have completed
+__device__ __forceinline__ void tc_commit_pair_mc(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], %1;" ::"r"(smem_u32(bar)), "h"((uint16_t)3)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
+template <bool kFP8, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const TcParams p) {
+    constexpr int ES = kFP8 ? 1 : 2;                 // element size
+    constexpr int BK = SLAB / ES;                    // K elements per stage
+    constexpr int UMMA_K = 32 / ES;                  // K per MMA (32 bytes)
+    constexpr int B_BOX_COLS = SLAB / ES;            // N columns per B box
+    constexpr int B_BOXES = (BN / 2) / B_BOX_COLS;   // this CTA's half of N: 2 (bf16) or 1 (fp8)
+    constexpr int B_BOX_BYTES = BK * SLAB;           // 8 KiB or 16 KiB
+    // the pair's MMA: M = 256 (128 rows from each CTA), N = 256 (128 columns from each)
+    constexpr uint32_t IDESC = make_idesc(kFP8 ? 0 : 1, kFP8 ? 0 : 1, 0, 1, 2 * BM, BN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES);
+    uint64_t* empty = full + STAGES2;
+    uint64_t* tfull = empty + STAGES2;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();        // 0: the pair's leader, 1: its peer
+    const bool leader = rank == 0;
+    const int pair = (int)blockIdx.x >> 1, n_pairs = (int)gridDim.x >> 1;
+    const int total = p.num_m * p.num_n;            // 256 x 256 tiles
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES2; ++s) {
+            mbar_init(&full[s], 1);      // leader: its producer's expect_tx, both CTAs' bytes
+            mbar_init(&empty[s], 1);     // each CTA: the leader's multicast commit
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);     // each CTA: the leader's multicast commit
+            mbar_init(&tempty[b], 8);    // leader: the epilogue warps of both CTAs
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();   // both CTAs' barriers initialised and TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = pair; t < total && ok; t += n_pairs) {
+                int tm, tn;
+                tile_coords(t, p.num_m, p.num_n, tm, tn);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1, p.status)) { ok = false; break; }
+                    uint8_t* sa = smem + s * STAGE2_BYTES;
+                    uint8_t* sb = sa + A_STAGE_BYTES;
+                    // the leader's full barrier counts the bytes of both CTAs' loads
+                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * STAGE2_BYTES);
+                    const uint32_t fb = cluster_addr(&full[s], 0);
+                    tma_load_2d_pair(sa, &tmA, fb, kb * BK, tm * 2 * BM + (int)rank * BM);
+#pragma unroll
+                    for (int j = 0; j < B_BOXES; ++j)
+                        tma_load_2d_pair(sb + j * B_BOX_BYTES, &tmB, fb,
+                                         tn * BN + (int)rank * (BN / 2) + j * B_BOX_COLS, kb * BK);
+                    if (++s == STAGES2) { s = 0; ph ^= 1; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            int i = 0;
+            for (int t = pair; t < total && ok; t += n_pairs, ++i) {
+                const int acc = i & 1;
+                const uint32_t acc_ph = (i >> 1) & 1;
+                if (!mbar_wait_cluster(&tempty[acc], acc_ph ^ 1, p.status)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait_cluster(&full[s], ph, p.status)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + s * STAGE2_BYTES);
+                    const uint32_t sb = sa + A_STAGE_BYTES;
+#pragma unroll
+                    for (int k = 0; k < SLAB / 32; ++k) {
+                        const uint64_t ad = smem_desc_sw128(sa + k * 32, 16, 1024);
+                        const uint64_t bd = smem_desc_sw128(sb + k * UMMA_K * SLAB, B_BOX_BYTES, 1024);
+                        tc_mma_pair<kFP8>(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+                    }
+                    tc_commit_pair_mc(&empty[s]);
+                    if (++s == STAGES2) { s = 0; ph ^= 1; }
+                }
+                if (ok) tc_commit_pair_mc(&tfull[acc]);
+            }
+            // Every MMA of the pair has finished before TMEM is freed or the peer exits.
+            tc_commit_pair(drain);
+            mbar_wait(drain, 0, p.status);
+        }
+    } else {
+        const int quad = warp & 3;             // TMEM lanes [32*quad, 32*quad + 32)
+        const int row_in_tile = quad * 32 + lane;
+        const uint32_t tempty0 = cluster_addr(&tempty[0], 0), tempty1 = cluster_addr(&tempty[1], 0);
+        float amx = 0.0f;                      // this thread's max |C| (NaN ignored)
+        int i = 0;
+        for (int t = pair; t < total; t += n_pairs, ++i) {
+            const int acc = i & 1;
+            const uint32_t acc_ph = (i >> 1) & 1;
+            int tm, tn;
+            tile_coords(t, p.num_m, p.num_n, tm, tn);
+            if (!mbar_wait_warp(&tfull[acc], acc_ph, p.status)) break;
+            tc_fence_after();
+            const int row = tm * 2 * BM + (int)rank * BM + row_in_tile;
+            const bool row_ok = row < p.M;
+            float inv_c = 1.0f;
+            if constexpr (sizeof(OutT) == 1) {   // E4M3 out: the quantiser's RN(1/scale)
+                inv_c = __frcp_rn(p.scale_c[0]);
+                inv_c = inv_c > FLT_MAX ? FLT_MAX : inv_c;
+            }
+            float sa = 1.0f;
+            if (p.scale_mode == kTensorScale) sa = p.scale_a[0] * p.scale_b[0];
+            else if (p.scale_mode == kRowColScale && row_ok) sa = p.scale_a[row];
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                __syncwarp();  // tcgen05.ld is warp-collective: reconverge first
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
+                tmem_ld_wait();
+                if (c == BN / 32 - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);
+                }
+                const int col0 = tn * BN + c * 32;
+                if (col0 >= p.N) continue;  // warp-uniform
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * sa;
+                if (p.scale_mode == kRowColScale) {  // all lanes take part in the shuffles
+                    const float sbv = (col0 + lane < p.N) ? p.scale_b[col0 + lane] : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] *= __shfl_sync(0xffffffffu, sbv, j);
+                }
+                if (p.amax && row_ok) {
+                    const int nv = p.N - col0;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < nv) amx = fmaxf(amx, fabsf(v[j]));
+                }
+                if (!row_ok) continue;
+                auto store_to = [&](OutT* out) {
+                    const bool full_chunk = col0 + 32 <= p.N &&
+                                            ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
+                    if constexpr (sizeof(OutT) == 1) {
+                        uint32_t w8[8];
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            w8[j >> 2] = f32x2_to_e4m3x2(__fmul_rn(v[j], inv_c), __fmul_rn(v[j + 1], inv_c)) |
+                                         (f32x2_to_e4m3x2(__fmul_rn(v[j + 2], inv_c),
+                                                          __fmul_rn(v[j + 3], inv_c)) << 16);
+                        if (full_chunk) {
+                            reinterpret_cast<uint4*>(out)[0] = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+                            reinterpret_cast<uint4*>(out)[1] = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+                        } else {
+                            uint8_t* o8 = reinterpret_cast<uint8_t*>(out);
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)   // constant indices: w8 stays in registers
+                                if (col0 + j < p.N) o8[j] = (uint8_t)(w8[j >> 2] >> (8 * (j & 3)));
+                        }
+                    } else if constexpr (sizeof(OutT) == 4) {
+                        if (full_chunk) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<float4*>(out + j) =
+                                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)   // constant indices: v stays in registers
+                                if (col0 + j < p.N) out[j] = v[j];
+                        }
+                    } else {
+                        if (full_chunk) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 8) {
+                                uint4 w;
+                                w.x = f32x2_to_bf16x2(v[j], v[j + 1]);
+                                w.y = f32x2_to_bf16x2(v[j + 2], v[j + 3]);
+                                w.z = f32x2_to_bf16x2(v[j + 4], v[j + 5]);
+                                w.w = f32x2_to_bf16x2(v[j + 6], v[j + 7]);
+                                *reinterpret_cast<uint4*>(out + j) = w;
+                            }
+                        } else {
+                            uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (col0 + j < p.N)
+                                    o16[j] = (uint16_t)(f32x2_to_bf16x2(v[j], 0.0f) & 0xffffu);
+                        }
+                    }
+                };
+                store_to(static_cast<OutT*>(p.C) + (int64_t)row * p.N + col0);
+            }
+        }
+        if (p.amax) {   // non-negative floats order like their bit patterns
+            const float m = warp_max(amx);
+            if (lane == 0) atomicMax(reinterpret_cast<unsigned*>(p.amax), __float_as_uint(m));
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync();   // the leader's MMAs (which read this CTA's shared memory) are done
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    }
+}
+
 // ------------------------------------------------------------------ fp32 as 3 x TF32
 // C = A B in fp32 on the tensor cores (kind::tf32).  Each operand is split as
 // x = hi + lo with hi = x with its low 13 mantissa bits cleared (exactly a TF32
@@ -639,6 +974,61 @@ struct AllGather {
     unsigned seq = 0;
 };
 
+// How many SM pairs can hold a k_gemm_tc2 cluster at once on this device (0 if
+// none), with the kernel's shared-memory attribute set on first use.
+template <bool kFP8, typename OutT>
+int pair_slots() {
+    static std::atomic<int> slots[64];   // per device ordinal: 0 unknown, -1 none, else count
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return 0;
+    int n = slots[dev].load();
+    if (n == 0) {
+        auto kern = k_gemm_tc2<kFP8, OutT>;
+        n = -1;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES) ==
+            cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 2;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.gridDim = dim3(2 * sm_count());
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = SMEM2_BYTES;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int c = 0;
+            if (cudaOccupancyMaxActiveClusters(&c, kern, &cfg) == cudaSuccess && c > 0) n = c;
+        }
+        cudaGetLastError();   // a refusal above only means: no pairs
+        slots[dev].store(n);
+    }
+    return n > 0 ? n : 0;
+}
+
+template <bool kFP8, typename OutT>
+int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const TcParams& p, int pairs,
+                cudaStream_t st) {
+    const int total = p.num_m * p.num_n;
+    const int n_pairs = total < pairs ? total : pairs;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * n_pairs);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = SMEM2_BYTES;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    AMPB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc2<kFP8, OutT>, tmA, tmB, p));
+    AMPB_CHECK_LAUNCH("k_gemm_tc2");
+    return AMP_OK;
+}
+
 template <bool kFP8, typename OutT>
 int launch_tc(const void* A, const void* B, void* C, int M, int N, int K, const float* sa,
               const float* sb, int mode, cudaStream_t st, const float* sc = nullptr,
@@ -699,6 +1089,15 @@ int launch_tc(const void* A, const void* B, void* C, int M, int N, int K, const 
         p.done = static_cast<unsigned*>(done);
     }
     if (amax) AMPB_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st));
+    if (!ag) {
+        // 256 x 256 tiles on SM pairs once there are enough of them to fill the pairs
+        const int pm = (M + 2 * BM - 1) / (2 * BM), pn = p.num_n;
+        const int pairs = pair_slots<kFP8, OutT>();
+        if (pairs > 0 && (int64_t)pm * pn >= pairs) {
+            p.num_m = pm;
+            return launch_pair<kFP8, OutT>(tmA, tmB, p, pairs, st);
+        }
+    }
     auto kern = ag ? k_gemm_tc<kFP8, OutT, true> : k_gemm_tc<kFP8, OutT, false>;
     static std::atomic<uint64_t> attr_done[2];  // one bit per device ordinal (< 64) and mode
     int dev = 0;

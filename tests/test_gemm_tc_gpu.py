@@ -60,6 +60,16 @@ def test_bf16_8192_cube_bf16_out(cuda, amp_lib):
     assert oracle.max_rel_err(C, ref64(A, B)) < TOL_BF16
 
 
+@pytest.mark.parametrize("M,N,K", [(2488, 2008, 1000), (4096 + 136, 4096 - 56, 512)])
+@pytest.mark.parametrize("out", [torch.float32, torch.bfloat16])
+def test_bf16_pair_tiles_ragged(M, N, K, out, cuda, amp_lib):
+    """Sizes with >= 74 tiles of 256 x 256 run on SM pairs (2-SM MMAs); M and N
+    here end inside the second CTA's half of a tile."""
+    A, B = bf16_operands(M, N, K, seed=M + 2 * N)
+    C = run_bf16(A, B, out)
+    assert oracle.max_rel_err(C, ref64(A, B)) < TOL_BF16
+
+
 def test_bf16_rejects_unaligned_k(cuda, amp_lib):
     A, B = bf16_operands(64, 64, 60, seed=0)
     with pytest.raises(AmpError, match="multiples"):
@@ -94,7 +104,7 @@ def fp8_ref(qa, sa, qb, sb):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 128), (256, 512, 512), (100, 80, 48),
-                                   (333, 272, 1024)])
+                                   (333, 272, 1024), (2440, 2000, 1008)])
 @pytest.mark.parametrize("out", [torch.float32, torch.bfloat16])
 def test_fp8_rowcol_scales_small(M, N, K, out, cuda, amp_lib):
     qa, sa, qb, sb, _, _ = fp8_operands(M, N, K, seed=M * 3 + N)
@@ -129,6 +139,7 @@ def test_fp8_4096_cube_vs_prequant(cuda, amp_lib):
 
 
 @pytest.mark.parametrize("M,N,K,rowcol", [(512, 768, 1024, True), (300, 784, 512, True),
+                                          (2440, 2000, 512, True),
                                           (256, 256, 256, False)])
 def test_fp8_output_quantisation_and_amax(M, N, K, rowcol, cuda, amp_lib):
     """amax_c is max |v| of the fp32 result exactly, and the E4M3 C is the
