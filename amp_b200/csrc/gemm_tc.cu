@@ -403,9 +403,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // of B, and holds its 128 rows of the accumulator in its own TMEM, so each SM
 // streams two thirds of the operand bytes of a 128 x 256 single-SM tile.  Only
 // the leader (cluster rank 0) issues MMAs; both CTAs' TMA loads count on the
-// leader's full barriers; the leader's commits arrive on both CTAs' barriers
-// (tcgen05.commit multicast); the peer's epilogue releases the accumulator on the
-// leader's barrier.  No TMA load uses multicast.
+// leader's full barriers; each of the leader's commits arrives on the same
+// barrier in both CTAs (CTA mask 0b11); the peer's epilogue releases the
+// accumulator on the leader's barrier.  Every operand copy lands only in the
+// shared memory of the CTA that issues it.
 constexpr int STAGES2 = 6;
 constexpr int STAGE2_BYTES = A_STAGE_BYTES + (BN / 2) * SLAB;   // 16 KiB A + 16 KiB B
 constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
@@ -536,10 +537,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES2; ++s) {
             mbar_init(&full[s], 1);      // leader: its producer's expect_tx, both CTAs' bytes
-            mbar_init(&empty[s], 1);     // each CTA: the leader's multicast commit
+            mbar_init(&empty[s], 1);     // each CTA: the leader's commit (CTA mask 0b11)
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&tfull[b], 1);     // each CTA: the leader's multicast commit
+            mbar_init(&tfull[b], 1);     // each CTA: the leader's commit (CTA mask 0b11)
             mbar_init(&tempty[b], 8);    // leader: the epilogue warps of both CTAs
         }
         mbar_init(drain, 1);

@@ -355,7 +355,9 @@ class GemmWorkload:
                 else "single"}
 
     def kernel_table(self):
-        return [(f"k_gemm_tc<{'e4m3' if self.fp8 else 'bf16'}>", self.units_per_step())]
+        # 256 x 256 tiles on SM pairs (k_gemm_tc2) unless the all-gather epilogue runs
+        name = "k_gemm_tc" if self.peer is not None else "k_gemm_tc2"
+        return [(f"{name}<{'e4m3' if self.fp8 else 'bf16'}>", self.units_per_step())]
 
     def _launch(self):
         if self.peer is not None:
