@@ -103,6 +103,93 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm
     tn = local / gm;
 }
 
+// ---- epilogue steps on one 32-column chunk of a C row (both GEMM kernels)
+
+// Scales a row takes: sa multiplies every accumulator (per-tensor product, or
+// scale_a[row] per row); inv_c is the E4M3 output's RN(1/scale_c), as the quantiser.
+template <typename OutT>
+__device__ __forceinline__ void row_scales(const TcParams& p, int row, bool row_ok, float& sa,
+                                           float& inv_c) {
+    inv_c = 1.0f;
+    if constexpr (sizeof(OutT) == 1) {
+        inv_c = __frcp_rn(p.scale_c[0]);
+        inv_c = inv_c > FLT_MAX ? FLT_MAX : inv_c;
+    }
+    sa = 1.0f;
+    if (p.scale_mode == kTensorScale) sa = p.scale_a[0] * p.scale_b[0];
+    else if (p.scale_mode == kRowColScale && row_ok) sa = p.scale_a[row];
+}
+
+// v = accumulators x sa (x scale_b[col] per column: all lanes take part in the shuffles)
+__device__ __forceinline__ void scale_chunk(const uint32_t (&r)[32], float (&v)[32], float sa,
+                                            const TcParams& p, int col0, int lane) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * sa;
+    if (p.scale_mode == kRowColScale) {
+        const float sbv = (col0 + lane < p.N) ? p.scale_b[col0 + lane] : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] *= __shfl_sync(0xffffffffu, sbv, j);
+    }
+}
+
+// amx = max(amx, |v[j]|) over the nv columns inside C (NaN ignored by fmaxf)
+__device__ __forceinline__ void amax_chunk(float& amx, const float (&v)[32], int nv) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+        if (j < nv) amx = fmaxf(amx, fabsf(v[j]));
+}
+
+// Stores the first min(nv, 32) values of v at `out` as OutT (E4M3 codes of v * inv_c
+// for 1-byte C).  Every loop has constant indices, so v stays in registers.
+template <typename OutT>
+__device__ __forceinline__ void store_chunk(OutT* out, const float (&v)[32], int nv, float inv_c) {
+    const bool full_chunk = nv >= 32 && ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
+    if constexpr (sizeof(OutT) == 1) {
+        uint32_t w8[8];
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+            w8[j >> 2] = f32x2_to_e4m3x2(__fmul_rn(v[j], inv_c), __fmul_rn(v[j + 1], inv_c)) |
+                         (f32x2_to_e4m3x2(__fmul_rn(v[j + 2], inv_c), __fmul_rn(v[j + 3], inv_c))
+                          << 16);
+        if (full_chunk) {
+            reinterpret_cast<uint4*>(out)[0] = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+            reinterpret_cast<uint4*>(out)[1] = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+        } else {
+            uint8_t* o8 = reinterpret_cast<uint8_t*>(out);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nv) o8[j] = (uint8_t)(w8[j >> 2] >> (8 * (j & 3)));
+        }
+    } else if constexpr (sizeof(OutT) == 4) {
+        if (full_chunk) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(out + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nv) out[j] = v[j];
+        }
+    } else {
+        if (full_chunk) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+                uint4 w;
+                w.x = f32x2_to_bf16x2(v[j], v[j + 1]);
+                w.y = f32x2_to_bf16x2(v[j + 2], v[j + 3]);
+                w.z = f32x2_to_bf16x2(v[j + 4], v[j + 5]);
+                w.w = f32x2_to_bf16x2(v[j + 6], v[j + 7]);
+                *reinterpret_cast<uint4*>(out + j) = w;
+            }
+        } else {
+            uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nv) o16[j] = (uint16_t)(f32x2_to_bf16x2(v[j], 0.0f) & 0xffffu);
+        }
+    }
+}
+
 template <bool kFP8, typename OutT, bool kAllGather>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -227,14 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int row = tm * BM + row_in_tile;
             const bool row_ok = row < p.M;
-            float inv_c = 1.0f;
-            if constexpr (sizeof(OutT) == 1) {   // E4M3 out: the quantiser's RN(1/scale)
-                inv_c = __frcp_rn(p.scale_c[0]);
-                inv_c = inv_c > FLT_MAX ? FLT_MAX : inv_c;
-            }
-            float sa = 1.0f;
-            if (p.scale_mode == kTensorScale) sa = p.scale_a[0] * p.scale_b[0];
-            else if (p.scale_mode == kRowColScale && row_ok) sa = p.scale_a[row];
+            float sa, inv_c;
+            row_scales<OutT>(p, row, row_ok, sa, inv_c);
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
                 __syncwarp();  // tcgen05.ld is warp-collective: reconverge first
@@ -252,19 +333,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 constexpr int CPG = 128 / (32 * (int)sizeof(OutT));   // chunks per group
                 const bool staged = kAllGather && (tn * BN + (c / CPG + 1) * CPG * 32 <= p.N);
                 float v[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * sa;
-                if (p.scale_mode == kRowColScale) {  // all lanes take part in the shuffles
-                    const float sbv = (col0 + lane < p.N) ? p.scale_b[col0 + lane] : 0.0f;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] *= __shfl_sync(0xffffffffu, sbv, j);
-                }
-                if (p.amax && row_ok) {
-                    const int nv = p.N - col0;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (j < nv) amx = fmaxf(amx, fabsf(v[j]));
-                }
+                scale_chunk(r, v, sa, p, col0, lane);
+                if (p.amax && row_ok) amax_chunk(amx, v, p.N - col0);
                 if constexpr (kAllGather && sizeof(OutT) != 1) {
                     if (staged) {
                         // this row's 32 values into 16-byte columns [slot0, slot0 + Q) of the
@@ -308,64 +378,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 if (!row_ok) continue;
-                auto store_to = [&](OutT* out) {
-                    const bool full_chunk = col0 + 32 <= p.N &&
-                                            ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
-                    if constexpr (sizeof(OutT) == 1) {
-                        uint32_t w8[8];
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            w8[j >> 2] = f32x2_to_e4m3x2(__fmul_rn(v[j], inv_c), __fmul_rn(v[j + 1], inv_c)) |
-                                         (f32x2_to_e4m3x2(__fmul_rn(v[j + 2], inv_c),
-                                                          __fmul_rn(v[j + 3], inv_c)) << 16);
-                        if (full_chunk) {
-                            reinterpret_cast<uint4*>(out)[0] = make_uint4(w8[0], w8[1], w8[2], w8[3]);
-                            reinterpret_cast<uint4*>(out)[1] = make_uint4(w8[4], w8[5], w8[6], w8[7]);
-                        } else {
-                            uint8_t* o8 = reinterpret_cast<uint8_t*>(out);
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)   // constant indices: w8 stays in registers
-                                if (col0 + j < p.N) o8[j] = (uint8_t)(w8[j >> 2] >> (8 * (j & 3)));
-                        }
-                    } else if constexpr (sizeof(OutT) == 4) {
-                        if (full_chunk) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4*>(out + j) =
-                                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)   // constant indices: v stays in registers
-                                if (col0 + j < p.N) out[j] = v[j];
-                        }
-                    } else {
-                        if (full_chunk) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 8) {
-                                uint4 w;
-                                w.x = f32x2_to_bf16x2(v[j], v[j + 1]);
-                                w.y = f32x2_to_bf16x2(v[j + 2], v[j + 3]);
-                                w.z = f32x2_to_bf16x2(v[j + 4], v[j + 5]);
-                                w.w = f32x2_to_bf16x2(v[j + 6], v[j + 7]);
-                                *reinterpret_cast<uint4*>(out + j) = w;
-                            }
-                        } else {
-                            uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (col0 + j < p.N)
-                                    o16[j] = (uint16_t)(f32x2_to_bf16x2(v[j], 0.0f) & 0xffffu);
-                        }
-                    }
-                };
                 if constexpr (!kAllGather) {
-                    store_to(static_cast<OutT*>(p.C) + (int64_t)row * p.N + col0);
+                    store_chunk(static_cast<OutT*>(p.C) + (int64_t)row * p.N + col0, v, p.N - col0,
+                                inv_c);
                 } else {
                     // every rank's C, this rank last (peers first, spread over the links)
                     for (int i = 1; i <= p.world; ++i) {
                         const int d = (p.rank + i) % p.world;
-                        store_to(static_cast<OutT*>(p.peers[d]) + (int64_t)row * p.ldc + p.col_base +
-                                 col0);
+                        store_chunk(static_cast<OutT*>(p.peers[d]) + (int64_t)row * p.ldc +
+                                        p.col_base + col0,
+                                    v, p.N - col0, inv_c);
                     }
                 }
             }
@@ -410,6 +432,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int STAGES2 = 6;
 constexpr int STAGE2_BYTES = A_STAGE_BYTES + (BN / 2) * SLAB;   // 16 KiB A + 16 KiB B
 constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
+static_assert(SMEM2_BYTES <= 227 * 1024 && SMEM_BYTES_AG <= 227 * 1024,
+              "dynamic shared memory above the 227 KiB a CTA can have");
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
@@ -631,14 +655,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int row = tm * 2 * BM + (int)rank * BM + row_in_tile;
             const bool row_ok = row < p.M;
-            float inv_c = 1.0f;
-            if constexpr (sizeof(OutT) == 1) {   // E4M3 out: the quantiser's RN(1/scale)
-                inv_c = __frcp_rn(p.scale_c[0]);
-                inv_c = inv_c > FLT_MAX ? FLT_MAX : inv_c;
-            }
-            float sa = 1.0f;
-            if (p.scale_mode == kTensorScale) sa = p.scale_a[0] * p.scale_b[0];
-            else if (p.scale_mode == kRowColScale && row_ok) sa = p.scale_a[row];
+            float sa, inv_c;
+            row_scales<OutT>(p, row, row_ok, sa, inv_c);
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
                 __syncwarp();  // tcgen05.ld is warp-collective: reconverge first
@@ -652,71 +670,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int col0 = tn * BN + c * 32;
                 if (col0 >= p.N) continue;  // warp-uniform
                 float v[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * sa;
-                if (p.scale_mode == kRowColScale) {  // all lanes take part in the shuffles
-                    const float sbv = (col0 + lane < p.N) ? p.scale_b[col0 + lane] : 0.0f;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] *= __shfl_sync(0xffffffffu, sbv, j);
-                }
-                if (p.amax && row_ok) {
-                    const int nv = p.N - col0;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (j < nv) amx = fmaxf(amx, fabsf(v[j]));
-                }
+                scale_chunk(r, v, sa, p, col0, lane);
+                if (p.amax && row_ok) amax_chunk(amx, v, p.N - col0);
                 if (!row_ok) continue;
-                auto store_to = [&](OutT* out) {
-                    const bool full_chunk = col0 + 32 <= p.N &&
-                                            ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
-                    if constexpr (sizeof(OutT) == 1) {
-                        uint32_t w8[8];
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            w8[j >> 2] = f32x2_to_e4m3x2(__fmul_rn(v[j], inv_c), __fmul_rn(v[j + 1], inv_c)) |
-                                         (f32x2_to_e4m3x2(__fmul_rn(v[j + 2], inv_c),
-                                                          __fmul_rn(v[j + 3], inv_c)) << 16);
-                        if (full_chunk) {
-                            reinterpret_cast<uint4*>(out)[0] = make_uint4(w8[0], w8[1], w8[2], w8[3]);
-                            reinterpret_cast<uint4*>(out)[1] = make_uint4(w8[4], w8[5], w8[6], w8[7]);
-                        } else {
-                            uint8_t* o8 = reinterpret_cast<uint8_t*>(out);
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)   // constant indices: w8 stays in registers
-                                if (col0 + j < p.N) o8[j] = (uint8_t)(w8[j >> 2] >> (8 * (j & 3)));
-                        }
-                    } else if constexpr (sizeof(OutT) == 4) {
-                        if (full_chunk) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4*>(out + j) =
-                                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)   // constant indices: v stays in registers
-                                if (col0 + j < p.N) out[j] = v[j];
-                        }
-                    } else {
-                        if (full_chunk) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 8) {
-                                uint4 w;
-                                w.x = f32x2_to_bf16x2(v[j], v[j + 1]);
-                                w.y = f32x2_to_bf16x2(v[j + 2], v[j + 3]);
-                                w.z = f32x2_to_bf16x2(v[j + 4], v[j + 5]);
-                                w.w = f32x2_to_bf16x2(v[j + 6], v[j + 7]);
-                                *reinterpret_cast<uint4*>(out + j) = w;
-                            }
-                        } else {
-                            uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (col0 + j < p.N)
-                                    o16[j] = (uint16_t)(f32x2_to_bf16x2(v[j], 0.0f) & 0xffffu);
-                        }
-                    }
-                };
-                store_to(static_cast<OutT*>(p.C) + (int64_t)row * p.N + col0);
+                store_chunk(static_cast<OutT*>(p.C) + (int64_t)row * p.N + col0, v, p.N - col0, inv_c);
             }
         }
         if (p.amax) {   // non-negative floats order like their bit patterns
