@@ -8,12 +8,19 @@ Workloads (``--workload``):
   fp8_quant (default)  per-tensor amax-scaled FP8 E4M3 quantise + dequantise of
                        2^26 bf16 values (N(0,1), 0.1% N(0,50) outliers); metric =
                        algorithmic bytes (8 B/element) per second.  N > 1: each
-                       rank its own 2^26 shard against the global amax (1-float
-                       NCCL all-reduce MAX in the step), weak scaling.
+                       rank its own 2^26 shard against the global amax (a 1-float
+                       max all-reduce through peer mailboxes), weak scaling.
   gemm_bf16            C = A @ B, M=N=K=S (default 8192), bf16 in, fp32 accumulate,
                        bf16 out; metric = 2*S^3 FLOP per second.  N > 1: B and C
-                       split along N, C all-gathered over NCCL (strong scaling).
+                       split along N; the all-gather of C is fused into the GEMM
+                       epilogue (``--gather nccl``: NCCL after it), strong scaling.
   gemm_fp8             same with E4M3 operands, per-row A / per-column B scales.
+  fa2_fwd              FlashAttention-2 forward, B=4 H=32 S=4096 D=128 causal;
+                       N > 1: (batch*head) split, O and lse all-gathered in the epilogue.
+  fa2_bwd              the backward of the same configuration (dQ, dK, dV).
+  paged_decode         GQA decode over the paged KV cache (B=8, Hq=32, Hkv=8,
+                       context U[512, 16384], 16-token pages); replicas at N > 1.
+  paged_prefill        the last 512 tokens of each context as a paged prefill.
 
 Timing: W untimed warm-up steps; then K steps, each bracketed by CUDA events on
 the launching stream with an L2 flush before every step (256 MiB written, then
@@ -189,7 +196,7 @@ class QuantWorkload:
     def __init__(self, dist: Dist, args):
         import torch
         from amp_b200 import fp8, workloads
-        self.torch, self.fp8, self.dist = torch, fp8, dist
+        self.torch, self.fp8, self.dist, self.args = torch, fp8, dist, args
         self.n = n = args.elements
         dev = torch.device("cuda", torch.cuda.current_device())
         self.x = workloads.quant_input_torch(n, seed=1234 + dist.rank, device=dev)
@@ -215,14 +222,19 @@ class QuantWorkload:
     def launches_per_step(self) -> int:
         return 3 if self.dist.world == 1 else 4
 
-    def config(self):
-        return {"workload": "fp8_e4m3_per_tensor_quant_dequant", "elements_per_gpu": self.n,
-                "global_elements": self.n * self.dist.world,
+    @classmethod
+    def describe(cls, args, world: int, rank: int = 0) -> dict:
+        n = args.elements
+        return {"workload": "fp8_e4m3_per_tensor_quant_dequant", "elements_per_gpu": n,
+                "global_elements": n * world,
                 "input": "bf16 N(0,1) + 0.1% N(0,50) outliers (seeded, synthetic)",
                 "scale": "amax/448, RNE satfinite", "l2": "L2 flushed before every step (256 MiB written, then 256 MiB read)",
-                "parallelism": f"shard{self.dist.world}+all-reduce(max) of 1 float through peer "
+                "parallelism": f"shard{world}+all-reduce(max) of 1 float through peer "
                                "mailboxes (NVLink stores, no NCCL)"
-                if self.dist.world > 1 else "single"}
+                if world > 1 else "single"}
+
+    def config(self):
+        return self.describe(self.args, self.dist.world, self.dist.rank)
 
     def kernel_table(self):
         if self.dist.world == 1:
@@ -301,7 +313,7 @@ class GemmWorkload:
     def __init__(self, dist: Dist, args):
         import torch
         from amp_b200 import gemm
-        self.torch, self.gemm, self.dist = torch, gemm, dist
+        self.torch, self.gemm, self.dist, self.args = torch, gemm, dist, args
         S = self.S = args.size
         p = dist.world
         if S % (256 * p):
@@ -340,19 +352,23 @@ class GemmWorkload:
     def launches_per_step(self) -> int:
         return 1
 
-    def config(self):
-        p = self.dist.world
-        return {"workload": f"{'fp8_e4m3' if self.fp8 else 'bf16'}_gemm", "M": self.S,
-                "N": self.S, "K": self.S, "out": "bf16",
+    @classmethod
+    def describe(cls, args, world: int, rank: int = 0) -> dict:
+        S, p = args.size, world
+        return {"workload": f"{'fp8_e4m3' if cls.fp8 else 'bf16'}_gemm", "M": S,
+                "N": S, "K": S, "out": "bf16",
                 "inputs": "N(0,1)" + (" quantised per row (A) / per column (B), amax/448"
-                                      if self.fp8 else ""),
+                                      if cls.fp8 else ""),
                 "l2": "operands (2 x %d MiB) exceed L2; L2 flushed before every step"
-                      % (self.S * self.S * (1 if self.fp8 else 2) >> 20),
+                      % (S * S * (1 if cls.fp8 else 2) >> 20),
                 "parallelism": (f"N-split over {p} GPUs, all-gather of C fused into the GEMM "
                                 "epilogue (stores into every rank's C over NVLink)"
-                                if self.peer is not None else
+                                if args.gather == "peer" else
                                 f"N-split over {p} GPUs + NCCL all-gather of C") if p > 1
                 else "single"}
+
+    def config(self):
+        return self.describe(self.args, self.dist.world, self.dist.rank)
 
     def kernel_table(self):
         # 256 x 256 tiles on SM pairs (k_gemm_tc2) unless the all-gather epilogue runs
@@ -450,7 +466,7 @@ class AttentionWorkload:
     def __init__(self, dist: Dist, args):
         import torch
         from amp_b200 import attention
-        self.torch, self.att, self.dist = torch, attention, dist
+        self.torch, self.att, self.dist, self.args = torch, attention, dist, args
         self.B, self.H, self.S, self.D = args.batch, args.heads, args.seq, 128
         p = dist.world
         if (self.B * self.H) % p:
@@ -485,18 +501,22 @@ class AttentionWorkload:
     def launches_per_step(self) -> int:
         return 1
 
-    def config(self):
-        p = self.dist.world
-        return {"workload": "flash_attn2_fwd_causal", "batch": self.B, "heads": self.H,
-                "seq_len": self.S, "head_dim": self.D, "dtype": "bf16, fp32 softmax/accumulate",
+    @classmethod
+    def describe(cls, args, world: int, rank: int = 0) -> dict:
+        B, H, S, D, p = args.batch, args.heads, args.seq, 128, world
+        return {"workload": "flash_attn2_fwd_causal", "batch": B, "heads": H,
+                "seq_len": S, "head_dim": D, "dtype": "bf16, fp32 softmax/accumulate",
                 "flop_convention": "4*B*H*D*S*(S+1)/2 (visible pairs)",
                 "l2": "Q/K/V %d MiB each exceed L2; L2 flushed before every step"
-                      % (self.B * self.H * self.S * self.D * 2 >> 20),
+                      % (B * H * S * D * 2 >> 20),
                 "parallelism": (f"(batch*head) split over {p} GPUs, all-gather of O and lse fused "
                                 "into the attention epilogue (stores into every rank's O over "
-                                "NVLink)" if self.peer_o is not None else
+                                "NVLink)" if cls.fused_gather and args.gather == "peer" else
                                 f"(batch*head) split over {p} GPUs + NCCL all-gather of O")
                 if p > 1 else "single"}
+
+    def config(self):
+        return self.describe(self.args, self.dist.world, self.dist.rank)
 
     def kernel_table(self):
         return [("k_flash_fwd<128>", self.units_per_step())]
@@ -571,9 +591,8 @@ class PagedDecodeWorkload:
     def __init__(self, dist: Dist, args):
         import torch
         from amp_b200 import paged, workloads as wl
-        self.torch, self.paged, self.dist = torch, paged, dist
-        rng = np.random.default_rng(2025 + dist.rank)
-        self.ctx = rng.integers(wl.PAGED_CTX_LO, wl.PAGED_CTX_HI + 1, size=wl.PAGED_B).astype(np.int32)
+        self.torch, self.paged, self.dist, self.args = torch, paged, dist, args
+        self.ctx = self.context_lens(dist.rank)
         bt, self.num_pages = wl.paged_layout(self.ctx, seed=2026 + dist.rank)
         dev = torch.device("cuda", torch.cuda.current_device())
         g = torch.Generator(device=dev)
@@ -604,14 +623,27 @@ class PagedDecodeWorkload:
     def launches_per_step(self) -> int:
         return 2
 
-    def config(self):
-        return {"workload": "paged_gqa_decode", "batch": self.B, "q_heads": self.Hq,
-                "kv_heads": self.Hkv, "head_dim": self.D, "page_tokens": 16,
-                "context_lens": self.ctx.tolist(), "total_context": int(self.ctx.sum()),
+    @staticmethod
+    def context_lens(rank: int) -> np.ndarray:
+        """This rank's seeded context lengths, U[512, 16384] for each of the 8 sequences."""
+        from amp_b200 import workloads as wl
+        rng = np.random.default_rng(2025 + rank)
+        return rng.integers(wl.PAGED_CTX_LO, wl.PAGED_CTX_HI + 1, size=wl.PAGED_B).astype(np.int32)
+
+    @classmethod
+    def describe(cls, args, world: int, rank: int = 0) -> dict:
+        from amp_b200 import workloads as wl
+        ctx = cls.context_lens(rank)
+        return {"workload": "paged_gqa_decode", "batch": wl.PAGED_B, "q_heads": wl.PAGED_HQ,
+                "kv_heads": wl.PAGED_HKV, "head_dim": wl.PAGED_D, "page_tokens": wl.PAGE,
+                "context_lens": ctx.tolist(), "total_context": int(ctx.sum()),
                 "block_table": "seeded random permutation of the pool",
                 "l2": "KV pools exceed L2; L2 flushed before every step",
-                "parallelism": "replicas (each rank its own batch)" if self.dist.world > 1
+                "parallelism": "replicas (each rank its own batch)" if world > 1
                 else "single"}
+
+    def config(self):
+        return self.describe(self.args, self.dist.world, self.dist.rank)
 
     def kernel_table(self):
         return [("k_paged_decode + k_paged_combine", self.units_per_step())]
@@ -694,9 +726,11 @@ class PagedPrefillWorkload(PagedDecodeWorkload):
     def launches_per_step(self) -> int:
         return 1
 
-    def config(self):
-        c = super().config()
-        c.update({"workload": "paged_gqa_prefill", "new_tokens_per_seq": self.Lq,
+    @classmethod
+    def describe(cls, args, world: int, rank: int = 0) -> dict:
+        from amp_b200 import workloads as wl
+        c = super().describe(args, world, rank)
+        c.update({"workload": "paged_gqa_prefill", "new_tokens_per_seq": wl.PAGED_LQ,
                   "flop_convention": "4*Hq*D*sum(visible (query, key) pairs)"})
         return c
 
@@ -735,11 +769,12 @@ class AttentionBwdWorkload(AttentionWorkload):
     def launches_per_step(self) -> int:
         return 3
 
-    def config(self):
-        c = super().config()
+    @classmethod
+    def describe(cls, args, world: int, rank: int = 0) -> dict:
+        c = super().describe(args, world, rank)
         c["workload"] = "flash_attn2_bwd_causal"
         c["flop_convention"] = "2.5 x 4*B*H*D*S*(S+1)/2 (five products over the visible pairs)"
-        c["parallelism"] = "single" if self.dist.world == 1 else f"(batch*head) split over {self.dist.world} GPUs"
+        c["parallelism"] = "single" if world == 1 else f"(batch*head) split over {world} GPUs"
         return c
 
     def kernel_table(self):
@@ -945,14 +980,14 @@ def run_reference(args):
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
         "warmup": args.warmup, "higher_is_better": True, "scaling": W.scaling,
         "vs_baseline": None, "dtype": W.dtype, "data": "synthetic (seeded)",
-        "config": {"workload": W.name, "size": args.size, "elements": args.elements},
+        "config": W.describe(args, int(os.environ.get("WORLD_SIZE", "1"))),
         "impl": "reference", "cpu_baseline": cb,
         "e2e": {"value": round(v, 4), "unit": W.unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
 
 
-def main():
+def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -969,7 +1004,11 @@ def main():
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="N>1 GEMM: all-gather fused into the epilogue (peer) or NCCL after it")
-    args = ap.parse_args()
+    return ap
+
+
+def main():
+    args = build_parser().parse_args()
     if args.impl == "reference":
         args.steps = args.steps or 5
         args.warmup = args.warmup if args.warmup is not None else 3
