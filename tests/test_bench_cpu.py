@@ -73,3 +73,15 @@ def test_reference_arm_other_ranks_exit_without_work():
 def test_warmup_below_three_is_rejected():
     r = _run(["--impl", "reference", "--steps", "1", "--warmup", "1"])
     assert r.returncode != 0 and "warmup" in (r.stderr + r.stdout)
+
+
+@pytest.mark.parametrize("name", sorted(bench.WORKLOADS))
+def test_instance_config_is_describe(name):
+    """config() of a set-up workload (here without its device buffers) is describe()."""
+    class _Dist:
+        world, rank = 2, 0
+    W = bench.WORKLOADS[name]
+    args = bench.build_parser().parse_args(["--workload", name])
+    w = object.__new__(W)
+    w.args, w.dist = args, _Dist()
+    assert w.config() == W.describe(args, 2)
