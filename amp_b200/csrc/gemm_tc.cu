@@ -943,8 +943,9 @@ int pair_slots() {
     if (n == 0) {
         auto kern = k_gemm_tc2<kFP8, OutT>;
         n = -1;
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES) ==
-            cudaSuccess) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             SMEM2_BYTES);
+        if (e == cudaSuccess) {
             cudaLaunchConfig_t cfg = {};
             cudaLaunchAttribute attr[1];
             attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -957,9 +958,11 @@ int pair_slots() {
             cfg.attrs = attr;
             cfg.numAttrs = 1;
             int c = 0;
-            if (cudaOccupancyMaxActiveClusters(&c, kern, &cfg) == cudaSuccess && c > 0) n = c;
+            e = cudaOccupancyMaxActiveClusters(&c, kern, &cfg);
+            if (e == cudaSuccess && c > 0) n = c;
         }
-        cudaGetLastError();   // a refusal above only means: no pairs
+        // a refusal above only means: no pairs (clear that error, and no other)
+        if (e != cudaSuccess) cudaGetLastError();
         slots[dev].store(n);
     }
     return n > 0 ? n : 0;
