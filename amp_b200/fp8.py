@@ -23,6 +23,17 @@ def _check_bf16(x: torch.Tensor) -> None:
         raise ValueError("expected a contiguous bfloat16 CUDA tensor")
 
 
+def _check_buf(t: torch.Tensor | None, dtype, n: int, device, name: str) -> None:
+    """A caller-supplied buffer (None: allocated here) holds at least n elements of
+    dtype, contiguous, on the input's device: the kernels write through its pointer."""
+    if t is None:
+        return
+    if not t.is_cuda or t.device != device or t.dtype != dtype or not t.is_contiguous() \
+            or t.numel() < n:
+        raise ValueError(f"{name}: expected a contiguous {dtype} tensor of >= {n} elements on "
+                         f"{device}, got {t.dtype} {tuple(t.shape)} on {t.device}")
+
+
 def workspace_bytes(n: int) -> int:
     return int(lib().amp_fp8_quant_workspace_bytes(n))
 
@@ -37,9 +48,13 @@ def quantize_e4m3(x: torch.Tensor, workspace: torch.Tensor | None = None,
     _check_bf16(x)
     n = x.numel()
     dev = x.device
+    ws_b = workspace_bytes(n)
+    _check_buf(out, torch.uint8, n, dev, "out")
+    _check_buf(scale, torch.float32, 1, dev, "scale")
+    _check_buf(amax, torch.float32, 1, dev, "amax")
+    _check_buf(workspace, torch.uint8, ws_b, dev, "workspace")
     q = out if out is not None else torch.empty(x.shape, dtype=torch.uint8, device=dev)
     s = scale if scale is not None else torch.empty(1, dtype=torch.float32, device=dev)
-    ws_b = workspace_bytes(n)
     ws = workspace if workspace is not None else torch.empty(ws_b, dtype=torch.uint8, device=dev)
     call("amp_fp8_quant_e4m3_dev", x.data_ptr(), n, q.data_ptr(), s.data_ptr(),
          amax.data_ptr() if amax is not None else None, ws.data_ptr(), ws.numel(), _stream(dev))
@@ -51,8 +66,10 @@ def amax_bf16(x: torch.Tensor, workspace: torch.Tensor | None = None,
     """max |x| of a bf16 tensor into a float32[1] device tensor (NaN ignored)."""
     _check_bf16(x)
     dev = x.device
-    a = out if out is not None else torch.empty(1, dtype=torch.float32, device=dev)
     ws_b = workspace_bytes(x.numel())
+    _check_buf(out, torch.float32, 1, dev, "out")
+    _check_buf(workspace, torch.uint8, ws_b, dev, "workspace")
+    a = out if out is not None else torch.empty(1, dtype=torch.float32, device=dev)
     ws = workspace if workspace is not None else torch.empty(ws_b, dtype=torch.uint8, device=dev)
     call("amp_fp8_amax_bf16_dev", x.data_ptr(), x.numel(), a.data_ptr(), ws.data_ptr(),
          ws.numel(), _stream(dev))
@@ -65,8 +82,10 @@ def amax_allreduce_peer(x: torch.Tensor, mailboxes, workspace: torch.Tensor | No
     others through `mailboxes` (a collective.PeerMailboxes); no NCCL call."""
     _check_bf16(x)
     dev = x.device
-    a = out if out is not None else torch.empty(1, dtype=torch.float32, device=dev)
     ws_b = workspace_bytes(x.numel())
+    _check_buf(out, torch.float32, 1, dev, "out")
+    _check_buf(workspace, torch.uint8, ws_b, dev, "workspace")
+    a = out if out is not None else torch.empty(1, dtype=torch.float32, device=dev)
     ws = workspace if workspace is not None else torch.empty(ws_b, dtype=torch.uint8, device=dev)
     call("amp_fp8_amax_allreduce_peer_dev", x.data_ptr(), x.numel(), a.data_ptr(), ws.data_ptr(),
          ws.numel(), mailboxes.table.data_ptr(), mailboxes.g.rank, mailboxes.g.world,
@@ -80,6 +99,9 @@ def quantize_e4m3_from_amax(x: torch.Tensor, amax: torch.Tensor,
     """Quantise with an externally supplied amax (e.g. all-reduced over ranks)."""
     _check_bf16(x)
     dev = x.device
+    _check_buf(amax, torch.float32, 1, dev, "amax")
+    _check_buf(out, torch.uint8, x.numel(), dev, "out")
+    _check_buf(scale, torch.float32, 1, dev, "scale")
     q = out if out is not None else torch.empty(x.shape, dtype=torch.uint8, device=dev)
     s = scale if scale is not None else torch.empty(1, dtype=torch.float32, device=dev)
     call("amp_fp8_quant_e4m3_from_amax_dev", x.data_ptr(), x.numel(), amax.data_ptr(),
@@ -93,6 +115,8 @@ def dequantize_e4m3(q: torch.Tensor, scale: torch.Tensor,
     if not q.is_cuda or q.dtype != torch.uint8 or not q.is_contiguous():
         raise ValueError("expected a contiguous uint8 CUDA tensor of E4M3 codes")
     dev = q.device
+    _check_buf(scale, torch.float32, 1, dev, "scale")
+    _check_buf(out, torch.bfloat16, q.numel(), dev, "out")
     y = out if out is not None else torch.empty(q.shape, dtype=torch.bfloat16, device=dev)
     call("amp_fp8_dequant_e4m3_dev", q.data_ptr(), q.numel(), scale.data_ptr(), y.data_ptr(),
          _stream(dev))

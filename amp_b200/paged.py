@@ -36,6 +36,24 @@ def _check_pools(k_pool, v_pool, block_table, ctx_lens):
             raise ValueError(f"{nm}: expected a contiguous int32 CUDA tensor")
 
 
+def _check_q(q, out, lse, k_pool, block_table, ctx_lens, rank: int):
+    """q (and a caller-supplied out) [B, Hq, (Lq,) D] bf16 with D the pools' head
+    dimension and B rows of block table and context lengths; lse [B, Hq, (Lq)] fp32."""
+    if not q.is_cuda or q.dtype != torch.bfloat16 or not q.is_contiguous() or q.dim() != rank \
+            or q.device != k_pool.device or q.shape[-1] != k_pool.shape[3]:
+        raise ValueError(f"q: expected a contiguous bf16 CUDA tensor of rank {rank} on "
+                         f"{k_pool.device} with head dimension {k_pool.shape[3]}")
+    B = q.shape[0]
+    if block_table.dim() != 2 or block_table.shape[0] < B or ctx_lens.numel() < B:
+        raise ValueError(f"block_table [>= {B}, pages] and ctx_lens [>= {B}] expected")
+    if out is not None and (out.dtype != q.dtype or out.shape != q.shape or out.device != q.device
+                            or not out.is_contiguous()):
+        raise ValueError("out must be a contiguous tensor shaped like q")
+    if lse is not None and (lse.dtype != torch.float32 or tuple(lse.shape) != tuple(q.shape[:-1])
+                            or lse.device != q.device or not lse.is_contiguous()):
+        raise ValueError(f"lse must be a contiguous float32 tensor of shape {tuple(q.shape[:-1])}")
+
+
 def decode_workspace_bytes(B: int, Hq: int, D: int, max_context_len: int) -> int:
     return int(lib().amp_paged_decode_workspace_bytes(B, Hq, D, max_context_len))
 
@@ -44,11 +62,17 @@ def paged_attn_decode(q, k_pool, v_pool, block_table, ctx_lens, max_context_len:
                       scale: float = 0.0, out=None, lse=None, workspace=None):
     """One query token per sequence: q [B, Hq, D] -> (out [B, Hq, D], lse [B, Hq])."""
     _check_pools(k_pool, v_pool, block_table, ctx_lens)
+    _check_q(q, out, lse, k_pool, block_table, ctx_lens, 3)
     B, Hq, D = q.shape
     num_pages, Hkv = k_pool.shape[0], k_pool.shape[1]
+    ws_b = decode_workspace_bytes(B, Hq, D, max_context_len)
+    if workspace is not None and (not workspace.is_cuda or workspace.device != q.device
+                                  or workspace.dtype != torch.uint8
+                                  or not workspace.is_contiguous() or workspace.numel() < ws_b):
+        raise ValueError(f"workspace: expected a contiguous uint8 tensor of >= {ws_b} bytes "
+                         f"on {q.device}")
     out = out if out is not None else torch.empty_like(q)
     lse = lse if lse is not None else torch.empty(B, Hq, dtype=torch.float32, device=q.device)
-    ws_b = decode_workspace_bytes(B, Hq, D, max_context_len)
     ws = workspace if workspace is not None else torch.empty(ws_b, dtype=torch.uint8,
                                                              device=q.device)
     call("amp_paged_attn_decode_bf16_dev", q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
@@ -62,6 +86,7 @@ def paged_attn_prefill(q, k_pool, v_pool, block_table, ctx_lens, scale: float = 
                        out=None, lse=None):
     """q [B, Hq, Lq, D]: the last Lq tokens of each context, bottom-right causal."""
     _check_pools(k_pool, v_pool, block_table, ctx_lens)
+    _check_q(q, out, lse, k_pool, block_table, ctx_lens, 4)
     B, Hq, Lq, D = q.shape
     num_pages, Hkv = k_pool.shape[0], k_pool.shape[1]
     out = out if out is not None else torch.empty_like(q)

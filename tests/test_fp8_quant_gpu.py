@@ -133,3 +133,25 @@ def test_every_bf16_value_over_many_scales(cuda, amp_lib):
         want = oracle.quant_e4m3_with_amax(bits, a)
         got = q.cpu().numpy()
         assert np.array_equal(got, want), (a, np.count_nonzero(got != want))
+
+
+def test_caller_buffers_are_checked_before_launch(cuda, amp_lib):
+    """Buffers a caller hands in are checked on the host (dtype, device, size),
+    since the kernels write through their pointers."""
+    x = torch.zeros(1000, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(ValueError, match="out"):
+        fp8.quantize_e4m3(x, out=torch.empty(999, dtype=torch.uint8, device=cuda))
+    with pytest.raises(ValueError, match="scale"):
+        fp8.quantize_e4m3(x, scale=torch.empty(1, dtype=torch.float64, device=cuda))
+    with pytest.raises(ValueError, match="workspace"):
+        fp8.quantize_e4m3(x, workspace=torch.empty(16, dtype=torch.uint8, device=cuda))
+    with pytest.raises(ValueError, match="amax"):
+        fp8.quantize_e4m3_from_amax(x, torch.zeros(1))
+    with pytest.raises(ValueError, match="out"):
+        fp8.amax_bf16(x, out=torch.empty(1, dtype=torch.float16, device=cuda))
+    q, s = fp8.quantize_e4m3(x)
+    with pytest.raises(ValueError, match="out"):
+        fp8.dequantize_e4m3(q, s, out=torch.empty(1000, dtype=torch.float32, device=cuda))
+    with pytest.raises(ValueError, match="scale"):
+        fp8.dequantize_e4m3(q, s.cpu())
+    torch.cuda.synchronize()

@@ -236,3 +236,28 @@ def test_paged_kernels_on_amp_scheduler_batches(cuda, amp_lib):
     finally:
         s.close()
     assert n_pre > 0 and n_dec > 0
+
+
+def test_query_and_output_buffers_are_checked_before_launch(cuda, amp_lib):
+    ctx = np.array([40, 17], np.int32)
+    ctx, bt, npg, kp, vp = workloads.paged_inputs(seed=3, B=2, Hq=8, Hkv=2, ctx_lens=ctx)
+    k_pool, v_pool, btd, ctxd = to_dev(ctx, bt, kp, vp)
+    q = torch.zeros(2, 8, 128, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(ValueError, match="q: expected"):
+        paged.paged_attn_decode(q.float(), k_pool, v_pool, btd, ctxd, 64)
+    with pytest.raises(ValueError, match="q: expected"):
+        paged.paged_attn_decode(q[..., :64].contiguous(), k_pool, v_pool, btd, ctxd, 64)
+    with pytest.raises(ValueError, match="block_table"):
+        paged.paged_attn_decode(torch.zeros(3, 8, 128, dtype=torch.bfloat16, device=cuda),
+                                k_pool, v_pool, btd, ctxd, 64)
+    with pytest.raises(ValueError, match="lse must"):
+        paged.paged_attn_decode(q, k_pool, v_pool, btd, ctxd, 64,
+                                lse=torch.empty(2, 8, 1, device=cuda))
+    with pytest.raises(ValueError, match="out must"):
+        paged.paged_attn_decode(q, k_pool, v_pool, btd, ctxd, 64, out=torch.empty_like(q).float())
+    with pytest.raises(ValueError, match="workspace"):
+        paged.paged_attn_decode(q, k_pool, v_pool, btd, ctxd, 64,
+                                workspace=torch.empty(8, dtype=torch.uint8, device=cuda))
+    with pytest.raises(ValueError, match="q: expected"):
+        paged.paged_attn_prefill(q, k_pool, v_pool, btd, ctxd)   # prefill q is [B, Hq, Lq, D]
+    torch.cuda.synchronize()
