@@ -1,0 +1,79 @@
+"""The dump contract: dumps laid out as amp_b200/tools/parity_dump.cpp writes
+them (write_json: same keys, key order and default 6-significant-digit stream
+formatting) are consumed by AMP's own scripts/parity_check.py, which passes
+identical outputs, fails a perturbed one and refuses dumps of another
+shape/seed.  AMP's synthetic FAIL fixtures fail the same way.  Runs where the
+AMP sources are present (AMP_REF); the GPU test of the dump tool checks that
+the tool writes this schema."""
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from amp_b200.gemm import FP32_TILES
+
+AMP_REF = Path(os.environ.get("AMP_REF", "/root/reference"))
+PARITY = AMP_REF / "scripts" / "parity_check.py"
+pytestmark = pytest.mark.skipif(not PARITY.exists(), reason="AMP's parity_check.py not present")
+
+
+def write_dump(path, vendor, M, N, K, seed, entries):
+    """parity_dump.cpp's write_json, in Python (floats as std::ostream prints them)."""
+    g = lambda v: "%g" % v
+    lines = ["{", f'  "vendor": "{vendor}",', f'  "M": {M}, "N": {N}, "K": {K}, "seed": {seed},',
+             '  "tiles": [']
+    for i, (bm, bn, bk, gflops, ms, err, out) in enumerate(entries):
+        body = ",".join(g(v) for v in out)
+        lines.append(f'    {{"bm": {bm}, "bn": {bn}, "bk": {bk}, "gflops": {g(gflops)}, '
+                     f'"latency_ms": {g(ms)}, "max_rel_err_vs_cpu": {g(err)}, "output": [{body}]}}'
+                     + ("," if i + 1 != len(entries) else ""))
+    lines += ["  ]", "}"]
+    Path(path).write_text("\n".join(lines) + "\n")
+
+
+def parity(a, b):
+    return subprocess.run([sys.executable, str(PARITY), str(a), str(b)], capture_output=True,
+                          text=True, timeout=120)
+
+
+@pytest.fixture(scope="module")
+def harness_c(oracle_lib):
+    A, B = oracle_lib.amp_harness_inputs(96, 96, 96, 42)
+    return oracle_lib.gemm_fp32_amp(A, B).astype(np.float32)
+
+
+def entries(C):
+    return [(bm, bn, bk, 1234.5, 0.0123, 0.0, C.ravel()) for (bm, bn, bk) in FP32_TILES]
+
+
+def test_identical_outputs_pass(tmp_path, harness_c):
+    write_dump(tmp_path / "a.json", "nvidia", 96, 96, 96, 42, entries(harness_c))
+    write_dump(tmp_path / "b.json", "cpu-oracle", 96, 96, 96, 42, entries(harness_c))
+    r = parity(tmp_path / "a.json", tmp_path / "b.json")
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "FAIL" not in r.stdout
+
+
+def test_one_perturbed_element_fails(tmp_path, harness_c):
+    bad = harness_c.copy()
+    bad[5, 7] += np.float32(2e-3) * max(1.0, abs(float(bad[5, 7])))
+    write_dump(tmp_path / "a.json", "nvidia", 96, 96, 96, 42, entries(bad))
+    write_dump(tmp_path / "b.json", "cpu-oracle", 96, 96, 96, 42, entries(harness_c))
+    r = parity(tmp_path / "a.json", tmp_path / "b.json")
+    assert r.returncode == 1 and "FAIL" in r.stdout, r.stdout
+
+
+def test_other_seed_is_not_comparable(tmp_path, harness_c):
+    write_dump(tmp_path / "a.json", "nvidia", 96, 96, 96, 42, entries(harness_c))
+    write_dump(tmp_path / "b.json", "cpu-oracle", 96, 96, 96, 43, entries(harness_c))
+    r = parity(tmp_path / "a.json", tmp_path / "b.json")
+    assert r.returncode == 1 and "not comparable" in r.stdout
+
+
+def test_amp_synthetic_fail_fixtures_fail():
+    fx = AMP_REF / "tests" / "fixtures"
+    r = parity(fx / "synthetic_fail_a.json", fx / "synthetic_fail_b.json")
+    assert r.returncode == 1 and "FAIL" in r.stdout
