@@ -61,6 +61,31 @@ int mailbox_max_dev(const float* in, float* out, unsigned long long* const* mbox
     return AMP_OK;
 }
 
+namespace {
+
+// cudaMalloc + zero + IPC handle of `bytes`; on any failure nothing stays allocated.
+int create_shared(size_t bytes, void** out, void* handle_out) {
+    void* p = nullptr;
+    AMPB_CHECK_CUDA(cudaMalloc(&p, bytes));
+    const cudaError_t ez = cudaMemset(p, 0, bytes);
+    if (ez != cudaSuccess) {
+        cudaFree(p);
+        return cuda_status(ez, "cudaMemset");
+    }
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        set_error(AMP_ERR_UNSUPPORTED, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+        return AMP_ERR_UNSUPPORTED;
+    }
+    memcpy(handle_out, &h, sizeof(h));
+    *out = p;
+    return AMP_OK;
+}
+
+}  // namespace
+
 }  // namespace ampb
 
 using namespace ampb;
@@ -73,19 +98,7 @@ int amp_peer_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
 
 int amp_peer_mailbox_create(void** mailbox, void* handle_out) {
     AMPB_REQUIRE(mailbox && handle_out, AMP_ERR_INVALID, "NULL argument");
-    void* p = nullptr;
-    AMPB_CHECK_CUDA(cudaMalloc(&p, kMailboxBytes));
-    AMPB_CHECK_CUDA(cudaMemset(p, 0, kMailboxBytes));
-    cudaIpcMemHandle_t h;
-    const cudaError_t e = cudaIpcGetMemHandle(&h, p);
-    if (e != cudaSuccess) {
-        cudaFree(p);
-        set_error(AMP_ERR_UNSUPPORTED, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
-        return AMP_ERR_UNSUPPORTED;
-    }
-    memcpy(handle_out, &h, sizeof(h));
-    *mailbox = p;
-    return AMP_OK;
+    return create_shared(kMailboxBytes, mailbox, handle_out);
 }
 
 // A device buffer of `bytes` (zeroed) that the other processes of the node can
@@ -93,19 +106,7 @@ int amp_peer_mailbox_create(void** mailbox, void* handle_out) {
 // of the all-gather GEMM.  Freed with amp_peer_mailbox_free.
 int amp_peer_buffer_create(size_t bytes, void** buffer, void* handle_out) {
     AMPB_REQUIRE(buffer && handle_out && bytes > 0, AMP_ERR_INVALID, "bad peer buffer arguments");
-    void* p = nullptr;
-    AMPB_CHECK_CUDA(cudaMalloc(&p, bytes));
-    AMPB_CHECK_CUDA(cudaMemset(p, 0, bytes));
-    cudaIpcMemHandle_t h;
-    const cudaError_t e = cudaIpcGetMemHandle(&h, p);
-    if (e != cudaSuccess) {
-        cudaFree(p);
-        set_error(AMP_ERR_UNSUPPORTED, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
-        return AMP_ERR_UNSUPPORTED;
-    }
-    memcpy(handle_out, &h, sizeof(h));
-    *buffer = p;
-    return AMP_OK;
+    return create_shared(bytes, buffer, handle_out);
 }
 
 int amp_peer_mailbox_open(const void* handle, void** mailbox) {
