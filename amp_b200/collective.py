@@ -145,8 +145,10 @@ class PeerMailboxes:
                                   device=torch.device("cuda", torch.cuda.current_device()))
 
     def next_seq(self) -> int:
-        """Sequence number of the next exchange (1, 2, ...; the same on every rank)."""
-        self.seq = self.seq % 0xFFFFFFFF + 1
+        """Sequence number of the next exchange (the same on every rank): 1, 2, ...,
+        2**32 - 2, then 1 again.  An exchange uses mailbox row seq & 1, so consecutive
+        numbers must alternate in parity, also across the wrap (2**32 - 2 is even)."""
+        self.seq = self.seq % 0xFFFFFFFE + 1
         return self.seq
 
     def close(self) -> None:

@@ -19,8 +19,9 @@
 // step's sequence number.  Alternating the two rows by parity means a fast
 // rank can never overwrite a value a slow rank has not read yet: posting step
 // s + 2 needs every rank's step s + 1 value, which each rank writes only after
-// it has read all of step s.  The poll is bounded (2 s) and reports through
-// the device status word.
+// it has read all of step s.  Sequence numbers run 1 .. 2^32 - 2 and wrap to 1,
+// so the parity alternates across the wrap too.  The poll is bounded (2 s) and
+// reports through the device status word.
 #include <cstring>
 
 #include "peer.cuh"

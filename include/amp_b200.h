@@ -84,7 +84,9 @@ AMP_API int amp_fp8_amax_bf16_dev(const void* x_bf16, int64_t n, float* amax_out
  * AMP's collective layer would do (include/collective.hpp:79-85, allreduce).
  * `mailboxes` is a DEVICE array of `world` mailbox pointers (own at [rank]);
  * every rank calls with the same seq, which starts at 1 and grows by one per
- * call.  A peer that does not post within 2 s sets AMP_ERR_TIMEOUT in
+ * call, wrapping from 2^32 - 2 back to 1: consecutive calls on one set of
+ * mailboxes use alternate rows (seq & 1), so seq never repeats its parity.
+ * A peer that does not post within 2 s sets AMP_ERR_TIMEOUT in
  * amp_device_status(). */
 AMP_API int amp_fp8_amax_allreduce_peer_dev(const void* x_bf16, int64_t n, float* amax_out,
                                             void* workspace, size_t workspace_bytes,

@@ -118,3 +118,18 @@ def test_single_rank_is_identity():
     assert column_range(256, g, 64) == (0, 256)
     with pytest.raises(ValueError):
         column_range(100, CommGroup(0, 3), 1)
+
+
+def test_mailbox_sequence_alternates_parity_across_the_wrap():
+    """Exchanges use mailbox row seq & 1; two consecutive exchanges in one row would
+    let a fast rank overwrite a value a slow rank has not read."""
+    from amp_b200.collective import PeerMailboxes
+    mb = object.__new__(PeerMailboxes)
+    mb.seq = 0
+    first = [mb.next_seq() for _ in range(4)]
+    assert first == [1, 2, 3, 4]
+    mb.seq = 0xFFFFFFFE - 3
+    seqs = [mb.next_seq() for _ in range(8)]
+    assert 0 not in seqs and max(seqs) <= 0xFFFFFFFE
+    assert all((a ^ b) & 1 for a, b in zip(seqs, seqs[1:])), seqs
+    assert seqs[2] == 0xFFFFFFFE and seqs[3] == 1
