@@ -10,6 +10,7 @@ functions are backend-agnostic (gloo on CPU runs them in tests).
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 from dataclasses import dataclass
 
@@ -150,6 +151,19 @@ class PeerMailboxes:
         numbers must alternate in parity, also across the wrap (2**32 - 2 is even)."""
         self.seq = self.seq % 0xFFFFFFFE + 1
         return self.seq
+
+    @contextlib.contextmanager
+    def sequence(self):
+        """The sequence number of one exchange, given back if the body raises (the
+        exchange was never launched): a number used up without its exchange would
+        make the next exchange reuse the last one's row."""
+        prev = self.seq
+        seq = self.next_seq()
+        try:
+            yield seq
+        except BaseException:
+            self.seq = prev
+            raise
 
     def close(self) -> None:
         from ._lib import call

@@ -87,9 +87,10 @@ def amax_allreduce_peer(x: torch.Tensor, mailboxes, workspace: torch.Tensor | No
     _check_buf(workspace, torch.uint8, ws_b, dev, "workspace")
     a = out if out is not None else torch.empty(1, dtype=torch.float32, device=dev)
     ws = workspace if workspace is not None else torch.empty(ws_b, dtype=torch.uint8, device=dev)
-    call("amp_fp8_amax_allreduce_peer_dev", x.data_ptr(), x.numel(), a.data_ptr(), ws.data_ptr(),
-         ws.numel(), mailboxes.table.data_ptr(), mailboxes.g.rank, mailboxes.g.world,
-         mailboxes.next_seq(), _stream(dev))
+    with mailboxes.sequence() as seq:
+        call("amp_fp8_amax_allreduce_peer_dev", x.data_ptr(), x.numel(), a.data_ptr(),
+             ws.data_ptr(), ws.numel(), mailboxes.table.data_ptr(), mailboxes.g.rank,
+             mailboxes.g.world, seq, _stream(dev))
     return a
 
 

@@ -64,25 +64,26 @@ def matmul_allgather(A: torch.Tensor, B_slab: torch.Tensor, out: PeerBuffer,
         if not t.is_cuda or not t.is_contiguous() or tuple(t.shape) != shape:
             raise ValueError(f"{nm}: expected a contiguous CUDA tensor of shape {shape}")
     stream = torch.cuda.current_stream(A.device).cuda_stream
-    seq = out.mailboxes.next_seq()
-    if A.dtype == torch.bfloat16:
-        if B_slab.dtype != torch.bfloat16:
-            raise ValueError("A and B_slab must have the same type")
-        call("amp_gemm_bf16_allgather_dev", A.data_ptr(), B_slab.data_ptr(), out.table.data_ptr(),
-             gemm.AMP_DTYPE[out.dtype], g.rank, g.world, out.mailboxes.table.data_ptr(), seq,
-             M, Np, K, stream)
-    elif A.dtype in (torch.uint8, torch.float8_e4m3fn):
-        if B_slab.dtype not in (torch.uint8, torch.float8_e4m3fn):
-            raise ValueError("A and B_slab must both hold E4M3 codes")
-        rowcol = scale_a.numel() == M and M != 1 or scale_b.numel() == Np and Np != 1
-        n_a, n_b, mode = (M, Np, 2) if rowcol else (1, 1, 1)
-        sa = gemm._scale_tensor(scale_a, n_a, A.device, "scale_a")
-        sb = gemm._scale_tensor(scale_b, n_b, A.device, "scale_b")
-        call("amp_gemm_fp8e4m3_allgather_dev", A.data_ptr(), B_slab.data_ptr(), sa.data_ptr(),
-             sb.data_ptr(), mode, out.table.data_ptr(), gemm.AMP_DTYPE[out.dtype], g.rank,
-             g.world, out.mailboxes.table.data_ptr(), seq, M, Np, K, stream)
-    else:
-        raise ValueError(f"unsupported operand type {A.dtype}")
+    with out.mailboxes.sequence() as seq:
+        if A.dtype == torch.bfloat16:
+            if B_slab.dtype != torch.bfloat16:
+                raise ValueError("A and B_slab must have the same type")
+            call("amp_gemm_bf16_allgather_dev", A.data_ptr(), B_slab.data_ptr(),
+                 out.table.data_ptr(), gemm.AMP_DTYPE[out.dtype], g.rank, g.world,
+                 out.mailboxes.table.data_ptr(), seq, M, Np, K, stream)
+        elif A.dtype in (torch.uint8, torch.float8_e4m3fn):
+            if B_slab.dtype not in (torch.uint8, torch.float8_e4m3fn):
+                raise ValueError("A and B_slab must both hold E4M3 codes")
+            rowcol = scale_a.numel() == M and M != 1 or scale_b.numel() == Np and Np != 1
+            n_a, n_b, mode = (M, Np, 2) if rowcol else (1, 1, 1)
+            sa = gemm._scale_tensor(scale_a, n_a, A.device, "scale_a")
+            sb = gemm._scale_tensor(scale_b, n_b, A.device, "scale_b")
+            call("amp_gemm_fp8e4m3_allgather_dev", A.data_ptr(), B_slab.data_ptr(),
+                 sa.data_ptr(), sb.data_ptr(), mode, out.table.data_ptr(),
+                 gemm.AMP_DTYPE[out.dtype], g.rank, g.world, out.mailboxes.table.data_ptr(), seq,
+                 M, Np, K, stream)
+        else:
+            raise ValueError(f"unsupported operand type {A.dtype}")
     return out.tensor
 
 
@@ -131,9 +132,10 @@ def flash_attn_allgather(q, k, v, causal: bool, o_out: PeerBuffer, lse_out: Peer
     ks = k.reshape(B * Hkv, S, D)[lo:hi].contiguous()
     vs = v.reshape(B * Hkv, S, D)[lo:hi].contiguous()
     stream = torch.cuda.current_stream(q.device).cuda_stream
-    call("amp_flash_attn_fwd_allgather_dev", qs.data_ptr(), ks.data_ptr(), vs.data_ptr(),
-         o_out.table.data_ptr(), lse_out.table.data_ptr() if lse_out is not None else None,
-         g.rank, g.world, lo, o_out.mailboxes.table.data_ptr(), o_out.mailboxes.next_seq(),
-         1, hi - lo, hi - lo, S, S, D, int(causal), float(scale), stream)
+    with o_out.mailboxes.sequence() as seq:
+        call("amp_flash_attn_fwd_allgather_dev", qs.data_ptr(), ks.data_ptr(), vs.data_ptr(),
+             o_out.table.data_ptr(), lse_out.table.data_ptr() if lse_out is not None else None,
+             g.rank, g.world, lo, o_out.mailboxes.table.data_ptr(), seq,
+             1, hi - lo, hi - lo, S, S, D, int(causal), float(scale), stream)
     o = o_out.tensor.view(B, Hq, S, D)
     return o, (lse_out.tensor.view(B, Hq, S) if lse_out is not None else None)

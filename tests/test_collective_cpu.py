@@ -133,3 +133,19 @@ def test_mailbox_sequence_alternates_parity_across_the_wrap():
     assert 0 not in seqs and max(seqs) <= 0xFFFFFFFE
     assert all((a ^ b) & 1 for a, b in zip(seqs, seqs[1:])), seqs
     assert seqs[2] == 0xFFFFFFFE and seqs[3] == 1
+
+
+def test_sequence_number_is_given_back_when_nothing_was_launched():
+    """An exchange that raises before its launch must not use up a sequence number
+    (the next exchange would reuse the last one's row)."""
+    from amp_b200.collective import PeerMailboxes
+    mb = object.__new__(PeerMailboxes)
+    mb.seq = 0xFFFFFFFE
+    with pytest.raises(RuntimeError):
+        with mb.sequence() as seq:
+            assert seq == 1
+            raise RuntimeError("rejected before launch")
+    assert mb.seq == 0xFFFFFFFE
+    with mb.sequence() as seq:
+        assert seq == 1
+    assert mb.seq == 1 and mb.next_seq() == 2
