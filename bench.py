@@ -68,6 +68,16 @@ def load_traffic():
     return json.loads(p.read_text()) if p.exists() else {}
 
 
+def traffic_for(W, world: int, kernel: str):
+    """DRAM bytes per launch of `kernel` from the 1-GPU ncu captures
+    (profiles/traffic.json).  Under weak scaling a rank's launch is the captured
+    one at any N; under strong scaling at N > 1 it is a smaller one, and no figure
+    is reported."""
+    if world > 1 and W.scaling != "weak":
+        return None
+    return load_traffic().get(W.name, {}).get(kernel)
+
+
 def host_threads() -> int:
     return len(os.sched_getaffinity(0))
 
@@ -937,7 +947,7 @@ def run_amp(args, dist: Dist):
                 "peak": round(peak, 1), "unit": punit, "frac": round(achieved / peak, 4),
                 "peak_source": f"{peak_src}: MEASURED_PEAKS.json {pkey}" if peak_src == "measured"
                 else "fallback figure of the profiling recipe",
-                "traffic": load_traffic().get(W.name, {}).get(dom_name),
+                "traffic": traffic_for(W, dist.world, dom_name),
                 "algorithmic_units_per_launch": dom_units, "kernel_ms": round(dom_ms, 5),
                 "all_kernels": [{"kernel": n, "ms": round(m, 5),
                                  "rate": round(u / (m * 1e-3) / W.scale, 2)}

@@ -85,3 +85,14 @@ def test_instance_config_is_describe(name):
     w = object.__new__(W)
     w.args, w.dist = args, _Dist()
     assert w.config() == W.describe(args, 2)
+
+
+def test_traffic_is_reported_only_for_the_captured_launch():
+    t = bench.load_traffic()
+    q = "quantise (k_amax_partials + k_quant_encode)"
+    assert bench.traffic_for(bench.QuantWorkload, 1, q) == t["fp8_quant"][q]
+    assert bench.traffic_for(bench.QuantWorkload, 8, q) == t["fp8_quant"][q]   # weak scaling
+    g = "k_gemm_tc2<bf16>"
+    assert bench.traffic_for(bench.GemmWorkload, 1, g) == t["gemm_bf16"][g]
+    assert bench.traffic_for(bench.GemmWorkload, 2, g) is None                 # strong scaling
+    assert bench.traffic_for(bench.AttentionWorkload, 4, "k_flash_fwd<128>") is None
