@@ -75,3 +75,40 @@ def test_argument_errors_return_before_cuda(amp_lib):
 
 def test_abi_version(amp_lib):
     assert amp_lib.amp_abi_version() >= 100
+
+
+@pytest.mark.parametrize("header", sorted(p.name for p in (ROOT / "include").glob("*.h")))
+@pytest.mark.parametrize("lang", [["gcc", "-std=c99", "-pedantic", "-x", "c"],
+                                  ["g++", "-std=c++11", "-x", "c++"]])
+def test_headers_compile_as_c_and_cxx(header, lang):
+    """The boundary is a C ABI: each header stands alone in strict C and in C++."""
+    r = subprocess.run([*lang, "-Wall", "-Wextra", "-Werror", "-fsyntax-only",
+                        str(ROOT / "include" / header)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+
+
+LOADER = r"""
+#include <dlfcn.h>
+#include <stdio.h>
+#include "amp_plugin.h"
+int main(int argc, char** argv) {
+    void* h = dlopen(argv[1], RTLD_NOW);          /* as amp_validate_kernel loads plugins */
+    if (!h) { fprintf(stderr, "%s\n", dlerror()); return 2; }
+    amp_user_gemm_fp32_fn fn = (amp_user_gemm_fp32_fn)dlsym(h, AMP_PLUGIN_GEMM_FP32_SYMBOL);
+    if (!fn) { fprintf(stderr, "%s\n", dlerror()); return 3; }
+    return 0;
+}
+"""
+
+
+def test_plugin_resolves_through_amps_loader_contract(amp_lib, tmp_path):
+    """A plain-C host with no CUDA linked resolves the plugin symbol through
+    the header's typedef and name macro after dlopen(RTLD_NOW); nothing is called."""
+    import amp_b200
+    src = tmp_path / "loader.c"
+    src.write_text(LOADER)
+    exe = tmp_path / "loader"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", str(ROOT / "include"),
+                    str(src), "-o", str(exe), "-ldl"], check=True)
+    r = subprocess.run([str(exe), str(amp_b200.LIB_PATH)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
