@@ -4,7 +4,6 @@ Bar: max|x-ref|/max(1,|ref|) < 2e-2 for dQ, dK, dV (AMP's metric and bf16 bar; P
 and dS are rounded to bf16 before the tensor-core products, as in the forward).
 The forward's own O and lse feed the backward, as in training.
 """
-import numpy as np
 import pytest
 import torch
 

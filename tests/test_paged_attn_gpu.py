@@ -12,7 +12,7 @@ import torch
 import oracle
 from oracle import attention as ref
 from amp_b200 import paged, workloads
-from amp_b200._lib import AmpError, lib
+from amp_b200._lib import lib
 
 pytestmark = pytest.mark.gpu
 TOL_O = 2e-2
