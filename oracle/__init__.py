@@ -7,6 +7,8 @@ bench.py's CPU-baseline / reference legs may import it.  The product
   * ``liboracle.so`` (oracle.c): bit-exact E4M3 codec, amax quantiser,
     AMP's fp32 CPU GEMM and an fp64 GEMM.
   * ``attention.py``: fp64 FlashAttention-2 forward / paged-KV restatement.
+  * ``parity_dump.py``: the oracle ("B") side of the parity dumps of the
+    extension ops, in the dump tool's file layout.
   * ``_ref/`` (built by ``make -C oracle ref`` from the reference sources in
     place): AMP's own FP8 codec and its ``amp_validate_kernel`` binary.
 """

@@ -148,7 +148,12 @@ ORC_API float orc_scale_from_amax(float amax) {
 
 #include <float.h>
 ORC_API float orc_inv_scale(float scale) {
-    float inv = 1.0f / scale;
+    /* The reciprocal is taken of a volatile copy: inlined into a caller, GCC's
+       value-range propagation would conclude from "1/scale is infinite" that
+       scale == 0 and rewrite the caller's scale, which is wrong for a subnormal
+       scale (a tiny amax), whose reciprocal overflows. */
+    const volatile float s = scale;
+    float inv = 1.0f / s;
     return inv > FLT_MAX ? FLT_MAX : inv;   /* NaN stays NaN */
 }
 

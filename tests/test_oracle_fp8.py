@@ -124,3 +124,18 @@ def test_rowwise_and_colwise_are_per_slice_tensors(oracle_lib):
     for c in range(9):
         q, s, _ = oracle_lib.quant_e4m3(np.ascontiguousarray(x[:, c]))
         assert (qc[:, c] == q).all() and sc[c] == np.float32(s)
+
+
+def test_subnormal_scale_survives_the_reciprocal_clamp(oracle_lib):
+    """A tiny amax gives a subnormal scale whose reciprocal overflows and is clamped
+    to FLT_MAX; the scale itself must stay amax/448 (a compiler that infers
+    scale == 0 from an infinite reciprocal would return 0)."""
+    for a in (1e-38, 3e-39, 1e-39, 2e-40):   # all nonzero in bf16 (min 2^-133)
+        x16 = oracle_lib.f32_to_bf16_bits(np.array([a, -a / 2, 0.0], np.float32))
+        amax = oracle_lib.bf16_bits_to_f32(x16[:1])[0]
+        q, s, got_amax = oracle_lib.quant_e4m3(x16)
+        assert got_amax == amax
+        assert s == np.float32(amax) / np.float32(448) and s > 0, (a, s)
+        # the reciprocal is clamped, so the codes are those of x * FLT_MAX
+        big = np.float32(np.finfo(np.float32).max)
+        assert np.array_equal(q, oracle_lib.e4m3_encode(oracle_lib.bf16_bits_to_f32(x16) * big))

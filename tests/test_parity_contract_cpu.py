@@ -5,7 +5,7 @@ order, 6-significant-digit stream formatting), so dumps written here are dumps
 as the tool writes them.  AMP's own scripts/parity_check.py (where the AMP
 sources are present, AMP_REF) passes the B200 dump against the oracle's, passes
 identical outputs, fails a perturbed one and refuses another shape/seed; AMP's
-synthetic FAIL fixtures fail the same way."""
+synthetic FAIL fixtures fail the same way.  (write_dump: oracle/parity_dump.py.)"""
 import os
 import subprocess
 import sys
@@ -15,25 +15,12 @@ import numpy as np
 import pytest
 
 from amp_b200.gemm import FP32_TILES
+from oracle.parity_dump import write_dump
 
 AMP_REF = Path(os.environ.get("AMP_REF", "/root/reference"))
 PARITY = AMP_REF / "scripts" / "parity_check.py"
 needs_amp = pytest.mark.skipif(not PARITY.exists(), reason="AMP's parity_check.py not present")
 B200_DUMP = Path(__file__).resolve().parent / "golden" / "b200_parity_dump_96.json"
-
-
-def write_dump(path, vendor, M, N, K, seed, entries):
-    """parity_dump.cpp's write_json, in Python (floats as std::ostream prints them)."""
-    g = lambda v: "%g" % v
-    lines = ["{", f'  "vendor": "{vendor}",', f'  "M": {M}, "N": {N}, "K": {K}, "seed": {seed},',
-             '  "tiles": [']
-    for i, (bm, bn, bk, gflops, ms, err, out) in enumerate(entries):
-        body = ",".join(g(v) for v in out)
-        lines.append(f'    {{"bm": {bm}, "bn": {bn}, "bk": {bk}, "gflops": {g(gflops)}, '
-                     f'"latency_ms": {g(ms)}, "max_rel_err_vs_cpu": {g(err)}, "output": [{body}]}}'
-                     + ("," if i + 1 != len(entries) else ""))
-    lines += ["  ]", "}"]
-    Path(path).write_text("\n".join(lines) + "\n")
 
 
 def parity(a, b):
