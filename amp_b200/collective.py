@@ -156,7 +156,13 @@ class PeerMailboxes:
     def sequence(self):
         """The sequence number of one exchange, given back if the body raises (the
         exchange was never launched): a number used up without its exchange would
-        make the next exchange reuse the last one's row."""
+        make the next exchange reuse the last one's row.
+
+        This keeps the ranks in step when every rank raises alike, which is the
+        case for argument checks that depend only on shapes and types every rank
+        shares.  If only some ranks raise, the others have launched and used the
+        number (their exchange ends in the device timeout status): call
+        `resync()` on every rank before the next exchange."""
         prev = self.seq
         seq = self.next_seq()
         try:
@@ -164,6 +170,18 @@ class PeerMailboxes:
         except BaseException:
             self.seq = prev
             raise
+
+    def resync(self) -> int:
+        """Collective: agree on the sequence counter after an exchange that failed
+        on some ranks only.  Every rank takes the largest counter of the group, so
+        the next exchange has one number everywhere and a row no rank used last."""
+        if self.g.world > 1:
+            dev = (torch.device("cuda", torch.cuda.current_device())
+                   if dist.get_backend(self.g.group) == "nccl" else torch.device("cpu"))
+            t = torch.tensor([self.seq], dtype=torch.int64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.g.group)
+            self.seq = int(t.item())
+        return self.seq
 
     def close(self) -> None:
         from ._lib import call

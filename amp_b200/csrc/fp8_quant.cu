@@ -409,36 +409,41 @@ int amp_user_fp8_dequant_e4m3(const uint8_t* q, int64_t n, float scale, uint16_t
 // ---------------------------------------------------------------------------
 // Allocation-free variant of the per-tensor quantiser.
 //
-// Some callers cannot allocate device memory at the point where they
-// quantise: an inference-engine plugin whose enqueue() may only use memory
-// the engine handed it, code running while a CUDA graph is being captured
-// (cudaMalloc is not allowed there), or a host runtime that owns every
-// device allocation itself.  amp_fp8_quant_e4m3_dev asks them for a
-// workspace; this entry point instead keeps the amax pass's per-block
-// partial maxima in a file-scope device array, so the caller passes only the
-// input and the outputs.
+// Some callers cannot call cudaMalloc at the point where they quantise: an
+// inference-engine plugin whose enqueue() may only use the memory its engine
+// handed it, or a host runtime that owns every device allocation itself and
+// budgets it up front.  amp_fp8_quant_e4m3_dev asks them for a workspace;
+// this entry point instead keeps the amax pass's per-block partial maxima in
+// a file-scope device array, so the caller passes only the input and the
+// outputs, and the call allocates nothing.
 //
 // Limits and sharing rules:
 //   * the array holds kNoAllocParts floats (8 KiB) on every GPU that loads
 //     the library, for the life of the process;
 //   * the number of partials does not grow with n: the amax pass launches
-//     at most kNoAllocParts blocks (8 per SM, capped) and grid-strides over
-//     the tensor, so any n >= 0 is accepted; the entry point still checks
-//     the launch's partial count against the array size and returns
-//     AMP_ERR_INVALID with a message rather than overrun it;
+//     at most kMaxParts blocks (8 per SM, capped) and grid-strides over the
+//     tensor, and a static_assert keeps kMaxParts within the array, so any
+//     n >= 0 is accepted; the entry point still checks the launch's partial
+//     count against the array and returns AMP_ERR_INVALID with a message
+//     rather than overrun it;
 //   * every call on a device shares the array and leaves its contents
-//     behind; nothing in it has to start at zero (the amax pass overwrites
-//     every slot the encode pass reads), but two calls whose kernels
-//     overlap on the GPU (different streams, no ordering between them)
-//     race on it and may produce wrong scales;
-//   * the first call on each device looks up the array's device address
-//     with cudaGetSymbolAddress (the host-side name is only a stand-in);
-//     make that first call before capturing a stream into a CUDA graph.
+//     behind; nothing in it has to start at zero (the amax pass writes every
+//     slot the encode pass then reads), but two calls whose kernels overlap
+//     on the GPU (different streams, no ordering between them) race on it and
+//     may produce wrong scales;
+//   * the first call on each device, with that device current, looks up the
+//     array's device address with cudaGetSymbolAddress (in host code the
+//     array's name is only a stand-in) and caches it for the process; make
+//     that first call before any stream capture.  The cache assumes the
+//     device's primary context lives as long as the process: after a
+//     cudaDeviceReset the cached address is stale.
 // ---------------------------------------------------------------------------
 namespace ampb {
 namespace {
 
 constexpr int kNoAllocParts = 2048;
+static_assert(kNoAllocParts >= kMaxParts,
+              "the no-alloc scratch must hold every partial the amax pass can write");
 static __device__ __align__(256) float g_noalloc_parts[kNoAllocParts];
 
 constexpr int kMaxDevices = 64;

@@ -101,15 +101,18 @@ AMP_API int amp_fp8_quant_e4m3_from_amax_dev(const void* x_bf16, int64_t n, cons
 AMP_API int amp_fp8_dequant_e4m3_dev(const uint8_t* q, int64_t n, const float* scale, void* y_bf16,
                              void* stream);
 
-/* Allocation-free form of amp_fp8_quant_e4m3_dev, for callers that may not
- * allocate device memory (an engine plugin limited to memory the engine hands
- * it, code running during CUDA graph capture, a runtime that owns all device
- * allocations).  No counterpart in the reference.  The amax pass's partial
+/* Allocation-free form of amp_fp8_quant_e4m3_dev, for callers that cannot
+ * call cudaMalloc when they quantise (an engine plugin limited to the memory
+ * its engine hands it, a runtime that owns and budgets every device
+ * allocation).  No counterpart in the reference.  The amax pass's partial
  * maxima live in a library-owned 8 KiB device array per GPU (held until
- * process exit), so only input and outputs are passed; any n >= 0 is
- * accepted.  The first call on each device resolves that array's address
- * (cudaGetSymbolAddress): make it before capturing a stream into a graph.
- * Calls share the array: calls whose kernels overlap on one GPU race. */
+ * process exit), so only input and outputs are passed and nothing is
+ * allocated; any n >= 0 is accepted (the pass grid-strides, its partial count
+ * is capped at the array's size).  The first call on each device resolves the
+ * array's address (cudaGetSymbolAddress) and caches it for the process: make
+ * it before any stream capture, and not across a cudaDeviceReset.  Calls
+ * share the array and it keeps the last call's partials: calls whose kernels
+ * overlap on one GPU race. */
 AMP_API int amp_fp8_quant_e4m3_noalloc_dev(const void* x_bf16, int64_t n, uint8_t* q,
                                            float* scale_out, float* amax_out, void* stream);
 

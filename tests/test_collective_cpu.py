@@ -103,8 +103,31 @@ def body_other_collectives(rank, world):
     barrier(g)
 
 
+def body_mailbox_resync_after_one_rank_raises(rank, world):
+    """Rank 1 rejects an exchange before its launch (a check that failed on it
+    alone) while rank 0 used the number; resync() puts both on one counter."""
+    from amp_b200.collective import CommGroup, PeerMailboxes
+    mb = object.__new__(PeerMailboxes)
+    mb.g, mb.seq = CommGroup.current(), 6
+    try:
+        with mb.sequence() as seq:
+            assert seq == 7
+            if rank == 1:
+                raise ValueError("rejected on this rank only")
+    except ValueError:
+        pass
+    assert mb.seq == (7 if rank == 0 else 6)
+    assert mb.resync() == 7
+    with mb.sequence() as seq:
+        got = torch.tensor([seq])
+    both = [torch.zeros(1, dtype=got.dtype) for _ in range(world)]
+    dist.all_gather(both, got)
+    assert [int(t) for t in both] == [8] * world
+
+
 @pytest.mark.parametrize("body", ["body_global_amax", "body_gather_columns", "body_gather_heads",
-                                  "body_other_collectives"])
+                                  "body_other_collectives",
+                                  "body_mailbox_resync_after_one_rank_raises"])
 def test_two_ranks_gloo(body):
     run_ranks(body)
 

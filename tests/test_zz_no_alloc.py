@@ -1,14 +1,13 @@
 """The allocation-free quantiser entry point gives the same result as the
 workspace one.
 
-amp_fp8_quant_e4m3_noalloc_dev serves callers that are not allowed to
-allocate device memory when they quantise (for example an engine plugin that
-may only use the memory its engine passes in, or code running while a stream
-is captured into a CUDA graph).  It keeps its scratch in a library-owned
-device array instead of a caller workspace.  This file is collected last so a
-failure here never hides the other tests' results.
+amp_fp8_quant_e4m3_noalloc_dev serves callers that cannot call cudaMalloc when
+they quantise (for example an engine plugin that may only use the memory its
+engine passes in, or a runtime that owns and budgets every device allocation).
+It keeps its scratch in a library-owned device array instead of a caller
+workspace.  This file is collected last so a failure here never hides the
+other tests' results.
 """
-import ctypes as C
 
 import numpy as np
 import pytest
@@ -44,9 +43,11 @@ def _run(entry, x, with_workspace):
 
 
 def test_noalloc_matches_workspace_entry_point_twice_in_a_row(cuda, amp_lib):
-    # Two calls in a row on different tensors: the second is much smaller, so
-    # any partial left behind by the first call that the second read would
-    # show up as a wrong amax/scale.
+    # Two calls in a row on different tensors through the shared scratch
+    # array: a large one (one partial maximum per block of a full grid, outliers up to ~250)
+    # and then a small one whose values are all far below the first call's
+    # amax.  Both must give the workspace entry point's codes, scale and amax
+    # exactly, i.e. the second call's result depends on its own input only.
     for n, seed in ((1 << 22) + 5, 101), (3001, 102):
         bits = workloads.quant_input_numpy(n, seed=seed)
         if n == 3001:
