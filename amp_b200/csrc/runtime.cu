@@ -1,11 +1,13 @@
 // runtime.cu -- status reporting, device queries and the host-pointer staging
 // pool shared by the amp_user_* entry points.
 #include <cstdarg>
+#include <cstddef>
 #include <cstring>
 #include <mutex>
 #include <vector>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 #include "runtime.h"
 
 namespace ampb {
@@ -119,9 +121,17 @@ int device_status(int** out) {
     std::lock_guard<std::mutex> lk(g_status_mu);
     if ((int)g_status.size() <= dev) g_status.resize(dev + 1, nullptr);
     if (!g_status[dev]) {
+        // status word (int 0) + wait limit (u64 at byte 8), see tc_common.cuh
+        struct Block { int status[2]; unsigned long long limit_ns; };
+        static_assert(offsetof(Block, limit_ns) == kStatusLimitOffsetInts * sizeof(int), "layout");
+        const Block init = {{AMP_DEV_OK, 0}, kWaitTimeoutNs};
         int* p = nullptr;
-        AMPB_CHECK_CUDA(cudaMalloc(&p, sizeof(int)));
-        AMPB_CHECK_CUDA(cudaMemset(p, 0, sizeof(int)));
+        AMPB_CHECK_CUDA(cudaMalloc(&p, sizeof(Block)));
+        const cudaError_t e = cudaMemcpy(p, &init, sizeof(Block), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            cudaFree(p);
+            return cuda_status(e, "cudaMemcpy(status block)");
+        }
         g_status[dev] = p;
     }
     *out = g_status[dev];
@@ -149,6 +159,20 @@ int amp_device_status(int clear) {
         ampb::set_error(AMP_ERR_TIMEOUT, "a kernel's bounded wait expired (device status %d)", v);
         return AMP_ERR_TIMEOUT;
     }
+    return AMP_OK;
+}
+
+int amp_set_wait_timeout_ns(uint64_t ns) {
+    AMPB_REQUIRE(ns <= 600ull * 1000000000ull, AMP_ERR_INVALID,
+                 "wait limit %llu ns is above the 600 s cap", (unsigned long long)ns);
+    int* p = nullptr;
+    int rc = ampb::device_status(&p);
+    if (rc) return rc;
+    const unsigned long long v = ns ? ns : ampb::kWaitTimeoutNs;
+    // ordered after every kernel already queued on the device (blocking copy)
+    AMPB_CHECK_CUDA(cudaDeviceSynchronize());
+    AMPB_CHECK_CUDA(cudaMemcpy(p + ampb::kStatusLimitOffsetInts, &v, sizeof(v),
+                               cudaMemcpyHostToDevice));
     return AMP_OK;
 }
 

@@ -2,10 +2,11 @@
 // mbarriers with bounded waits, TMA tile loads, tcgen05 (TMEM alloc, MMA,
 // commit, loads, fences) and the shared-memory / instruction descriptors.
 //
-// Every wait on an mbarrier is bounded: after kWaitTimeoutNs of polling the
-// waiting thread records AMP_DEV_ERR_TIMEOUT in the kernel's status word and
-// returns false, so a broken pipeline ends the kernel instead of hanging the
-// GPU.  Callers propagate the failure by leaving their loops.
+// Every wait on an mbarrier is bounded: after the device's wait limit of
+// polling (2 s unless amp_set_wait_timeout_ns changed it) the waiting thread
+// records AMP_DEV_ERR_TIMEOUT in the kernel's status word and returns false,
+// so a broken pipeline ends the kernel instead of hanging the GPU.  Callers
+// propagate the failure by leaving their loops.
 #pragma once
 
 #include <cuda.h>
@@ -14,8 +15,17 @@
 
 namespace ampb {
 
-constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s, the default wait limit
 enum : int { AMP_DEV_OK = 0, AMP_DEV_ERR_TIMEOUT = 1, AMP_DEV_ERR_BAD_PAGE = 2 };
+
+// The per-device status block (runtime.cu) is 16 bytes: the status word at
+// int [0] and the wait limit in ns as a u64 at byte 8.  Kernels receive the
+// status word's address, so the limit needs no argument of its own; it is
+// read only once a wait has failed its first try.
+constexpr int kStatusLimitOffsetInts = 2;
+__device__ __forceinline__ uint64_t wait_limit_ns(const int* status) {
+    return *reinterpret_cast<const volatile unsigned long long*>(status + kStatusLimitOffsetInts);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -88,13 +98,14 @@ template <bool kSleep = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
     if (mbar_try_wait<kSleep>(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
+    const uint64_t limit = wait_limit_ns(status);
     uint32_t n = 0;
     // a sleeping try_wait may take up to the hint, so the clock is read every time
     constexpr uint32_t kCheckMask = kSleep ? 0u : 1023u;
     while (true) {
         if (mbar_try_wait<kSleep>(bar, parity)) return true;
         if ((++n & kCheckMask) == 0) {
-            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            if (globaltimer_ns() - t0 > limit) {
                 atomicExch(status, AMP_DEV_ERR_TIMEOUT);
                 return false;
             }

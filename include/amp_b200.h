@@ -50,6 +50,12 @@ AMP_API int amp_abi_version(void);
  * failure path of the pipelined tensor-core kernels, which end instead of
  * hanging.  clear != 0 resets the flag. */
 AMP_API int amp_device_status(int clear);
+/* Sets the current device's limit on every bounded device-side wait (mbarrier
+ * waits of the pipelined kernels, peer-mailbox polls); 0 restores the default
+ * of 2 s.  Takes effect for kernels launched after it returns (it synchronises
+ * the device first).  The reference has no device-side waits; this is the
+ * failure path's knob, e.g. a short limit in a test whose peer never posts. */
+AMP_API int amp_set_wait_timeout_ns(uint64_t ns);
 
 /* ------------------------------------------------------------------------
  * FP8 E4M3 per-tensor amax-scaled quantise / dequantise.
