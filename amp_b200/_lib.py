@@ -60,6 +60,7 @@ SIGNATURES: dict[str, tuple] = {
     "amp_paged_pack_block_table": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
     "amp_paged_pool_bytes": (_sz, [_i32, _i32, _i32]),
     "amp_gemm_fp32_dev": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp]),
+    "amp_gemm_fp32_exact_dev": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "amp_gemm_fp32_3xtf32_dev": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "amp_gemm_fp32_tile_dev": (_i32, [_i32, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "amp_user_gemm_fp32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32]),
@@ -71,6 +72,24 @@ SIGNATURES: dict[str, tuple] = {
     "amp_peer_mailbox_close": (_i32, [_vp]),
     "amp_peer_mailbox_free": (_i32, [_vp]),
     "amp_peer_allreduce_max_f32": (_i32, [_vp, _vp, _vp, _i32, _i32, C.c_uint, _vp]),
+    "amp_comm_available": (_i32, []),
+    "amp_comm_nccl_version": (_i32, [_vp]),
+    "amp_comm_unique_id": (_i32, [_vp]),
+    "amp_comm_init_rank": (_i32, [_vp, _i32, _i32, _i32, _vp]),
+    "amp_comm_destroy": (_i32, [_vp]),
+    "amp_comm_rank": (_i32, [_vp, _vp, _vp, _vp]),
+    "amp_comm_allreduce": (_i32, [_vp, _vp, _sz, _i32, _i32, _vp]),
+    "amp_comm_allreduce_max_f32": (_i32, [_vp, _vp, _sz, _vp]),
+    "amp_comm_allgather": (_i32, [_vp, _vp, _vp, _sz, _i32, _vp]),
+    "amp_comm_broadcast": (_i32, [_vp, _vp, _sz, _i32, _i32, _vp]),
+    "amp_comm_barrier": (_i32, [_vp, _vp]),
+    "amp_gemm_sharded_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32]),
+    "amp_gemm_bf16_sharded_dev": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _sz,
+                                         _vp]),
+    "amp_gemm_fp8e4m3_sharded_dev": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32,
+                                            _i32, _vp, _sz, _vp]),
+    "amp_flash_attn_fwd_sharded_dev": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
+                                              _i32, _i32, _i32, _i32, _f32, _vp]),
 }
 
 

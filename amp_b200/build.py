@@ -80,12 +80,28 @@ def build(jobs: int | None = None, force: bool = False, verbose: bool = False) -
             raise RuntimeError(f"link failed:\n{r.stderr}\n{r.stdout}")
         os.replace(tmp, LIB)
     build_tools(force)
+    check_dropins(force)
     if verbose:
         print(f"built {LIB}")
     return LIB
 
 
 TOOLS = PKG / "tools"
+DROPIN = PKG / "dropin"
+
+
+def check_dropins(force: bool = False) -> None:
+    """Compile the stand-alone kernel files under dropin/ for sm_100a (objects
+    only, nothing links them): they are handed to AMP's scripts/amp_check.sh,
+    which builds its own wrapper around them."""
+    for src in sorted(DROPIN.glob("*.cu")):
+        obj = BUILD / ("dropin_" + src.stem + ".o")
+        if force or _stale(obj, [src]):
+            cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-c", str(src),
+                   "-o", str(obj)]
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode != 0:
+                raise RuntimeError(f"nvcc failed for {src.name}:\n{r.stderr}")
 
 
 def build_tools(force: bool = False) -> None:

@@ -38,7 +38,8 @@ def _check(t: torch.Tensor, dtype, shape, name):
 
 def launch_matmul(cfg: TileCfg, dA: torch.Tensor, dB: torch.Tensor, dC: torch.Tensor,
                   M: int, N: int, K: int) -> None:
-    """C = A @ B in fp32 (AMP::launch_matmul)."""
+    """C = A @ B in fp32 (AMP::launch_matmul), accumulated in the order and
+    rounding of AMP's CPU reference GEMM (bit-identical to it)."""
     _check(dA, torch.float32, (M, K), "A")
     _check(dB, torch.float32, (K, N), "B")
     _check(dC, torch.float32, (M, N), "C")
@@ -46,13 +47,17 @@ def launch_matmul(cfg: TileCfg, dA: torch.Tensor, dB: torch.Tensor, dC: torch.Te
          dC.data_ptr(), M, N, K, _stream(dA))
 
 
-def matmul_fp32(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
+def matmul_fp32(A: torch.Tensor, B: torch.Tensor, exact: bool = False) -> torch.Tensor:
+    """C = A @ B in fp32.  exact=False: FFMA (one rounding per multiply-add);
+    exact=True: product and sum rounded separately, k ascending, as AMP's CPU
+    reference GEMM does (bit-identical to it)."""
     M, K = A.shape
     N = B.shape[1]
     C = torch.empty((M, N), dtype=torch.float32, device=A.device)
     _check(A, torch.float32, (M, K), "A")
     _check(B, torch.float32, (K, N), "B")
-    call("amp_gemm_fp32_dev", A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, _stream(A))
+    call("amp_gemm_fp32_exact_dev" if exact else "amp_gemm_fp32_dev", A.data_ptr(), B.data_ptr(),
+         C.data_ptr(), M, N, K, _stream(A))
     return C
 
 

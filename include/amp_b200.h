@@ -35,11 +35,20 @@ extern "C" {
 #define AMP_ERR_UNSUPPORTED (-2) /* valid request this build does not implement        */
 #define AMP_ERR_TIMEOUT (-3)     /* a bounded device-side wait expired                 */
 #define AMP_ERR_NO_DEVICE (-4)   /* no CUDA device visible                             */
+#define AMP_ERR_COMM (-5)        /* a collective (NCCL) call failed                    */
 
 /* Element types named in signatures that take a dtype selector. */
 #define AMP_DTYPE_F32 0
 #define AMP_DTYPE_BF16 1
-#define AMP_DTYPE_E4M3 2   /* FP8 GEMM output only (amp_gemm_fp8e4m3_ex_dev) */
+#define AMP_DTYPE_E4M3 2   /* FP8 GEMM output; moved as bytes by the collectives */
+#define AMP_DTYPE_I32 3    /* collectives only (block tables, context lengths) */
+
+/* Reductions of amp_comm_allreduce, in the order of AMP::ReduceOp
+ * (include/collective.hpp:49). */
+#define AMP_REDUCE_SUM 0
+#define AMP_REDUCE_MAX 1
+#define AMP_REDUCE_MIN 2
+#define AMP_REDUCE_PROD 3
 
 /* Message for the last nonzero status returned on this thread. */
 AMP_API const char* amp_last_error(void);
@@ -132,10 +141,18 @@ AMP_API int amp_user_fp8_dequant_e4m3(const uint8_t* q, int64_t n, float scale, 
  * Replaces AMP::launch_matmul(TileCfg, dA, dB, dC, M, N, K, stream)
  * (kernels/matmul.cuh:96-98, dispatcher kernels/matmul.cu:24-35).  The host
  * pointer form is amp_user_gemm_fp32 in amp_plugin.h.
+ * amp_gemm_fp32_dev accumulates with FFMA (one rounding per multiply-add).
  * ---------------------------------------------------------------------- */
 AMP_API int amp_gemm_fp32_dev(const float* A, const float* B, float* C, int M, int N, int K,
                               void* stream);
-/* Same, named by one of AMP's tile configs (bm,bn,bk) in {(16,16,16),
+/* Exact form: each product rounded to fp32, then each sum, k ascending from
+ * 0 -- the order and rounding of AMP's cpu_reference_gemm
+ * (tests/amp_validate_kernel.cpp:20-28), so C is bit-identical to the CPU
+ * reference AMP's validator and parity dump compare against.  The plugin
+ * amp_user_gemm_fp32 and amp_gemm_fp32_tile_dev use this form. */
+AMP_API int amp_gemm_fp32_exact_dev(const float* A, const float* B, float* C, int M, int N,
+                                    int K, void* stream);
+/* Exact form named by one of AMP's tile configs (bm,bn,bk) in {(16,16,16),
  * (32,16,16), (32,32,16), (32,32,32)} or (0,0,0); any other config is an
  * error, as in the reference dispatcher ("unknown FP32 tile cfg").  The tile
  * names the dump entry; the kernel's own blocking is chosen by size. */
@@ -146,7 +163,7 @@ AMP_API int amp_gemm_fp32_tile_dev(int bm, int bn, int bk, const float* A, const
  * hi/lo split of each operand, opt-in: ~5x the FFMA kernel's rate at 4096^3, but
  * the tensor core's fp32 accumulation makes the error grow with K (max_rel_err
  * 1.9e-4 at 1024^3 for U[-1,1] inputs; AMP's validator inputs in [-10, 10] fail
- * its 1e-3 bar), so amp_gemm_fp32_dev / the plugin stay on FFMA.  K and N must be
+ * its 1e-3 bar), so the plugin stays on the exact CUDA-core form.  K and N must be
  * multiples of 4 and the operands 16-byte aligned; uses library scratch (calls on
  * one device must be ordered). */
 AMP_API int amp_gemm_fp32_3xtf32_dev(const float* A, const float* B, float* C, int M, int N,
@@ -327,6 +344,68 @@ AMP_API int amp_peer_mailbox_free(void* mailbox);
 /* all-reduce(max) of one float per rank through the mailboxes (device in/out). */
 AMP_API int amp_peer_allreduce_max_f32(const float* in, float* out, void* const* mailboxes,
                                        int rank, int world, unsigned seq, void* stream);
+
+/* ----------------------------------------------------------------------
+ * Collectives over NCCL for C and C++ hosts: one communicator per process
+ * and GPU.  Replaces AMP's CommGroup / CommUniqueId and their operations
+ * (include/collective.hpp:34-104, src/collective.cpp:101-203).  NCCL is
+ * loaded at run time (libnccl.so.2, or the file named by AMP_B200_NCCL_LIB),
+ * so the library itself does not depend on it.  Operations are asynchronous
+ * on `stream`; every rank must issue the same operations in the same order.
+ * ---------------------------------------------------------------------- */
+#define AMP_COMM_UNIQUE_ID_BYTES 128 /* CommUniqueId::kBytes (collective.hpp:43-46) */
+typedef struct amp_comm amp_comm;
+
+/* 1 if NCCL could be loaded, else 0 (amp_last_error() says why). */
+AMP_API int amp_comm_available(void);
+AMP_API int amp_comm_nccl_version(int* version);
+/* comm_get_unique_id (collective.hpp:60): on one rank, then shared out of band. */
+AMP_API int amp_comm_unique_id(uint8_t* id /* AMP_COMM_UNIQUE_ID_BYTES */);
+/* comm_init_rank (collective.hpp:64-65): makes device_id current, joins the group. */
+AMP_API int amp_comm_init_rank(amp_comm** comm, int rank, int world, int device_id,
+                               const uint8_t* id);
+/* comm_destroy (collective.hpp:71); NULL is a no-op. */
+AMP_API int amp_comm_destroy(amp_comm* comm);
+AMP_API int amp_comm_rank(const amp_comm* comm, int* rank, int* world, int* device_id);
+/* allreduce (collective.hpp:79-80), in place; dtype AMP_DTYPE_F32/BF16/I32,
+ * op AMP_REDUCE_*. */
+AMP_API int amp_comm_allreduce(amp_comm* comm, void* buf, size_t count, int dtype, int op,
+                               void* stream);
+/* The quantiser's exchange: all-reduce(MAX) of fp32 values (a sharded amax). */
+AMP_API int amp_comm_allreduce_max_f32(amp_comm* comm, float* buf, size_t count, void* stream);
+/* allgather (collective.hpp:87-89): recv[r * count ...] = send of rank r;
+ * in place when send == recv + rank * count elements. */
+AMP_API int amp_comm_allgather(amp_comm* comm, const void* send, void* recv, size_t count,
+                               int dtype, void* stream);
+/* broadcast (collective.hpp:83-84), in place. */
+AMP_API int amp_comm_broadcast(amp_comm* comm, void* buf, size_t count, int dtype, int root,
+                               void* stream);
+/* barrier (collective.hpp:104): a 1-float all-reduce on library staging memory. */
+AMP_API int amp_comm_barrier(amp_comm* comm, void* stream);
+
+/* N-sharded GEMM, NCCL form (no reference counterpart; the reference's GEMM
+ * is single-GPU): every rank holds all of A [M,K] and its column slab
+ * B_slab [K,Np] of B (columns rank*Np .. rank*Np+Np-1), computes its block of
+ * C in `workspace`, all-gathers the blocks in place and lays them out as the
+ * full row-major C [M, world*Np] on every rank.  C fp32 or bf16.  The
+ * workspace holds world*M*Np elements of C's type. */
+AMP_API size_t amp_gemm_sharded_workspace_bytes(int M, int Np, int world, int c_dtype);
+AMP_API int amp_gemm_bf16_sharded_dev(amp_comm* comm, const void* A, const void* B_slab, void* C,
+                                      int c_dtype, int M, int Np, int K, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+AMP_API int amp_gemm_fp8e4m3_sharded_dev(amp_comm* comm, const uint8_t* A, const uint8_t* B_slab,
+                                         const float* scale_a, const float* scale_b,
+                                         int scale_mode, void* C, int c_dtype, int M, int Np,
+                                         int K, void* workspace, size_t workspace_bytes,
+                                         void* stream);
+/* Sharded FlashAttention-2 forward, NCCL form: q/k/v/o/lse as in
+ * amp_flash_attn_fwd_bf16_dev on every rank; each rank computes a contiguous
+ * slice -- of batch*heads when Hq == Hkv, of whole sequences (batch) under
+ * GQA -- into its part of o / lse, then o and lse are all-gathered in place. */
+AMP_API int amp_flash_attn_fwd_sharded_dev(amp_comm* comm, const void* q, const void* k,
+                                           const void* v, void* o, float* lse, int B, int Hq,
+                                           int Hkv, int S_q, int S_kv, int head_dim, int causal,
+                                           float scale, void* stream);
 
 #ifdef __cplusplus
 }
