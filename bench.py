@@ -4,8 +4,13 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
                     [--impl amp_b200|reference] [--size S]
 
+The default (``--workload suite``) prints the headline workload's line with
+every other workload's full record (value, ms_per_step, roofline with traffic,
+clocks, e2e, cpu_baseline) in its ``workloads`` array, all measured in the
+same process; the non-headline workloads time min(K, --suite-steps) steps.
+
 Workloads (``--workload``):
-  fp8_quant (default)  per-tensor amax-scaled FP8 E4M3 quantise + dequantise of
+  fp8_quant (headline) per-tensor amax-scaled FP8 E4M3 quantise + dequantise of
                        2^26 bf16 values (N(0,1), 0.1% N(0,50) outliers); metric =
                        algorithmic bytes (8 B/element) per second.  N > 1: each
                        rank its own 2^26 shard against the global amax (a 1-float
@@ -14,13 +19,18 @@ Workloads (``--workload``):
                        bf16 out; metric = 2*S^3 FLOP per second.  N > 1: B and C
                        split along N; the all-gather of C is fused into the GEMM
                        epilogue (``--gather nccl``: NCCL after it), strong scaling.
-  gemm_fp8             same with E4M3 operands, per-row A / per-column B scales.
+                       ``library_bar``: cuBLAS at the same shape, same run.
+  gemm_fp8             same with E4M3 operands, per-row A / per-column B scales;
+                       the roofline's peak is cuBLASLt's FP8 GEMM timed in the run.
   fa2_fwd              FlashAttention-2 forward, B=4 H=32 S=4096 D=128 causal;
                        N > 1: (batch*head) split, O and lse all-gathered in the epilogue.
   fa2_bwd              the backward of the same configuration (dQ, dK, dV).
   paged_decode         GQA decode over the paged KV cache (B=8, Hq=32, Hkv=8,
                        context U[512, 16384], 16-token pages); replicas at N > 1.
   paged_prefill        the last 512 tokens of each context as a paged prefill.
+  gemm_fp32            AMP's fp32 plugin GEMM, M=N=K=1024, U[-1,1] seed 0, exact
+                       accumulation; e2e through amp_user_gemm_fp32 (pinned and
+                       pageable host buffers); replicas at N > 1.
 
 Timing: W untimed warm-up steps; then K steps, each bracketed by CUDA events on
 the launching stream with an L2 flush before every step (256 MiB written, then
@@ -463,6 +473,110 @@ class GemmFp8Workload(GemmWorkload):
     fp8 = True
 
 
+class GemmFp32Workload:
+    """AMP's fp32 GEMM, the plugin contract's path: C = A B with M = N = K = S
+    (default 1024), A and B ~ U[-1, 1] from seed 0, through the exact form
+    (AMP's CPU accumulation order and rounding; bit-identical to its CPU
+    reference GEMM).  The reference's tile names only label dump entries."""
+    name = "gemm_fp32"
+    metric = "fp32_gemm_TFLOPS"
+    unit = "TFLOP/s"
+    scale = 1e12
+    dtype = "fp32"
+    bound = "fp32"
+    scaling = "weak"
+
+    def __init__(self, dist: Dist, args):
+        import torch
+        from amp_b200 import gemm, workloads as wl
+        self.torch, self.gemm, self.dist, self.args = torch, gemm, dist, args
+        S = self.S = args.fp32_size
+        dev = torch.device("cuda", torch.cuda.current_device())
+        A, B = wl.gemm_fp32_inputs(S, S, S, seed=0)
+        self.A_h, self.B_h = A, B
+        self.A = torch.from_numpy(A).to(dev)
+        self.B = torch.from_numpy(B).to(dev)
+        self.C = torch.empty(S, S, dtype=torch.float32, device=dev)
+        self.cfg = gemm.TileCfg(32, 32, 32)
+
+    def units_per_step(self) -> float:
+        return 2.0 * self.S ** 3
+
+    def launches_per_step(self) -> int:
+        return 1
+
+    @classmethod
+    def describe(cls, args, world: int, rank: int = 0) -> dict:
+        S = args.fp32_size
+        return {"workload": "fp32_gemm", "M": S, "N": S, "K": S,
+                "inputs": "A, B ~ U[-1, 1], seed 0 (row-major fp32)",
+                "accumulation": "exact: fp32 product then fp32 sum, k ascending (AMP's "
+                                "cpu_reference_gemm order; bit-identical to it)",
+                "tiles": "AMP tile configs (16,16,16),(32,16,16),(32,32,16),(32,32,32) name "
+                         "dump entries; one blocking chosen by size",
+                "l2": "L2 flushed before every step",
+                "parallelism": "replicas (too small to shard)" if world > 1 else "single"}
+
+    def config(self):
+        return self.describe(self.args, self.dist.world, self.dist.rank)
+
+    def kernel_table(self):
+        return [("k_gemm_fp32<exact>", self.units_per_step())]
+
+    def step(self, ev=None):
+        if ev: ev[0].record()
+        S = self.S
+        self.gemm.launch_matmul(self.cfg, self.A, self.B, self.C, S, S, S)
+        if ev: ev[1].record()
+
+    def e2e(self, steps: int, warmup: int):
+        """AMP's plugin symbol amp_user_gemm_fp32 on host buffers: pinned, and
+        (e2e_pageable) the plain pageable arrays AMP's validator passes."""
+        torch = self.torch
+        from amp_b200._lib import call
+        S = self.S
+        Ah = torch.from_numpy(self.A_h).pin_memory()
+        Bh = torch.from_numpy(self.B_h).pin_memory()
+        Ch = torch.empty(S, S, dtype=torch.float32).pin_memory()
+        fn = lambda: call("amp_user_gemm_fp32", Ah.data_ptr(), Bh.data_ptr(), Ch.data_ptr(), S,
+                          S, S)
+        ms = _e2e_time(torch, fn, steps, warmup)
+        Cp = np.empty((S, S), np.float32)
+        fnp = lambda: call("amp_user_gemm_fp32", self.A_h.ctypes.data, self.B_h.ctypes.data,
+                           Cp.ctypes.data, S, S, S)
+        ms_p = _e2e_time(torch, fnp, steps, warmup)
+        return {"value": self.units_per_step() / (ms * 1e-3) / self.scale, "unit": self.unit,
+                "ms_per_step": ms, "h2d_bytes_per_step": 2 * 4 * S * S,
+                "d2h_bytes_per_step": 4 * S * S, "api": "amp_user_gemm_fp32 (pinned host buffers)",
+                "pageable": {"value": self.units_per_step() / (ms_p * 1e-3) / self.scale,
+                             "ms_per_step": ms_p,
+                             "api": "amp_user_gemm_fp32 (pageable host arrays, as AMP's "
+                                    "validator passes them)"}}
+
+    @classmethod
+    def cpu_reference(cls, args, budget_s: float, threads: int):
+        """AMP's cpu_reference_gemm at the full size (fp32, rows split over threads)."""
+        import oracle
+        from amp_b200 import workloads as wl
+        S = args.fp32_size
+        A, B = wl.gemm_fp32_inputs(S, S, S, seed=0)
+        Cm = np.empty((S, S), np.float32)
+        g = oracle.ref_gemm_lib()
+        if g is not None:
+            kind, cores = "reference", threads
+            run = lambda: g.ref_cpu_reference_gemm_mt(A.ctypes.data, B.ctypes.data,
+                                                      Cm.ctypes.data, S, S, S, threads)
+            what = "AMP cpu_reference_gemm (tests/amp_validate_kernel.cpp), rows split over threads"
+        else:
+            kind, cores = "port", 1
+            run = lambda: oracle.lib().orc_gemm_fp32_amp(A.ctypes.data, B.ctypes.data,
+                                                         Cm.ctypes.data, S, S, S)
+            what = "oracle restatement of AMP's cpu_reference_gemm"
+        reps, dt = timed_reps(run, budget_s)
+        return {"value": 2.0 * S ** 3 * reps / dt / cls.scale, "unit": cls.unit, "cores": cores,
+                "kind": kind, "sample": f"{reps} x the full {S}^3 GEMM in {dt:.1f} s; {what}"}
+
+
 class AttentionWorkload:
     name = "fa2_fwd"
     fused_gather = True
@@ -842,7 +956,12 @@ class AttentionBwdWorkload(AttentionWorkload):
 
 WORKLOADS = {w.name: w for w in (QuantWorkload, GemmWorkload, GemmFp8Workload,
                                  AttentionWorkload, AttentionBwdWorkload, PagedDecodeWorkload,
-                                 PagedPrefillWorkload)}
+                                 PagedPrefillWorkload, GemmFp32Workload)}
+# The default run: the headline (the FP8 quantiser configuration) and then, in
+# the same process and JSON line, every other workload of the measured configs.
+HEADLINE = "fp8_quant"
+SUITE = ("gemm_bf16", "gemm_fp8", "fa2_fwd", "paged_decode", "paged_prefill", "gemm_fp32",
+         "fa2_bwd")
 
 
 def _e2e_time_stream(torch, fn, steps, warmup):
@@ -878,40 +997,89 @@ def _e2e_time(torch, fn, steps, warmup):
     return sum(times) / len(times)
 
 
-def peak_for(W, peaks):
+def library_bar(W, flush, reps: int = 10):
+    """The vendor library's GEMM on the same square shape, timed here in the
+    same process and clock window (best of `reps`, L2 flushed before each):
+    torch.matmul (cuBLAS) for bf16, torch._scaled_mm with per-tensor scales
+    (cuBLASLt FP8, the call AMP's VendorGemm makes, src/gemm_vendor.cpp:226-230)
+    for E4M3.  A measurement bar only; nothing of it is on the product path."""
+    import torch
+    S = W.S
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    a = torch.randn(S, S, generator=g, device=dev).to(torch.bfloat16)
+    b = torch.randn(S, S, generator=g, device=dev).to(torch.bfloat16)
+    if W.fp8:
+        a8 = a.to(torch.float8_e4m3fn)
+        b8 = b.t().contiguous().to(torch.float8_e4m3fn).t()   # column-major B, as cuBLASLt wants
+        one = torch.ones((), device=dev)
+        fn = lambda: torch._scaled_mm(a8, b8, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        what = "cuBLASLt FP8 E4M3 (torch._scaled_mm, per-tensor scales, bf16 out)"
+    else:
+        fn = lambda: torch.matmul(a, b)
+        what = "cuBLAS bf16 (torch.matmul)"
+    for _ in range(3):
+        fn()
+    best = float("inf")
+    for _ in range(reps):
+        flush()
+        s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        fn()
+        e0.record()
+        e0.synchronize()
+        best = min(best, s0.elapsed_time(e0))
+    return {"kernel": what, "shape": [S, S, S], "value": round(2.0 * S ** 3 / (best * 1e-3) / 1e12, 1),
+            "unit": "TFLOP/s", "timing": f"best of {reps}, L2 flushed before each"}
+
+
+def peak_for(W, peaks, live=None):
+    """(peak, unit, source) for the roofline of workload W."""
+    live = live or {}
     if W.bound == "hbm":
-        return peaks["hbm_gbs"], "GB/s", "hbm_gbs"
+        return peaks["hbm_gbs"], "GB/s", "MEASURED_PEAKS.json hbm_gbs"
+    if W.bound == "fp32":
+        return (live["fp32_nominal"], "TFLOP/s",
+                "nominal FP32 FFMA rate (SMs x 128 lanes x 2 FLOP x max SM clock); no measured "
+                "figure exists for the FP32 pipe; the exact form issues FMUL + FADD, so its own "
+                "ceiling is half of this")
     bf16 = peaks["bf16_tflops"]
     if getattr(W, "fp8", False):
-        return 2 * bf16, "TFLOP/s", "2 x bf16_tflops (dense FP8 = 2x bf16 rate)"
-    return bf16, "TFLOP/s", "bf16_tflops (burst)"
+        if live.get("fp8_library"):
+            return (live["fp8_library"], "TFLOP/s",
+                    "measured here: cuBLASLt FP8 E4M3 GEMM at the same shape, same run "
+                    "(library_bar)")
+        return 2 * bf16, "TFLOP/s", "2 x MEASURED_PEAKS.json bf16_tflops (dense FP8 = 2x bf16)"
+    return bf16, "TFLOP/s", "MEASURED_PEAKS.json bf16_tflops (burst)"
 
 
-def run_amp(args, dist: Dist):
+def make_flush():
+    """L2 flush between steps (outside the timed events): write 256 MiB, then
+    read a second 256 MiB buffer so that the flush's own dirty lines are
+    written back before the step starts instead of during it."""
     import torch
-    import amp_b200
-    from amp_b200 import build as ampbuild
-    if not amp_b200.LIB_PATH.exists():
-        ampbuild.build()
-    torch.cuda.set_device(dist.local_rank)
-    W = WORKLOADS[args.workload](dist, args)
-    # L2 flush between steps (outside the timed events): write 256 MiB, then
-    # read a second 256 MiB buffer so that the flush's own dirty lines are
-    # written back before the step starts instead of during it.
     flush_w = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     flush_r = torch.ones(256 << 20, dtype=torch.uint8, device="cuda")
 
     def flush():
         flush_w.zero_()
         flush_r.sum(dtype=torch.int64)
+    return flush
 
-    for _ in range(args.warmup):
+
+def measure(W, args, dist: Dist, flush, steps: int, warmup: int, cpu_budget_s: float) -> dict:
+    """One workload's full record: device-timed value, per-kernel roofline,
+    clocks during the timed region, e2e through the host-pointer API and (rank
+    0 at N = 1) the CPU baseline."""
+    import torch
+    for _ in range(warmup):
         flush()
         W.step()
     nk = len(W.kernel_table())
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] for _ in range(args.steps)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] for _ in range(steps)]
     sev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
+           for _ in range(steps)]
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
@@ -919,7 +1087,7 @@ def run_amp(args, dist: Dist):
     dev_index = torch.cuda.current_device()
     nvml_index = int(phys.split(",")[dev_index]) if phys else dev_index
     with ClockSampler(nvml_index) as clocks:
-        for i in range(args.steps):
+        for i in range(steps):
             flush()
             sev[i][0].record()
             W.step(ev[i])
@@ -929,54 +1097,103 @@ def run_amp(args, dist: Dist):
     torch.cuda.synchronize()
     from amp_b200._lib import lib
     if lib().amp_device_status(1) != 0:
-        raise SystemExit("a kernel reported a device-side timeout during the timed region")
+        raise SystemExit(f"{W.name}: a kernel reported a device-side timeout in the timed region")
     total_ms = dist.max(sum(a.elapsed_time(b) for a, b in sev))
-    ms_per_step = total_ms / args.steps
+    ms_per_step = total_ms / steps
     value = W.units_per_step() * dist.world / (ms_per_step * 1e-3) / W.scale
 
     spans = []
     for k, (kname, units) in enumerate(W.kernel_table()):
-        ms = statistics.mean(ev[i][k].elapsed_time(ev[i][k + 1]) for i in range(args.steps))
+        ms = statistics.mean(ev[i][k].elapsed_time(ev[i][k + 1]) for i in range(steps))
         spans.append((ms, kname, units))
     spans.sort(reverse=True)
     dom_ms, dom_name, dom_units = spans[0]
+    csum = clocks.summary()
+    live = {}
+    bar = None
+    if isinstance(W, GemmWorkload):
+        bar = library_bar(W, flush)
+        if W.fp8:
+            live["fp8_library"] = bar["value"]
+    if W.bound == "fp32":
+        sms = torch.cuda.get_device_properties(dev_index).multi_processor_count
+        live["fp32_nominal"] = sms * 128 * 2 * (csum["sm_max_mhz"] or 1965) * 1e6 / 1e12
     peaks, peak_src = load_peaks()
-    peak, punit, pkey = peak_for(W, peaks)
+    peak, punit, pkey = peak_for(W, peaks, live)
     achieved = dom_units / (dom_ms * 1e-3) / W.scale
     roofline = {"bound": W.bound, "kernel": dom_name, "achieved": round(achieved, 2),
                 "peak": round(peak, 1), "unit": punit, "frac": round(achieved / peak, 4),
-                "peak_source": f"{peak_src}: MEASURED_PEAKS.json {pkey}" if peak_src == "measured"
+                "peak_source": pkey if peak_src == "measured" or "MEASURED" not in pkey
                 else "fallback figure of the profiling recipe",
                 "traffic": traffic_for(W, dist.world, dom_name),
                 "algorithmic_units_per_launch": dom_units, "kernel_ms": round(dom_ms, 5),
                 "all_kernels": [{"kernel": n, "ms": round(m, 5),
                                  "rate": round(u / (m * 1e-3) / W.scale, 2)}
                                 for m, n, u in spans]}
+    if getattr(W, "fp8", False) and live.get("fp8_library"):
+        roofline["frac_of_2x_bf16_peak"] = round(achieved / (2 * peaks["bf16_tflops"]), 4)
     e2e = None
     if not args.skip_e2e:
-        e2e = W.e2e(max(3, min(args.steps, 10)), 2)
+        e2e = W.e2e(max(3, min(steps, 10)), 2)
         e2e["ms_per_step"] = dist.max(e2e["ms_per_step"])  # every rank runs it on its shard
         e2e["value"] = W.units_per_step() * dist.world / (e2e["ms_per_step"] * 1e-3) / W.scale
     out = {
         "metric": W.metric, "value": round(value, 3), "unit": W.unit, "n_gpus": dist.world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+        "steps": steps, "warmup": warmup, "ms_per_step": round(ms_per_step, 5),
         "higher_is_better": True, "scaling": W.scaling, "vs_baseline": None,
         "dtype": W.dtype, "data": "synthetic (seeded)", "config": W.config(),
-        "impl": "amp_b200", "gpu_launches": W.launches_per_step() * args.steps,
-        "clocks": clocks.summary(), "roofline": roofline,
-        "e2e": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in e2e.items()}
-        if e2e else None,
+        "impl": "amp_b200", "gpu_launches": W.launches_per_step() * steps,
+        "clocks": csum, "roofline": roofline,
+        "e2e": _round(e2e) if e2e else None,
     }
+    if bar is not None:
+        bar["ratio"] = round(achieved / bar["value"], 4)   # this kernel over the library's
+        out["library_bar"] = bar
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = W.cpu_reference(args, budget_s=10.0, threads=host_threads())
-    if hasattr(W, "close"):
-        W.close()   # collective: every rank releases its peer resources here
+        out["cpu_baseline"] = W.cpu_reference(args, budget_s=cpu_budget_s,
+                                              threads=host_threads())
+    return out
+
+
+def _round(d):
+    return {k: (round(v, 4) if isinstance(v, float) else _round(v) if isinstance(v, dict) else v)
+            for k, v in d.items()}
+
+
+def run_one(name, args, dist: Dist, flush, steps, warmup, cpu_budget_s):
+    import torch
+    W = WORKLOADS[name](dist, args)
+    try:
+        return measure(W, args, dist, flush, steps, warmup, cpu_budget_s)
+    finally:
+        if hasattr(W, "close"):
+            W.close()   # collective: every rank releases its peer resources here
+        del W
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+
+
+def run_amp(args, dist: Dist):
+    import torch
+    import amp_b200
+    from amp_b200 import build as ampbuild
+    if not amp_b200.LIB_PATH.exists():
+        ampbuild.build()
+    torch.cuda.set_device(dist.local_rank)
+    flush = make_flush()
+    if args.workload != "suite":
+        return run_one(args.workload, args, dist, flush, args.steps, args.warmup, 10.0)
+    out = run_one(HEADLINE, args, dist, flush, args.steps, args.warmup, 10.0)
+    # the other workloads at the same warm-up and (capped) step count
+    steps = min(args.steps, args.suite_steps)
+    out["workloads"] = [run_one(n, args, dist, flush, steps, args.warmup, 4.0) for n in SUITE]
     return out
 
 
 def run_reference(args):
-    """The reference's own CPU code for the workload, on this host (rank 0 only)."""
-    W = WORKLOADS[args.workload]
+    """The reference's own CPU code for the workload (the headline's for the
+    suite), on this host (rank 0 only)."""
+    W = WORKLOADS[HEADLINE if args.workload == "suite" else args.workload]
     threads = host_threads()
     # each step is one bounded sample of the workload (about a second of CPU work)
     for _ in range(args.warmup):
@@ -1003,10 +1220,15 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="fp8_quant")
+    ap.add_argument("--workload", choices=["suite"] + sorted(WORKLOADS), default="suite",
+                    help="suite (default): the headline fp8_quant line with every other "
+                         "workload in its 'workloads' array; or one workload alone")
     ap.add_argument("--impl", choices=["amp_b200", "reference"], default="amp_b200")
     ap.add_argument("--elements", type=int, default=1 << 26)
     ap.add_argument("--size", type=int, default=8192)
+    ap.add_argument("--fp32-size", type=int, default=1024)
+    ap.add_argument("--suite-steps", type=int, default=200,
+                    help="cap on the timed steps of the suite's non-headline workloads")
     ap.add_argument("--batch", type=int, default=4)
     ap.add_argument("--heads", type=int, default=32)
     ap.add_argument("--seq", type=int, default=4096)
@@ -1023,7 +1245,7 @@ def main():
         args.steps = args.steps or 5
         args.warmup = args.warmup if args.warmup is not None else 3
     else:
-        heavy = args.workload != "fp8_quant"
+        heavy = args.workload not in ("fp8_quant", "suite")
         args.steps = args.steps or (200 if heavy else 2000)
         args.warmup = args.warmup if args.warmup is not None else (10 if heavy else 20)
     if args.warmup < 3:

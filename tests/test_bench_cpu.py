@@ -96,3 +96,30 @@ def test_traffic_is_reported_only_for_the_captured_launch():
     assert bench.traffic_for(bench.GemmWorkload, 1, g) == t["gemm_bf16"][g]
     assert bench.traffic_for(bench.GemmWorkload, 2, g) is None                 # strong scaling
     assert bench.traffic_for(bench.AttentionWorkload, 4, "k_flash_fwd<128>") is None
+
+
+def test_default_run_is_the_suite_over_every_workload():
+    args = bench.build_parser().parse_args([])
+    assert args.workload == "suite"
+    assert bench.HEADLINE == "fp8_quant" and bench.HEADLINE not in bench.SUITE
+    assert set(bench.SUITE) | {bench.HEADLINE} == set(bench.WORKLOADS)
+
+
+def test_roofline_peaks_name_their_source():
+    peaks = {"hbm_gbs": 6550.1, "bf16_tflops": 1662.9}
+    p, u, src = bench.peak_for(bench.QuantWorkload, peaks)
+    assert (p, u) == (6550.1, "GB/s") and "hbm_gbs" in src
+    p, u, src = bench.peak_for(bench.GemmWorkload, peaks)
+    assert p == 1662.9 and "bf16_tflops" in src
+    p, u, src = bench.peak_for(bench.GemmFp8Workload, peaks, {"fp8_library": 3069.0})
+    assert p == 3069.0 and "cuBLASLt" in src
+    p, u, src = bench.peak_for(bench.GemmFp8Workload, peaks)
+    assert p == 2 * 1662.9
+    p, u, src = bench.peak_for(bench.GemmFp32Workload, peaks, {"fp32_nominal": 74.4})
+    assert p == 74.4 and "nominal" in src
+
+
+def test_fp32_gemm_units():
+    G = object.__new__(bench.GemmFp32Workload)
+    G.S = 1024
+    assert G.units_per_step() == 2.0 * 1024 ** 3
