@@ -457,7 +457,6 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
 // bounded wait with cluster-scope acquire (arrivals come from the other CTA too)
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* status) {
     const uint64_t t0 = globaltimer_ns();
-    const uint64_t limit = wait_limit_ns(status);
     uint32_t n = 0;
     while (true) {
         uint32_t ok;
@@ -469,7 +468,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
             : "memory");
         if (ok) return true;
         if ((++n & 1023u) == 0) {
-            if (globaltimer_ns() - t0 > limit) {
+            if (wait_expired(globaltimer_ns() - t0, status)) {
                 atomicExch(status, AMP_DEV_ERR_TIMEOUT);
                 return false;
             }

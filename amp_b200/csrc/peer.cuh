@@ -22,7 +22,6 @@ __device__ __forceinline__ bool mailbox_exchange(unsigned long long* const* mbox
         asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(word) : "memory");
     }
     bool ok = true;
-    const uint64_t limit = wait_limit_ns(status);
     for (int p = lane; p < world; p += 32) {
         const unsigned long long* src = mbox[rank] + row + p;
         const uint64_t t0 = globaltimer_ns();
@@ -30,7 +29,7 @@ __device__ __forceinline__ bool mailbox_exchange(unsigned long long* const* mbox
         while (true) {
             asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(src) : "memory");
             if ((unsigned)(v >> 32) == seq) break;
-            if (globaltimer_ns() - t0 > limit) {
+            if (wait_expired(globaltimer_ns() - t0, status)) {
                 atomicExch(status, AMP_DEV_ERR_TIMEOUT);
                 ok = false;
                 break;

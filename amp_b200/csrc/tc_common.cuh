@@ -20,11 +20,18 @@ enum : int { AMP_DEV_OK = 0, AMP_DEV_ERR_TIMEOUT = 1, AMP_DEV_ERR_BAD_PAGE = 2 }
 
 // The per-device status block (runtime.cu) is 16 bytes: the status word at
 // int [0] and the wait limit in ns as a u64 at byte 8.  Kernels receive the
-// status word's address, so the limit needs no argument of its own; it is
-// read only once a wait has failed its first try.
+// status word's address, so the limit needs no argument of its own.  It is
+// read only once a wait has lasted kLimitFloorNs: a global load on every wait
+// would put its latency on the pipelines' hand-offs (it cost the GEMM ~20%),
+// so limits below the floor act as the floor.
 constexpr int kStatusLimitOffsetInts = 2;
+constexpr uint64_t kLimitFloorNs = 1000000ull;  // 1 ms
 __device__ __forceinline__ uint64_t wait_limit_ns(const int* status) {
     return *reinterpret_cast<const volatile unsigned long long*>(status + kStatusLimitOffsetInts);
+}
+// true once `elapsed` ns of waiting exceed the device's wait limit
+__device__ __forceinline__ bool wait_expired(uint64_t elapsed, const int* status) {
+    return elapsed > kLimitFloorNs && elapsed > wait_limit_ns(status);
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -98,14 +105,13 @@ template <bool kSleep = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
     if (mbar_try_wait<kSleep>(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    const uint64_t limit = wait_limit_ns(status);
     uint32_t n = 0;
     // a sleeping try_wait may take up to the hint, so the clock is read every time
     constexpr uint32_t kCheckMask = kSleep ? 0u : 1023u;
     while (true) {
         if (mbar_try_wait<kSleep>(bar, parity)) return true;
         if ((++n & kCheckMask) == 0) {
-            if (globaltimer_ns() - t0 > limit) {
+            if (wait_expired(globaltimer_ns() - t0, status)) {
                 atomicExch(status, AMP_DEV_ERR_TIMEOUT);
                 return false;
             }

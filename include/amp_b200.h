@@ -61,8 +61,9 @@ AMP_API int amp_abi_version(void);
 AMP_API int amp_device_status(int clear);
 /* Sets the current device's limit on every bounded device-side wait (mbarrier
  * waits of the pipelined kernels, peer-mailbox polls); 0 restores the default
- * of 2 s.  Takes effect for kernels launched after it returns (it synchronises
- * the device first).  The reference has no device-side waits; this is the
+ * of 2 s; limits below 1 ms act as 1 ms (kernels read the limit only after
+ * a wait has lasted that long).  Takes effect for kernels launched after it
+ * returns (it synchronises the device first).  The reference has no device-side waits; this is the
  * failure path's knob, e.g. a short limit in a test whose peer never posts. */
 AMP_API int amp_set_wait_timeout_ns(uint64_t ns);
 
