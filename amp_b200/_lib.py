@@ -31,6 +31,7 @@ SIGNATURES: dict[str, tuple] = {
     "amp_user_fp8_dequant_e4m3": (_i32, [_vp, _i64, _f32, _vp]),
     "amp_device_status": (_i32, [_i32]),
     "amp_set_wait_timeout_ns": (_i32, [C.c_uint64]),
+    "amp_release_staging": (_i32, []),
     "amp_gemm_bf16_dev": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp]),
     "amp_gemm_fp8e4m3_dev": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _vp]),
     "amp_gemm_fp8e4m3_ex_dev": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _vp, _i32, _i32,

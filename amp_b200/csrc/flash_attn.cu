@@ -735,5 +735,7 @@ extern "C" int amp_user_flash_attn_fwd_bf16(const uint16_t* Q, const uint16_t* K
     AMPB_CHECK_CUDA(cudaMemcpyAsync(O, dout, q, cudaMemcpyDeviceToHost, st));
     if (lse) AMPB_CHECK_CUDA(cudaMemcpyAsync(lse, dl, l, cudaMemcpyDeviceToHost, st));
     AMPB_CHECK_CUDA(cudaStreamSynchronize(st));
-    return amp_device_status(1);
+    const int status = amp_device_status(1);
+    if (status) return status;
+    return staging_end_of_call();
 }

@@ -381,7 +381,7 @@ int amp_user_fp8_quant_e4m3(const uint16_t* x, int64_t n, uint8_t* q, float* sca
     if (y && n) AMPB_CHECK_CUDA(cudaMemcpyAsync(y, dy, (size_t)n * 2, cudaMemcpyDeviceToHost, st));
     AMPB_CHECK_CUDA(cudaMemcpyAsync(scale_out, dscale, sizeof(float), cudaMemcpyDeviceToHost, st));
     AMPB_CHECK_CUDA(cudaStreamSynchronize(st));
-    return AMP_OK;
+    return staging_end_of_call();
 }
 
 int amp_user_fp8_dequant_e4m3(const uint8_t* q, int64_t n, float scale, uint16_t* y) {
@@ -401,7 +401,7 @@ int amp_user_fp8_dequant_e4m3(const uint8_t* q, int64_t n, float scale, uint16_t
         return rc;
     AMPB_CHECK_CUDA(cudaMemcpyAsync(y, dy, (size_t)n * 2, cudaMemcpyDeviceToHost, st));
     AMPB_CHECK_CUDA(cudaStreamSynchronize(st));
-    return AMP_OK;
+    return staging_end_of_call();
 }
 
 }  // extern "C"

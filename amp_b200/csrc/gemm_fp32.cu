@@ -286,7 +286,7 @@ int amp_user_gemm_fp32(const float* hA, const float* hB, float* hC, int M, int N
         return rc;
     AMPB_CHECK_CUDA(cudaMemcpyAsync(hC, dC, c, cudaMemcpyDeviceToHost, st));
     AMPB_CHECK_CUDA(cudaStreamSynchronize(st));
-    return AMP_OK;
+    return staging_end_of_call();
 }
 
 }  // extern "C"

@@ -1262,7 +1262,9 @@ int amp_user_gemm_bf16(const uint16_t* A, const uint16_t* B, void* C, int c_dtyp
     if ((rc = gemm_bf16_dev(dA, dB, dC, c_dtype == AMP_DTYPE_BF16, M, N, K, st))) return rc;
     AMPB_CHECK_CUDA(cudaMemcpyAsync(C, dC, c, cudaMemcpyDeviceToHost, st));
     AMPB_CHECK_CUDA(cudaStreamSynchronize(st));
-    return amp_device_status(1);
+    const int status = amp_device_status(1);
+    if (status) return status;
+    return staging_end_of_call();
 }
 
 int amp_user_gemm_fp8e4m3(const uint8_t* A, const uint8_t* B, const float* scale_a,
@@ -1292,7 +1294,9 @@ int amp_user_gemm_fp8e4m3(const uint8_t* A, const uint8_t* B, const float* scale
         return rc;
     AMPB_CHECK_CUDA(cudaMemcpyAsync(C, dC, c, cudaMemcpyDeviceToHost, st));
     AMPB_CHECK_CUDA(cudaStreamSynchronize(st));
-    return amp_device_status(1);
+    const int status = amp_device_status(1);
+    if (status) return status;
+    return staging_end_of_call();
 }
 
 }  // extern "C"

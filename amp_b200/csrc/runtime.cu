@@ -2,6 +2,7 @@
 // pool shared by the amp_user_* entry points.
 #include <cstdarg>
 #include <cstddef>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -90,6 +91,30 @@ std::mutex g_pool_mu;
 std::vector<std::vector<Slot>> g_pool;  // [device][slot]
 }  // namespace
 
+int staging_release_current_device() {
+    int dev = 0;
+    AMPB_CHECK_CUDA(cudaGetDevice(&dev));
+    AMPB_CHECK_CUDA(cudaDeviceSynchronize());  // nothing queued may still use a buffer
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    if ((int)g_pool.size() <= dev) return AMP_OK;
+    for (Slot& s : g_pool[dev]) {
+        if (s.ptr) AMPB_CHECK_CUDA(cudaFree(s.ptr));
+        s.ptr = nullptr;
+        s.bytes = 0;
+    }
+    return AMP_OK;
+}
+
+int staging_end_of_call() {
+    // AMP_B200_RELEASE_STAGING=1: every amp_user_* call returns its device
+    // buffers before it returns, as include/amp_plugin.h:32-39 words the contract
+    static const bool release = [] {
+        const char* e = std::getenv("AMP_B200_RELEASE_STAGING");
+        return e && *e && std::strcmp(e, "0") != 0;
+    }();
+    return release ? staging_release_current_device() : AMP_OK;
+}
+
 int staging_get(int slot, size_t bytes, void** out) {
     int dev = 0;
     AMPB_CHECK_CUDA(cudaGetDevice(&dev));
@@ -175,6 +200,8 @@ int amp_set_wait_timeout_ns(uint64_t ns) {
                                cudaMemcpyHostToDevice));
     return AMP_OK;
 }
+
+int amp_release_staging(void) { return ampb::staging_release_current_device(); }
 
 const char* amp_last_error(void) { return ampb::g_msg; }
 

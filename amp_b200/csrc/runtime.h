@@ -11,6 +11,11 @@ namespace ampb {
 // current device (grow-only, kept until process exit).  Slots let one call
 // hold several live buffers.  Not re-entrant across threads for one slot.
 int staging_get(int slot, size_t bytes, void** out);
+// Frees every staging buffer of the current device (after synchronising it).
+int staging_release_current_device();
+// Called by each amp_user_* entry point on success just before it returns:
+// releases the staging buffers when AMP_B200_RELEASE_STAGING is set.
+int staging_end_of_call();
 
 // Per-device status word written by kernels whose bounded waits expired
 // (AMP_DEV_ERR_TIMEOUT); allocated and zeroed on first use.

@@ -59,6 +59,14 @@ AMP_API int amp_abi_version(void);
  * failure path of the pipelined tensor-core kernels, which end instead of
  * hanging.  clear != 0 resets the flag. */
 AMP_API int amp_device_status(int clear);
+/* The amp_user_* entry points stage their host data in per-device device
+ * buffers that grow as needed and are kept across calls, so repeated calls do
+ * not pay cudaMalloc / cudaFree.  AMP's plugin contract says a plugin frees its
+ * device buffers before returning (include/amp_plugin.h:32-39): this call
+ * frees them on the current device (after synchronising it), and with the
+ * environment variable AMP_B200_RELEASE_STAGING=1 every amp_user_* call does so
+ * itself before it returns. */
+AMP_API int amp_release_staging(void);
 /* Sets the current device's limit on every bounded device-side wait (mbarrier
  * waits of the pipelined kernels, peer-mailbox polls); 0 restores the default
  * of 2 s; limits below 1 ms act as 1 ms (kernels read the limit only after

@@ -155,3 +155,30 @@ def test_3xtf32_rejects_shapes_tma_cannot_load(cuda, amp_lib):
     B = torch.zeros(6, 8, device="cuda")
     with pytest.raises(AmpError):
         gemm.matmul_fp32_3xtf32(A, B)
+
+
+def test_staging_buffers_are_released_on_request(cuda, amp_lib):
+    """The host-pointer entry points keep grow-only staging buffers; AMP's plugin
+    contract frees device buffers before returning, which amp_release_staging
+    (or AMP_B200_RELEASE_STAGING=1, below) provides."""
+    S = 2048
+    A, B = workloads.gemm_fp32_inputs(S, S, S, seed=1)
+    C = np.zeros((S, S), np.float32)
+    call("amp_user_gemm_fp32", A.ctypes.data, B.ctypes.data, C.ctypes.data, S, S, S)
+    free_before, _ = torch.cuda.mem_get_info(cuda)
+    call("amp_release_staging")
+    free_after, _ = torch.cuda.mem_get_info(cuda)
+    assert free_after - free_before >= 3 * S * S * 4 - (4 << 20), (free_before, free_after)
+    call("amp_user_gemm_fp32", A.ctypes.data, B.ctypes.data, C.ctypes.data, S, S, S)
+    assert np.array_equal(C, oracle.gemm_fp32_amp(A, B))
+
+
+@pytest.mark.skipif(not oracle.REF_VALIDATOR.exists(), reason="oracle/_ref not built")
+def test_amp_validate_kernel_with_per_call_release(tmp_path, cuda, amp_lib):
+    import os
+    out = tmp_path / "dump.json"
+    p = subprocess.run([str(oracle.REF_VALIDATOR), str(LIB_PATH), str(out), "512", "512", "512"],
+                       capture_output=True, text=True, timeout=600,
+                       env={**os.environ, "AMP_B200_RELEASE_STAGING": "1"})
+    assert p.returncode == 0 and "PASS" in p.stdout, p.stdout + p.stderr
+    assert json.loads(out.read_text())["tiles"][0]["max_rel_err_vs_cpu"] == 0
