@@ -1,8 +1,9 @@
 """The C++ stubs in INTEGRATION.md compile against include/amp_b200.h (and the
-scheduler stub against AMP's own include/scheduler.hpp where the AMP sources are
-present, AMP_REF).  Definitions compile at file scope; statement fragments
-compile inside a function, with their free variables declared at the types the
-entry points take, so a stub that passes a wrong type fails here."""
+scheduler and collective stubs against AMP's own include/scheduler.hpp and
+include/collective.hpp where the AMP sources are present, AMP_REF).
+Definitions compile at file scope; statement fragments compile inside a
+function, with their free variables declared at the types the entry points
+take, so a stub that passes a wrong type fails here."""
 import os
 import re
 import subprocess
@@ -24,7 +25,9 @@ PRELUDE = r"""
 #include <cuda_bf16.h>
 #include "amp_b200.h"
 %(sched)s
-int world, rank, M, N, K, S, bh_per_rank, max_pages, max_pages_total, max_ctx, Hq, Hkv, D;
+int world, rank, M, N, K, S, bh_per_rank, max_pages, max_pages_total, max_ctx, Hq, Hkv, D, Np;
+amp_comm* comm;
+void* dC;
 int64_t n;
 size_t ws_bytes;
 cudaStream_t s;
@@ -49,7 +52,7 @@ def compiles(code: str, tmp: Path, sched: bool) -> subprocess.CompletedProcess:
     src.write_text(code)
     inc = ["-I", str(ROOT / "include"), "-I", str(CUDA_INC)]
     if sched:
-        inc += ["-I", str(AMP_REF / "include")]
+        inc += ["-I", str(AMP_REF / "include"), "-DAMP_BACKEND_CUDA"]
     return subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-Wall", *inc, str(src)],
                           capture_output=True, text=True)
 
@@ -62,10 +65,13 @@ def test_there_are_stubs_to_check():
 def test_integration_stub_compiles(i, tmp_path):
     block = BLOCKS[i]
     sched = "AMP::" in block and "Batch" in block
-    if sched and not (AMP_REF / "include" / "scheduler.hpp").exists():
-        pytest.skip("AMP's scheduler.hpp not present")
-    prelude = PRELUDE % {"sched": '#include "scheduler.hpp"' if sched else "",
+    coll = "CommGroup" in block
+    header = "scheduler.hpp" if sched else "collective.hpp" if coll else None
+    if header and not (AMP_REF / "include" / header).exists():
+        pytest.skip(f"AMP's {header} not present")
+    prelude = PRELUDE % {"sched": f'#include "{header}"' if header else "",
                          "batch": "AMP::ScheduledBatch batch;" if sched else ""}
+    sched = bool(header)
     at_file_scope = compiles(prelude + block, tmp_path, sched)
     if at_file_scope.returncode == 0:
         return
