@@ -66,6 +66,15 @@ __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
     return v;
 }
 
+// Streaming 64-bit global load, no L1 allocation.
+__device__ __forceinline__ uint2 ldg_stream_v2(const void* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+                 : "=r"(v.x), "=r"(v.y)
+                 : "l"(p));
+    return v;
+}
+
 __device__ __forceinline__ void stg_v4(void* p, uint4 v) {
     asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
                  "r"(v.w)

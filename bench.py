@@ -287,7 +287,7 @@ class QuantWorkload:
         args = (xh.data_ptr(), n, qh.data_ptr(), C.byref(sc), yh.data_ptr())
         ms = _e2e_time(torch, lambda: call("amp_user_fp8_quant_e4m3", *args), steps, warmup)
         # the same call on pageable host arrays (what a plain C++ caller hands over)
-        xp = xh.numpy().copy()
+        xp = xh.view(torch.int16).numpy().copy()
         qp = np.empty(n, np.uint8)
         yp = np.empty(n, np.uint16)
         argsp = (xp.ctypes.data, n, qp.ctypes.data, C.byref(sc), yp.ctypes.data)
