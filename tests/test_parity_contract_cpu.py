@@ -102,3 +102,31 @@ def test_b200_dump_passes_amp_parity_check_against_the_oracle(tmp_path, harness_
     r = parity(B200_DUMP, tmp_path / "oracle.json")
     assert r.returncode == 0, r.stdout + r.stderr
     assert "FAIL" not in r.stdout
+
+
+EXT_DUMPS = {"bf16": ("b200_parity_dump_bf16_96.json", (96, 96, 96)),
+             "fp8": ("b200_parity_dump_fp8_96.json", (96, 96, 96)),
+             "quant": ("b200_parity_dump_quant_4096.json", (4096, 1, 1))}
+
+
+@pytest.mark.parametrize("op", sorted(EXT_DUMPS))
+def test_b200_extension_dumps_are_the_tools_layout(op, tmp_path):
+    import json
+    path = B200_DUMP.parent / EXT_DUMPS[op][0]
+    d = json.loads(path.read_text())
+    write_dump(tmp_path / "again.json", d["vendor"], d["M"], d["N"], d["K"], d["seed"], _tiles(d))
+    assert (tmp_path / "again.json").read_text() == path.read_text()
+
+
+@needs_amp
+@pytest.mark.parametrize("op", sorted(EXT_DUMPS))
+def test_b200_extension_dumps_pass_amp_parity_check_against_the_oracle(op, tmp_path, oracle_lib):
+    """The bf16 / FP8 GEMM and quantiser dumps the tool wrote on a B200
+    (golden/make_b200_dump.sh) against the oracle's dumps of the same op, through
+    AMP's parity_check.py unchanged."""
+    from oracle.parity_dump import write_op_dump
+    name, (M, N, K) = EXT_DUMPS[op]
+    write_op_dump(tmp_path / "oracle.json", op, M, N, K)
+    r = parity(B200_DUMP.parent / name, tmp_path / "oracle.json")
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "FAIL" not in r.stdout
