@@ -10,8 +10,11 @@
 // double-buffered shared memory, and the next k-tile is fetched from global
 // memory into registers while the current one is multiplied.
 //
-// Two accumulation modes, both in k order within a thread:
-//   * fast  (amp_gemm_fp32_dev): fp32 FFMA, one rounding per multiply-add;
+// Two accumulation modes, both in k order within a thread, on pairs of
+// adjacent output columns:
+//   * fast  (amp_gemm_fp32_dev): fp32 FFMA, one rounding per multiply-add, as
+//     packed fma.rn.f32x2 (two lanes' worth of work per issue slot, which is
+//     what bounds this kernel);
 //   * exact (amp_gemm_fp32_exact_dev, the plugin amp_user_gemm_fp32 and the
 //     tile-config launcher behind the parity dump): the product rounded to
 //     fp32, then the sum rounded to fp32, k ascending from 0 -- the order and
@@ -55,6 +58,33 @@ __device__ __forceinline__ void load_halves(const float* p, float* dst) {
             dst[H + i] = v1.x; dst[H + i + 1] = v1.y;
         }
     }
+}
+
+// Packed fp32 pairs (sm_100: one instruction for two lanes).  The exact form
+// uses mul.rn / add.rn, which are never contracted into an FMA.
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpk2(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_rn2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+// Exact step on a pair: each product rounded, then each sum, as scalar
+// mul.rn / add.rn (never contracted).  A packed mul.rn.f32x2 + add.rn.f32x2
+// pair was measured not to reproduce the separately rounded result, so the
+// exact form stays on scalar instructions.
+__device__ __forceinline__ uint64_t mul_add_rn2(uint64_t acc, uint64_t a, uint64_t b) {
+    float c0, c1, a0, a1, b0, b1;
+    unpk2(acc, c0, c1);
+    unpk2(a, a0, a1);
+    unpk2(b, b0, b1);
+    return pk2(__fadd_rn(c0, __fmul_rn(a0, b0)), __fadd_rn(c1, __fmul_rn(a1, b1)));
 }
 
 template <int BM, int BN, int BK, int TM, int TN>
@@ -143,11 +173,13 @@ __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN>::kThreads)
         }
     };
 
-    float acc[TM][TN];
+    // accumulators as packed pairs of adjacent columns: acc2[i][jp] = (C[i][2jp], C[i][2jp+1])
+    static_assert(TN % 2 == 0, "column pairs");
+    uint64_t acc2[TM][TN / 2];
 #pragma unroll
     for (int i = 0; i < TM; ++i)
 #pragma unroll
-        for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+        for (int j = 0; j < TN / 2; ++j) acc2[i][j] = 0ull;
 
     const int ktiles = (K + BK - 1) / BK;
     if (ktiles > 0) {
@@ -165,20 +197,30 @@ __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN>::kThreads)
             float a[TM], b[TN];
             load_halves<HM, BM / 2>(&As[buf][k][ty * HM], a);
             load_halves<HN, BN / 2>(&Bs[buf][k][tx * HN], b);
+            uint64_t b2[TN / 2];
 #pragma unroll
-            for (int i = 0; i < TM; ++i)
+            for (int j = 0; j < TN / 2; ++j) b2[j] = pk2(b[2 * j], b[2 * j + 1]);
 #pragma unroll
-                for (int j = 0; j < TN; ++j) {
+            for (int i = 0; i < TM; ++i) {
+                const uint64_t a2 = pk2(a[i], a[i]);
+#pragma unroll
+                for (int j = 0; j < TN / 2; ++j) {
                     if constexpr (kExact)
-                        acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], b[j]));
+                        acc2[i][j] = mul_add_rn2(acc2[i][j], a2, b2[j]);
                     else
-                        acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+                        acc2[i][j] = fma_rn2(a2, b2[j], acc2[i][j]);
                 }
+            }
         }
         if (kt + 1 < ktiles) store_tile(buf ^ 1);
         __syncthreads();
     }
 
+    float acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN / 2; ++j) unpk2(acc2[i][j], acc[i][2 * j], acc[i][2 * j + 1]);
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
         const int r = m0 + (i < HM ? ty * HM + i : BM / 2 + ty * HM + (i - HM));

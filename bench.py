@@ -34,7 +34,7 @@ Workloads (``--workload``):
 
 Timing: W untimed warm-up steps; then K steps, each bracketed by CUDA events on
 the launching stream with an L2 flush before every step (256 MiB written, then
-256 MiB read, outside the events); barrier + synchronize on both sides; the max over ranks.  NVML samples
+1 GiB read, outside the events); barrier + synchronize on both sides; the max over ranks.  NVML samples
 SM clocks and throttle reasons during the timed region.  ``e2e`` repeats the
 metric through the host-pointer C entry point (pinned host buffers, H2D +
 kernels + D2H inside the timed region).  ``roofline`` reports the dominant
@@ -248,7 +248,7 @@ class QuantWorkload:
         return {"workload": "fp8_e4m3_per_tensor_quant_dequant", "elements_per_gpu": n,
                 "global_elements": n * world,
                 "input": "bf16 N(0,1) + 0.1% N(0,50) outliers (seeded, synthetic)",
-                "scale": "amax/448, RNE satfinite", "l2": "L2 flushed before every step (256 MiB written, then 256 MiB read)",
+                "scale": "amax/448, RNE satfinite", "l2": "L2 flushed before every step (256 MiB written, then 1 GiB read)",
                 "parallelism": f"shard{world}+all-reduce(max) of 1 float through peer "
                                "mailboxes (NVLink stores, no NCCL)"
                 if world > 1 else "single"}
@@ -1066,15 +1066,18 @@ def peak_for(W, peaks, live=None):
 
 def make_flush():
     """L2 flush between steps (outside the timed events): write 256 MiB, then
-    read a second 256 MiB buffer so that the flush's own dirty lines are
-    written back before the step starts instead of during it."""
+    read 1 GiB (8x L2) so that the flush's own dirty lines are written back
+    before the step starts instead of during it.  (Measured: a read of only
+    256 MiB after the write left enough dirty lines behind to add 2.7 us of
+    write-back to the next 52 us quantise; reads of 1 GiB or more, with or
+    without the write, all give the same step time.)"""
     import torch
     flush_w = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-    flush_r = torch.ones(256 << 20, dtype=torch.uint8, device="cuda")
+    flush_r = torch.ones(1 << 28, dtype=torch.int32, device="cuda")
 
     def flush():
         flush_w.zero_()
-        flush_r.sum(dtype=torch.int64)
+        torch.amax(flush_r)   # a plain read of all 1 GiB (no widened temporary)
     return flush
 
 
