@@ -1007,12 +1007,15 @@ def _e2e_time(torch, fn, steps, warmup):
     return sum(times) / len(times)
 
 
-def library_bar(W, flush, reps: int = 10):
+def library_bar(W, flush, reps: int = 10, interleave: bool = True):
     """The vendor library's GEMM on the same square shape, timed here in the
-    same process and clock window (best of `reps`, L2 flushed before each):
-    torch.matmul (cuBLAS) for bf16, torch._scaled_mm with per-tensor scales
-    (cuBLASLt FP8, the call AMP's VendorGemm makes, src/gemm_vendor.cpp:226-230)
-    for E4M3.  A measurement bar only; nothing of it is on the product path."""
+    same process (L2 flushed before each launch): torch.matmul (cuBLAS) for
+    bf16, torch._scaled_mm with per-tensor scales (cuBLASLt FP8, the call AMP's
+    VendorGemm makes, src/gemm_vendor.cpp:226-230) for E4M3.  With `interleave`
+    (one GPU) the library's launches alternate with this kernel's, so the two
+    means see the same clocks and power state -- these GEMMs run at the 1 kW
+    cap, where back-to-back blocks of launches do not.  A measurement bar only;
+    nothing of it is on the product path."""
     import torch
     S = W.S
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -1029,21 +1032,33 @@ def library_bar(W, flush, reps: int = 10):
     else:
         fn = lambda: torch.matmul(a, b)
         what = "cuBLAS bf16 (torch.matmul)"
-    for _ in range(3):
-        fn()
-    ts = []
-    for _ in range(reps):
+
+    def timed(f):
         flush()
         s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s0.record()
-        fn()
+        f()
         e0.record()
         e0.synchronize()
-        ts.append(s0.elapsed_time(e0))
+        return s0.elapsed_time(e0)
+    for _ in range(3):
+        fn()
+    lib_ms, ours_ms = [], []
+    for _ in range(reps):
+        lib_ms.append(timed(fn))
+        if interleave:
+            ours_ms.append(timed(W._launch))
     rate = lambda ms: round(2.0 * S ** 3 / (ms * 1e-3) / 1e12, 1)
-    return {"kernel": what, "shape": [S, S, S], "value": rate(min(ts)),
-            "mean": rate(statistics.mean(ts)), "unit": "TFLOP/s",
-            "timing": f"value: best of {reps}, mean: their mean; L2 flushed before each"}
+    out = {"kernel": what, "shape": [S, S, S], "value": rate(min(lib_ms)),
+           "mean": rate(statistics.mean(lib_ms)), "unit": "TFLOP/s",
+           "timing": f"value: best of {reps}, mean: their mean; L2 flushed before each"}
+    if interleave:
+        # this kernel at the same shape, launch for launch beside the library's
+        units = 2.0 * S * S * W.Np
+        out["ours_interleaved_mean"] = round(units / (statistics.mean(ours_ms) * 1e-3) / 1e12, 1)
+        out["ratio_interleaved"] = round(statistics.mean(lib_ms) / statistics.mean(ours_ms)
+                                         * (units / (2.0 * S ** 3)), 4)
+    return out
 
 
 def peak_for(W, peaks, live=None):
@@ -1127,7 +1142,7 @@ def measure(W, args, dist: Dist, flush, steps: int, warmup: int, cpu_budget_s: f
     live = {}
     bar = None
     if isinstance(W, GemmWorkload):
-        bar = library_bar(W, flush)
+        bar = library_bar(W, flush, interleave=dist.world == 1)
         if W.fp8:
             live["fp8_library"] = bar["value"]
     if W.bound == "fp32":
@@ -1166,7 +1181,7 @@ def measure(W, args, dist: Dist, flush, steps: int, warmup: int, cpu_budget_s: f
         "e2e": _round(e2e) if e2e else None,
     }
     if bar is not None:
-        # this kernel's mean launch against the library's mean launch
+        # this kernel's mean launch in the timed region against the library's mean launch
         bar["ratio"] = round(achieved / bar["mean"], 4)
         out["library_bar"] = bar
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
