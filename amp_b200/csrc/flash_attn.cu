@@ -16,9 +16,10 @@
 //              zero-filled; 4-D page-gather maps for paged K/V).
 //   warp 1     TMEM (512 columns: S0 | S1 | O0 | O1) and one MMA-issuing lane.
 //              Per K/V tile j and query tile t: O_t += P_t,j V_j (TS form: P
-//              read from TMEM, V MN-major from shared memory), then, once that
-//              MMA has completed (P_t,j lives in S_t), S_t = Q_t K_{j+1}^T (SS
-//              form).  The two tiles' chains S -> softmax -> P -> PV -> S are
+//              read from TMEM, V MN-major from shared memory), then at once
+//              S_t = Q_t K_{j+1}^T (SS form) into the columns P_t,j occupies:
+//              MMAs issued by one thread execute in issue order, so the PV has
+//              read P before the QK overwrites it.  The two tiles' chains S -> softmax -> P -> PV -> S are
 //              offset by half a step, so the tensor core works on one tile
 //              while the other tile's softmax runs.
 //   warps 2-3  idle (they only hand their registers to the softmax warps).
@@ -296,9 +297,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tc_fence_after();
                             k1_ready = true;
                         }
-                        // P_t,j sits in S_t: PV_t,j must have read it before S_t is rewritten
-                        if (!mbar_wait(&pv_done[t], j & 1, p.status)) { ok = false; break; }
-                        tc_fence_after();
+                        // P_t,j sits in S_t, which this QK overwrites: tcgen05.mma
+                        // operations issued by one thread execute in issue order, so
+                        // PV_t,j has read P before QK_t,j+1 writes S_t -- no wait here.
                         qk(t, k1_addr);
                         tc_commit(&s_full[t]);
                         if (t == 1) tc_commit(&k_empty[s1]);

@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* dp_full = bars + 6;     // dP^T of the step in TMEM
     uint64_t* p_full = bars + 7;      // P^T written back (8 warps)
     uint64_t* ds_full = bars + 8;     // dS^T written back (8 warps)
-    uint64_t* dv_done = bars + 9;     // dV has read P^T: S^T may be rewritten
+    // bars + 9: unused (S^T_{t+1} follows dV_t in MMA issue order, no barrier between)
     uint64_t* dk_done = bars + 10;    // dK has read dS^T: dP^T may be rewritten
     uint64_t* drain = bars + 11;
     uint64_t* cols_ready = bars + 12; // [2]: the 256 element-wise threads posted the step
@@ -207,7 +207,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(dp_full, 1);
         mbar_init(p_full, 8);
         mbar_init(ds_full, 8);
-        mbar_init(dv_done, 1);
         mbar_init(dk_done, 1);
         mbar_init(drain, 1);
         mbar_init(&cols_ready[0], 256);
@@ -272,10 +271,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!mbar_wait(p_full, t & 1, p.status)) break;
                 tc_fence_after();
                 mma_ts<D>(T_dV, T_S, oa(t), t != 0);    // dV += P^T dO
-                tc_commit(dv_done);
                 if (more) {
+                    // S^T_{t+1} overwrites P^T_t, which dV_t reads: tcgen05.mma operations
+                    // issued by one thread execute in issue order, so no wait is needed
                     if (!mbar_wait(&qs_full[(t + 1) & 1], ((t + 1) >> 1) & 1, p.status)) break;
-                    if (!mbar_wait(dv_done, t & 1, p.status)) break;   // P^T_t read
                     tc_fence_after();
                     mma_ss<D>(T_S, ka, qa(t + 1));
                     tc_commit(s_full);
@@ -285,9 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mma_ts<D>(T_dK, T_dP, qa(t), t != 0);   // dK += dS^T Q
                 tc_commit(dk_done);
                 tc_commit(&qs_empty[t & 1]);
-                if (more) {
-                    if (!mbar_wait(dk_done, t & 1, p.status)) break;   // dS^T_t read
-                    tc_fence_after();
+                if (more) {   // dP^T_{t+1} over dS^T_t, after dK_t in issue order
                     mma_ss<D>(T_dP, va, oa(t + 1));
                     tc_commit(dp_full);
                 }
@@ -557,9 +554,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mma_ts<D>(T_dQ, T_dP, ka(j), j != 0);   // dQ += dS K
                 tc_commit(dq_done);
                 tc_commit(&k_empty[j & 1]);
-                if (more) {
+                if (more) {   // dP_{j+1} over dS_j, after dQ_j in issue order
                     if (!mbar_wait(&v_full[n1], ph1, p.status)) break;
-                    if (!mbar_wait(dq_done, j & 1, p.status)) break;   // dS_j read
                     tc_fence_after();
                     mma_ss<D>(T_dP, oa, va(j + 1));
                     tc_commit(&v_empty[n1]);
