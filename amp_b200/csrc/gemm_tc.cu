@@ -64,7 +64,14 @@ constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 // all-gather mode: per epilogue warp a [32 rows x 128 B] staging tile, so that
 // the stores to the other ranks go out as whole 128-byte row segments
-constexpr int AG_STAGE_BYTES = 4 * 32 * 128;
+// Staged rows are AG_GROUP = 128 bytes plus 16 of padding, so that the
+// epilogue lanes' 16-byte writes of their own rows spread over the banks while
+// every row stays contiguous for the bulk copy that sends it.  (Whole 512-byte
+// tile rows, with the pair kernel's ring cut to 4 stages to make room, measured
+// slower at 2 GPUs: bf16 1490 -> 1390, E4M3 2707 -> 2471 TFLOP/s a rank.)
+constexpr int AG_GROUP = 128;
+constexpr int AG_ROW_PITCH = AG_GROUP + 16;
+constexpr int AG_STAGE_BYTES = 4 * 32 * AG_ROW_PITCH;
 constexpr int SMEM_BYTES_AG = SMEM_BYTES + AG_STAGE_BYTES;
 constexpr uint32_t TMEM_COLS = 512;
 
@@ -190,6 +197,85 @@ __device__ __forceinline__ void store_chunk(OutT* out, const float (&v)[32], int
     }
 }
 
+// All-gather mode, one 32-value chunk of this thread's row: chunk groups of 128
+// bytes a row that lie inside N go through the warp's [32 rows x 128 B] staging
+// tile (all lanes, rows past M included); after a group's last chunk every lane
+// hands its row's 128 bytes to the bulk-copy (TMA) engine, one asynchronous
+// shared -> global copy per rank's C (this rank last), so the NVLink traffic is
+// streamed by the copy engine instead of by the epilogue's store instructions.
+// Before a lane rewrites its staging row it waits until its earlier copies have
+// read it.  Returns false for a chunk outside such a group, which the caller
+// stores row by row.  row0: the warp's first row of C; stage: the warp's tile.
+template <typename OutT>
+__device__ __forceinline__ bool ag_stage_chunk(const float (&v)[32], int c, int tn, int row0,
+                                               int lane, uint8_t* stage, const TcParams& p) {
+    static_assert(sizeof(OutT) != 1, "E4M3 output is stored row by row");
+    constexpr int CPG = AG_GROUP / (32 * (int)sizeof(OutT));   // chunks per group
+    if (tn * BN + (c / CPG + 1) * CPG * 32 > p.N) return false;
+    constexpr int Q = 32 * (int)sizeof(OutT) / 16;         // 16-byte slots of a chunk
+    uint4* row = reinterpret_cast<uint4*>(stage + lane * AG_ROW_PITCH);
+    if (c % CPG == 0)   // this lane's copies of the previous group have read its row
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+#pragma unroll
+    for (int k = 0; k < Q; ++k) {
+        uint4 w;
+        if constexpr (sizeof(OutT) == 4) {
+            w = make_uint4(__float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]),
+                           __float_as_uint(v[4 * k + 2]), __float_as_uint(v[4 * k + 3]));
+        } else {
+            w.x = f32x2_to_bf16x2(v[8 * k], v[8 * k + 1]);
+            w.y = f32x2_to_bf16x2(v[8 * k + 2], v[8 * k + 3]);
+            w.z = f32x2_to_bf16x2(v[8 * k + 4], v[8 * k + 5]);
+            w.w = f32x2_to_bf16x2(v[8 * k + 6], v[8 * k + 7]);
+        }
+        row[(c % CPG) * Q + k] = w;
+    }
+    if (c % CPG == CPG - 1 && row0 + lane < p.M) {
+        fence_proxy_async_smem();   // the row's generic-proxy writes, seen by the copies
+        const int gcol = p.col_base + tn * BN + (c - CPG + 1) * 32;
+        const int64_t off = ((int64_t)(row0 + lane) * p.ldc + gcol) * sizeof(OutT);
+        for (int i = 1; i <= p.world; ++i) {
+            uint8_t* dst = static_cast<uint8_t*>(p.peers[(p.rank + i) % p.world]) + off;
+            asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                         "r"(smem_u32(row)), "n"(AG_GROUP)
+                         : "memory");
+        }
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    return true;
+}
+
+// All-gather mode: a chunk outside the staged groups, row by row into every
+// rank's C (this rank last).
+template <typename OutT>
+__device__ __forceinline__ void ag_store_row_chunk(const float (&v)[32], int row, int col0,
+                                                   float inv_c, const TcParams& p) {
+    for (int i = 1; i <= p.world; ++i) {
+        const int d = (p.rank + i) % p.world;
+        store_chunk(static_cast<OutT*>(p.peers[d]) + (int64_t)row * p.ldc + p.col_base + col0, v,
+                    p.N - col0, inv_c);
+    }
+}
+
+// All-gather mode, after an epilogue warp's last tile: its stores and bulk copies
+// (local and remote) are made visible system-wide before it counts itself done; the last
+// of the launch's 4 * gridDim.x epilogue warps exchanges the call's sequence
+// number with every rank, so the kernel ends only once every rank's C is whole.
+__device__ __forceinline__ void ag_finish(int lane, const TcParams& p) {
+    // this lane's bulk copies have completed their writes
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __threadfence_system();
+    __syncwarp();
+    unsigned last = 0;
+    if (lane == 0) last = atomicAdd(p.done, 1u) == 4u * gridDim.x - 1u;
+    if (__shfl_sync(0xffffffffu, last, 0)) {
+        __shared__ unsigned got[kMaxPeers];
+        __threadfence_system();
+        mailbox_exchange(p.mbox, p.rank, p.world, p.seq, 1u, got, p.status);
+    }
+}
+
 template <bool kFP8, typename OutT, bool kAllGather>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -301,8 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         const int quad = warp & 3;             // TMEM lanes [32*quad, 32*quad + 32)
         const int row_in_tile = quad * 32 + lane;
-        uint4* ag_stage = reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES + 256) +
-                          (warp - 2) * 32 * 8;   // all-gather mode only
+        uint8_t* ag_stage = smem + STAGES * STAGE_BYTES + 256 +
+                            (warp - 2) * 32 * AG_ROW_PITCH;   // all-gather mode only
         float amx = 0.0f;                      // this thread's max |C| (NaN ignored)
         int i = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
@@ -328,87 +414,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const int col0 = tn * BN + c * 32;
                 if (col0 >= p.N) continue;  // warp-uniform
-                // all-gather mode: chunk groups of 128 bytes a row that lie inside N go
-                // through the staging tile (all lanes, rows past M included)
-                constexpr int CPG = 128 / (32 * (int)sizeof(OutT));   // chunks per group
-                const bool staged = kAllGather && (tn * BN + (c / CPG + 1) * CPG * 32 <= p.N);
                 float v[32];
                 scale_chunk(r, v, sa, p, col0, lane);
                 if (p.amax && row_ok) amax_chunk(amx, v, p.N - col0);
                 if constexpr (kAllGather && sizeof(OutT) != 1) {
-                    if (staged) {
-                        // this row's 32 values into 16-byte columns [slot0, slot0 + Q) of the
-                        // warp's staging row, swizzled by row so neither side conflicts
-                        constexpr int Q = 32 * (int)sizeof(OutT) / 16;
-                        const int slot0 = (c % CPG) * Q;
-#pragma unroll
-                        for (int k = 0; k < Q; ++k) {
-                            uint4 w;
-                            if constexpr (sizeof(OutT) == 4) {
-                                w = make_uint4(__float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]),
-                                               __float_as_uint(v[4 * k + 2]), __float_as_uint(v[4 * k + 3]));
-                            } else {
-                                w.x = f32x2_to_bf16x2(v[8 * k], v[8 * k + 1]);
-                                w.y = f32x2_to_bf16x2(v[8 * k + 2], v[8 * k + 3]);
-                                w.z = f32x2_to_bf16x2(v[8 * k + 4], v[8 * k + 5]);
-                                w.w = f32x2_to_bf16x2(v[8 * k + 6], v[8 * k + 7]);
-                            }
-                            ag_stage[lane * 8 + ((slot0 + k) ^ (lane & 7))] = w;
-                        }
-                        if (c % CPG == CPG - 1) {
-                            __syncwarp();
-                            // 32 rows x 128 B to every rank's C (this rank last): each store
-                            // instruction writes 4 whole row segments
-                            const int gcol = p.col_base + tn * BN + (c - CPG + 1) * 32;
-                            const int row0 = tm * BM + quad * 32;
-                            for (int i = 1; i <= p.world; ++i) {
-                                uint8_t* base = static_cast<uint8_t*>(p.peers[(p.rank + i) % p.world]);
-#pragma unroll
-                                for (int it = 0; it < 8; ++it) {
-                                    const int idx = it * 32 + lane, r8 = idx >> 3, c16 = idx & 7;
-                                    if (row0 + r8 < p.M)
-                                        *reinterpret_cast<uint4*>(
-                                            base + ((int64_t)(row0 + r8) * p.ldc + gcol) * sizeof(OutT) +
-                                            c16 * 16) = ag_stage[r8 * 8 + (c16 ^ (r8 & 7))];
-                                }
-                            }
-                            __syncwarp();
-                        }
+                    if (ag_stage_chunk<OutT>(v, c, tn, tm * BM + quad * 32, lane, ag_stage, p))
                         continue;
-                    }
                 }
                 if (!row_ok) continue;
-                if constexpr (!kAllGather) {
+                if constexpr (!kAllGather)
                     store_chunk(static_cast<OutT*>(p.C) + (int64_t)row * p.N + col0, v, p.N - col0,
                                 inv_c);
-                } else {
-                    // every rank's C, this rank last (peers first, spread over the links)
-                    for (int i = 1; i <= p.world; ++i) {
-                        const int d = (p.rank + i) % p.world;
-                        store_chunk(static_cast<OutT*>(p.peers[d]) + (int64_t)row * p.ldc +
-                                        p.col_base + col0,
-                                    v, p.N - col0, inv_c);
-                    }
-                }
+                else
+                    ag_store_row_chunk<OutT>(v, row, col0, inv_c, p);
             }
         }
         if (p.amax) {   // non-negative floats order like their bit patterns
             const float m = warp_max(amx);
             if (lane == 0) atomicMax(reinterpret_cast<unsigned*>(p.amax), __float_as_uint(m));
         }
-        if constexpr (kAllGather) {
-            // this warp's stores (local and remote) are visible system-wide before it
-            // counts itself done; the last of the 4 * gridDim.x warps signals the peers
-            __threadfence_system();
-            __syncwarp();
-            unsigned last = 0;
-            if (lane == 0) last = atomicAdd(p.done, 1u) == 4u * gridDim.x - 1u;
-            if (__shfl_sync(0xffffffffu, last, 0)) {
-                __shared__ unsigned got[kMaxPeers];
-                __threadfence_system();
-                mailbox_exchange(p.mbox, p.rank, p.world, p.seq, 1u, got, p.status);
-            }
-        }
+        if constexpr (kAllGather) ag_finish(lane, p);
     }
 
     tc_fence_before();
@@ -432,7 +457,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int STAGES2 = 6;
 constexpr int STAGE2_BYTES = A_STAGE_BYTES + (BN / 2) * SLAB;   // 16 KiB A + 16 KiB B
 constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
-static_assert(SMEM2_BYTES <= 227 * 1024 && SMEM_BYTES_AG <= 227 * 1024,
+constexpr int SMEM2_BYTES_AG = SMEM2_BYTES + AG_STAGE_BYTES;   // + the all-gather staging
+static_assert(SMEM2_BYTES_AG <= 227 * 1024 && SMEM_BYTES_AG <= 227 * 1024,
               "dynamic shared memory above the 227 KiB a CTA can have");
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -529,7 +555,7 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
                  : "memory");
 }
 
-template <bool kFP8, typename OutT>
+template <bool kFP8, typename OutT, bool kAllGather = false>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const TcParams p) {
@@ -545,9 +571,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES);
-    uint64_t* empty = full + STAGES2;
-    uint64_t* tfull = empty + STAGES2;
+    constexpr int ST = STAGES2;   // operand ring depth
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * STAGE2_BYTES);
+    uint64_t* empty = full + ST;
+    uint64_t* tfull = empty + ST;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -559,7 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int total = p.num_m * p.num_n;            // 256 x 256 tiles
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES2; ++s) {
+        for (int s = 0; s < ST; ++s) {
             mbar_init(&full[s], 1);      // leader: its producer's expect_tx, both CTAs' bytes
             mbar_init(&empty[s], 1);     // each CTA: the leader's commit (CTA mask 0b11)
         }
@@ -604,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < B_BOXES; ++j)
                         tma_load_2d_pair(sb + j * B_BOX_BYTES, &tmB, fb,
                                          tn * BN + (int)rank * (BN / 2) + j * B_BOX_COLS, kb * BK);
-                    if (++s == STAGES2) { s = 0; ph ^= 1; }
+                    if (++s == ST) { s = 0; ph ^= 1; }
                 }
             }
         }
@@ -632,7 +659,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tc_mma_pair<kFP8>(d_tmem, ad, bd, IDESC, (kb | k) != 0);
                     }
                     tc_commit_pair_mc(&empty[s]);
-                    if (++s == STAGES2) { s = 0; ph ^= 1; }
+                    if (++s == ST) { s = 0; ph ^= 1; }
                 }
                 if (ok) tc_commit_pair_mc(&tfull[acc]);
             }
@@ -644,6 +671,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quad = warp & 3;             // TMEM lanes [32*quad, 32*quad + 32)
         const int row_in_tile = quad * 32 + lane;
         const uint32_t tempty0 = cluster_addr(&tempty[0], 0), tempty1 = cluster_addr(&tempty[1], 0);
+        uint8_t* ag_stage = smem + ST * STAGE2_BYTES + 256 +
+                            (warp - 2) * 32 * AG_ROW_PITCH;   // all-gather mode only
         float amx = 0.0f;                      // this thread's max |C| (NaN ignored)
         int i = 0;
         for (int t = pair; t < total; t += n_pairs, ++i) {
@@ -672,14 +701,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float v[32];
                 scale_chunk(r, v, sa, p, col0, lane);
                 if (p.amax && row_ok) amax_chunk(amx, v, p.N - col0);
+                if constexpr (kAllGather && sizeof(OutT) != 1) {
+                    if (ag_stage_chunk<OutT>(v, c, tn, tm * 2 * BM + (int)rank * BM + quad * 32,
+                                             lane, ag_stage, p))
+                        continue;
+                }
                 if (!row_ok) continue;
-                store_chunk(static_cast<OutT*>(p.C) + (int64_t)row * p.N + col0, v, p.N - col0, inv_c);
+                if constexpr (!kAllGather)
+                    store_chunk(static_cast<OutT*>(p.C) + (int64_t)row * p.N + col0, v, p.N - col0,
+                                inv_c);
+                else
+                    ag_store_row_chunk<OutT>(v, row, col0, inv_c, p);
             }
         }
         if (p.amax) {   // non-negative floats order like their bit patterns
             const float m = warp_max(amx);
             if (lane == 0) atomicMax(reinterpret_cast<unsigned*>(p.amax), __float_as_uint(m));
         }
+        if constexpr (kAllGather) ag_finish(lane, p);
     }
 
     tc_fence_before();
@@ -934,17 +973,18 @@ struct AllGather {
 
 // How many SM pairs can hold a k_gemm_tc2 cluster at once on this device (0 if
 // none), with the kernel's shared-memory attribute set on first use.
-template <bool kFP8, typename OutT>
+template <bool kFP8, typename OutT, bool kAG = false>
 int pair_slots() {
     static std::atomic<int> slots[64];   // per device ordinal: 0 unknown, -1 none, else count
+    constexpr int smem = kAG ? SMEM2_BYTES_AG : SMEM2_BYTES;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return 0;
     int n = slots[dev].load();
     if (n == 0) {
-        auto kern = k_gemm_tc2<kFP8, OutT>;
+        auto kern = k_gemm_tc2<kFP8, OutT, kAG>;
         n = -1;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             SMEM2_BYTES);
+                                             smem);
         if (e == cudaSuccess) {
             cudaLaunchConfig_t cfg = {};
             cudaLaunchAttribute attr[1];
@@ -954,7 +994,7 @@ int pair_slots() {
             attr[0].val.clusterDim.z = 1;
             cfg.gridDim = dim3(2 * sm_count());
             cfg.blockDim = dim3(kThreads);
-            cfg.dynamicSmemBytes = SMEM2_BYTES;
+            cfg.dynamicSmemBytes = smem;
             cfg.attrs = attr;
             cfg.numAttrs = 1;
             int c = 0;
@@ -968,7 +1008,7 @@ int pair_slots() {
     return n > 0 ? n : 0;
 }
 
-template <bool kFP8, typename OutT>
+template <bool kFP8, typename OutT, bool kAG = false>
 int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const TcParams& p, int pairs,
                 cudaStream_t st) {
     const int total = p.num_m * p.num_n;
@@ -981,11 +1021,11 @@ int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const TcParams& 
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(2 * n_pairs);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = SMEM2_BYTES;
+    cfg.dynamicSmemBytes = kAG ? SMEM2_BYTES_AG : SMEM2_BYTES;
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    AMPB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc2<kFP8, OutT>, tmA, tmB, p));
+    AMPB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc2<kFP8, OutT, kAG>, tmA, tmB, p));
     AMPB_CHECK_LAUNCH("k_gemm_tc2");
     return AMP_OK;
 }
@@ -1050,13 +1090,14 @@ int launch_tc(const void* A, const void* B, void* C, int M, int N, int K, const 
         p.done = static_cast<unsigned*>(done);
     }
     if (amax) AMPB_CHECK_CUDA(cudaMemsetAsync(amax, 0, sizeof(float), st));
-    if (!ag) {
+    {
         // 256 x 256 tiles on SM pairs once there are enough of them to fill the pairs
         const int pm = (M + 2 * BM - 1) / (2 * BM), pn = p.num_n;
-        const int pairs = pair_slots<kFP8, OutT>();
+        const int pairs = ag ? pair_slots<kFP8, OutT, true>() : pair_slots<kFP8, OutT, false>();
         if (pairs > 0 && (int64_t)pm * pn >= pairs) {
             p.num_m = pm;
-            return launch_pair<kFP8, OutT>(tmA, tmB, p, pairs, st);
+            return ag ? launch_pair<kFP8, OutT, true>(tmA, tmB, p, pairs, st)
+                      : launch_pair<kFP8, OutT, false>(tmA, tmB, p, pairs, st);
         }
     }
     auto kern = ag ? k_gemm_tc<kFP8, OutT, true> : k_gemm_tc<kFP8, OutT, false>;

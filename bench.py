@@ -401,9 +401,8 @@ class GemmWorkload:
         return self.describe(self.args, self.dist.world, self.dist.rank)
 
     def kernel_table(self):
-        # 256 x 256 tiles on SM pairs (k_gemm_tc2) unless the all-gather epilogue runs
-        name = "k_gemm_tc" if self.peer is not None else "k_gemm_tc2"
-        return [(f"{name}<{'e4m3' if self.fp8 else 'bf16'}>", self.units_per_step())]
+        # 256 x 256 tiles on SM pairs (k_gemm_tc2), with the all-gather epilogue at N > 1
+        return [(f"k_gemm_tc2<{'e4m3' if self.fp8 else 'bf16'}>", self.units_per_step())]
 
     def _launch(self):
         if self.peer is not None:
