@@ -1112,6 +1112,12 @@ def measure(W, args, dist: Dist, flush, steps: int, warmup: int, cpu_budget_s: f
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
+    # A GPU-side pause (~1 ms a step, at most 200 ms; outside the events) lets the
+    # host queue the steps ahead of the GPU, so the events time GPU execution and
+    # not the pace at which each rank's Python enqueues: at N > 1 the steps are
+    # coupled by their exchanges, and one rank's host jitter would stall them all.
+    if hasattr(torch.cuda, "_sleep"):
+        torch.cuda._sleep(int(2e6) * min(steps, 200))
     phys = os.environ.get("CUDA_VISIBLE_DEVICES")
     dev_index = torch.cuda.current_device()
     nvml_index = int(phys.split(",")[dev_index]) if phys else dev_index
