@@ -3,7 +3,7 @@
 // (amp_comm_*), and the NCCL forms of the N-split GEMM and the
 // (batch*head)-split attention.  No Python and no torch are involved.
 //
-//   amp_b200_sharded <world> [M N K] [--op bf16|fp8|attn]
+//   amp_b200_sharded <world> [M N K] [--op bf16|fp8|attn|attn_gqa]
 //
 // The parent forks `world` ranks before anything touches CUDA; rank 0 makes
 // the communicator's unique id (AMP's comm_get_unique_id,
@@ -90,11 +90,12 @@ int run_rank(int rank, int world, int M, int N, int K, const std::string& op, in
     CK(cudaStreamCreate(&st));
     size_t diff = 0, bytes = 0;
     g_state = 12345;  // the same inputs on every rank
-    if (op == "attn") {
-        // q/k/v [B, H, S, D]: B = 2 * world sequences, H = 8 heads, S = M, D = 128
-        const int B = 2 * world, H = 8, S = M, D = 128;
-        const size_t n = (size_t)B * H * S * D;
-        std::vector<uint16_t> hq(n), hk(n), hv(n);
+    if (op == "attn" || op == "attn_gqa") {
+        // q [B, H, S, D], k/v [B, Hkv, S, D]: B = 2 * world sequences, H = 8 heads (Hkv = 8,
+        // split over batch*heads; or Hkv = 2 under GQA, split over whole sequences), S = M
+        const int B = 2 * world, H = 8, Hkv = op == "attn" ? 8 : 2, S = M, D = 128;
+        const size_t n = (size_t)B * H * S * D, nkv = (size_t)B * Hkv * S * D;
+        std::vector<uint16_t> hq(n), hk(nkv), hv(nkv);
         for (auto* v : {&hq, &hk, &hv})
             for (auto& x : *v) x = rand_bf16();
         void *q, *k, *v, *o, *o_ref, *l, *l_ref;
@@ -103,9 +104,9 @@ int run_rank(int rank, int world, int M, int N, int K, const std::string& op, in
         CK(cudaMalloc(&o_ref, n * 2));
         CK(cudaMalloc(&l, (size_t)B * H * S * 4));
         CK(cudaMalloc(&l_ref, (size_t)B * H * S * 4));
-        AK(amp_flash_attn_fwd_sharded_dev(comm, q, k, v, o, (float*)l, B, H, H, S, S, D, 1, 0.f,
+        AK(amp_flash_attn_fwd_sharded_dev(comm, q, k, v, o, (float*)l, B, H, Hkv, S, S, D, 1, 0.f,
                                           st));
-        AK(amp_flash_attn_fwd_bf16_dev(q, k, v, o_ref, (float*)l_ref, B, H, H, S, S, D, 1, 0.f,
+        AK(amp_flash_attn_fwd_bf16_dev(q, k, v, o_ref, (float*)l_ref, B, H, Hkv, S, S, D, 1, 0.f,
                                        st));
         CK(cudaStreamSynchronize(st));
         size_t d2 = 0;
@@ -189,7 +190,7 @@ int run_rank(int rank, int world, int M, int N, int K, const std::string& op, in
 
 int main(int argc, char** argv) {
     if (argc < 2) {
-        std::fprintf(stderr, "usage: %s <world> [M N K] [--op bf16|fp8|attn]\n", argv[0]);
+        std::fprintf(stderr, "usage: %s <world> [M N K] [--op bf16|fp8|attn|attn_gqa]\n", argv[0]);
         return 2;
     }
     const int world = std::atoi(argv[1]);
@@ -208,7 +209,7 @@ int main(int argc, char** argv) {
         K = std::atoi(pos[2].c_str());
     }
     if (world < 1 || world > 64 || M <= 0 || N <= 0 || K <= 0 || N % world ||
-        (op != "bf16" && op != "fp8" && op != "attn")) {
+        (op != "bf16" && op != "fp8" && op != "attn" && op != "attn_gqa")) {
         std::fprintf(stderr, "bad arguments\n");
         return 2;
     }

@@ -116,13 +116,13 @@ def _run_tool(world, op, mnk=("1024", "2048", "512")):
     assert all(x["mismatched_bytes"] == 0 and x["max_over_ranks"] == 0 for x in lines), r.stdout
 
 
-@pytest.mark.parametrize("op", ["bf16", "fp8", "attn"])
+@pytest.mark.parametrize("op", ["bf16", "fp8", "attn", "attn_gqa"])
 def test_cpp_host_one_rank(cuda, amp_lib, op):
     _run_tool(1, op)
 
 
 @pytest.mark.multigpu
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("op", ["bf16", "fp8", "attn"])
+@pytest.mark.parametrize("op", ["bf16", "fp8", "attn", "attn_gqa"])
 def test_cpp_host_two_ranks_bit_identical_to_one_gpu(cuda, amp_lib, op):
     _run_tool(2, op)
