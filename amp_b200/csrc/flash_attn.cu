@@ -9,9 +9,15 @@
 // flash_attn.cu:134,152) -- generalised here by an offset so that paged
 // prefill can use bottom-right alignment (key j visible iff j <= i + offset).
 //
-// One CTA per (batch*head, pair of 128-row query tiles), 384 threads in three
-// warpgroups (setmaxnreg: 72 registers for the first, 216 for the softmax ones):
-//   warp 0     TMA: both Q tiles once; K and V tiles (128 rows) into separate
+// Work items are (batch*head, pair of 128-row query tiles).  The dense forward
+// runs one persistent CTA per SM over units of two items of one head (the
+// heaviest and the lightest pair left under a causal mask, so units weigh the
+// same); the barriers' phases run on across items, the load warp fetches the
+// next item's Q and K/V while the current one finishes, and the next item's first
+// QK_0 is issued as soon as query tile 0 has finished.  The paged and all-gather
+// forms run one CTA per item.  384 threads in three warpgroups (setmaxnreg: 72
+// registers for the first, 216 for the softmax ones):
+//   warp 0     TMA: both Q tiles of each item; K and V tiles (128 rows) into separate
 //              2-stage rings (128-byte swizzle, 3-D maps so each head's tail is
 //              zero-filled; 4-D page-gather maps for paged K/V).
 //   warp 1     TMEM (512 columns: S0 | S1 | O0 | O1) and one MMA-issuing lane.
@@ -100,6 +106,14 @@ __device__ __forceinline__ float lg2_approx(float x) {
     return y;
 }
 
+// The value, opaque to the compiler: shared-memory descriptors built from it are
+// recomputed at each use instead of being hoisted out of the item and step loops
+// into registers the 72-register control warps do not have.
+__device__ __forceinline__ uint32_t opaque_u32(uint32_t x) {
+    asm volatile("mov.b32 %0, %0;" : "+r"(x));
+    return x;
+}
+
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -116,10 +130,14 @@ struct FaCfg {
     static constexpr uint32_t O_COL = 2 * BKV;            // S0 | S1 | O0 | O1
 };
 
-template <int D, bool kPaged, bool kAllGather = false>
+// kPersist: one CTA per SM walks a list of (batch*head, query-tile pair) items
+// (see item_at below) instead of one CTA per item, so that the next item's Q and
+// K/V loads and its first QK overlap the current item's last steps and epilogue.
+template <int D, bool kPaged, bool kAllGather = false, bool kPersist = false>
 __global__ void __launch_bounds__(kThreads, 1)
     k_flash_fwd(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
            const __grid_constant__ CUtensorMap tmV, const FaParams p) {
+    static_assert(!(kPersist && kAllGather), "the all-gather epilogue stages in Q: one item per CTA");
     using CF = FaCfg<D>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -128,43 +146,78 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* k_s = q_s + 2 * CF::TILE;          // [KV_STAGES][TILE]
     uint8_t* v_s = k_s + KV_STAGES * CF::TILE;        // [KV_STAGES][TILE]
     uint64_t* bars = reinterpret_cast<uint64_t*>(v_s + KV_STAGES * CF::TILE);
-    uint64_t* q_full = bars;
-    uint64_t* k_full = bars + 1;
+    uint64_t* q_full = bars;             // [2] per query tile
+    uint64_t* q_empty = q_full + 2;      // [2] the item's last QK_t has read Q_t
+    uint64_t* k_full = q_empty + 2;
     uint64_t* k_empty = k_full + KV_STAGES;
     uint64_t* v_full = k_empty + KV_STAGES;
     uint64_t* v_empty = v_full + KV_STAGES;
     uint64_t* s_full = v_empty + KV_STAGES;   // [2] per query tile
     uint64_t* p_full = s_full + 2;      // [2]
     uint64_t* pv_done = p_full + 2;     // [2]
-    uint64_t* drain = pv_done + 2;
+    uint64_t* o_free = pv_done + 2;     // [2] the epilogue has read O_t out of TMEM
+    uint64_t* drain = o_free + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_qb = (p.S_q + 2 * BQ - 1) / (2 * BQ);
-    const int qb = n_qb - 1 - (int)blockIdx.x;
-    const int bh = blockIdx.y;
-    const int b = bh / p.Hq, h = bh % p.Hq;
-    const int bh_kv = b * p.Hkv + h / (p.Hq / p.Hkv);
-    const int q0 = qb * 2 * BQ;
-    int S_kv = p.S_kv, coff = p.causal_offset;
-    if constexpr (kPaged) {
-        S_kv = max(0, p.ctx_lens[b]);
-        coff = S_kv - p.S_q;
-    }
-    const int n_all = (S_kv + BKV - 1) / BKV;
-    auto nblk = [&](int row0) {
-        int n = n_all;
-        if (p.causal) {
-            const int last = row0 + BQ - 1 + coff;
-            n = min(n, last < 0 ? 0 : last / BKV + 1);
+    // Items of this CTA, k = 0, 1, ...: 0 = no more, 1 = item (bh, qb), 2 = empty slot.
+    // Persistent: unit u = blockIdx.x + (k/2) * gridDim.x pairs query-tile pair
+    // n_qb-1-q (heaviest under a causal mask) with pair q of the same head, so every
+    // unit of a causal square problem carries the same work and consecutive units
+    // share a head (K/V stay in L2).  Otherwise the one item of the grid cell.
+    const int half = (n_qb + 1) / 2;
+    const int units = p.B * p.Hq * half;
+    auto item_at = [&](int k, int& bh, int& qb) -> int {
+        if constexpr (!kPersist) {
+            if (k > 0) return 0;
+            bh = blockIdx.y;
+            qb = n_qb - 1 - (int)blockIdx.x;
+            return 1;
+        } else {
+            const int u = (int)blockIdx.x + (k >> 1) * (int)gridDim.x;
+            if (u >= units) return 0;
+            bh = u / half;
+            const int q = u % half;
+            qb = (k & 1) ? q : n_qb - 1 - q;
+            return ((k & 1) && q == n_qb - 1 - q) ? 2 : 1;
         }
-        return max(n, 1);
     };
-    const int n0 = nblk(q0);
-    const int n1 = max(nblk(q0 + BQ), n0);
+    struct Geo {
+        int b, h, bh_kv, q0, S_kv, coff, n0, n1;
+    };
+    auto geo = [&](int bh, int qb) {
+        Geo g;
+        g.b = bh / p.Hq;
+        g.h = bh % p.Hq;
+        g.bh_kv = g.b * p.Hkv + g.h / (p.Hq / p.Hkv);
+        g.q0 = qb * 2 * BQ;
+        g.S_kv = p.S_kv;
+        g.coff = p.causal_offset;
+        if constexpr (kPaged) {
+            g.S_kv = max(0, p.ctx_lens[g.b]);
+            g.coff = g.S_kv - p.S_q;
+        }
+        const int n_all = (g.S_kv + BKV - 1) / BKV;
+        auto nblk = [&](int row0) {
+            int n = n_all;
+            if (p.causal) {
+                const int last = row0 + BQ - 1 + g.coff;
+                n = min(n, last < 0 ? 0 : last / BKV + 1);
+            }
+            return max(n, 1);
+        };
+        g.n0 = nblk(g.q0);
+        g.n1 = max(nblk(g.q0 + BQ), g.n0);
+        return g;
+    };
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&q_full[i], 1);
+            mbar_init(&q_empty[i], 1);
+            mbar_init(&o_free[i], 4);
+        }
         for (int s = 0; s < KV_STAGES; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], 1);
@@ -196,57 +249,79 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tmQ);
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
-            mbar_arrive_expect_tx(q_full, 2 * CF::TILE);
+            // K/V tiles run through the rings continuously across items: tile g of
+            // this CTA uses stage g % KV_STAGES in phase (g / KV_STAGES) & 1
+            int gkv = 0, li = 0;
+            bool ok = true;
+            for (int k = 0; ok; ++k) {
+                int bh, qb;
+                const int st = item_at(k, bh, qb);
+                if (st == 0) break;
+                if (st == 2) continue;
+                const Geo g = geo(bh, qb);
+                // Q_t of this item once the previous item's last QK_t has read Q_t.
+                // Persistent order: Q_0, K/V 0, Q_1, K/V 1.. -- Q_1 is freed last
+                // (tile 1 runs the previous item's last step), and the next item's
+                // first QK_0 is issued while it does.  One item: Q_0, Q_1, K/V 0, ...
+                auto load_q = [&](int t) {
+                    if (li > 0 && !mbar_wait(&q_empty[t], (li - 1) & 1, p.status)) return false;
+                    mbar_arrive_expect_tx(&q_full[t], CF::TILE);
 #pragma unroll
-            for (int t = 0; t < 2; ++t)
-#pragma unroll
-                for (int sl = 0; sl < CF::SLABS; ++sl)
-                    tma_load_3d(q_s + t * CF::TILE + sl * SLAB_BYTES, &tmQ, q_full, sl * 64,
-                                q0 + t * BQ, bh);
-            const int last_page = max(0, (S_kv + kPageTokens - 1) / kPageTokens - 1);
-            const int hk = h / (p.Hq / p.Hkv);
-            for (int j = 0; j < n1; ++j) {
-                const int s = j % KV_STAGES;
-                const uint32_t ph = (j / KV_STAGES) & 1;
-                int pages[BKV / kPageTokens];
-                if constexpr (kPaged) {
-                    const int* bt = p.block_table + (int64_t)b * p.max_pages;
-#pragma unroll
-                    for (int i = 0; i < BKV / kPageTokens; ++i) {
-                        const int pg = bt[min(j * (BKV / kPageTokens) + i, last_page)];
-                        const bool bad = pg < 0 || pg >= p.num_pages;
-                        if (bad && S_kv > 0) atomicExch(p.status, AMP_DEV_ERR_BAD_PAGE);
-                        pages[i] = bad ? 0 : pg;
-                    }
-                }
-                if (!mbar_wait(&k_empty[s], ph ^ 1, p.status)) break;
-                mbar_arrive_expect_tx(&k_full[s], CF::TILE);
-#pragma unroll
-                for (int sl = 0; sl < CF::SLABS; ++sl) {
-                    uint8_t* dst = k_s + s * CF::TILE + sl * SLAB_BYTES;
+                    for (int sl = 0; sl < CF::SLABS; ++sl)
+                        tma_load_3d(q_s + t * CF::TILE + sl * SLAB_BYTES, &tmQ, &q_full[t],
+                                    sl * 64, g.q0 + t * BQ, bh);
+                    return true;
+                };
+                if (!load_q(0)) break;
+                if (!kPersist && !load_q(1)) break;
+                const int last_page = max(0, (g.S_kv + kPageTokens - 1) / kPageTokens - 1);
+                const int hk = g.h / (p.Hq / p.Hkv);
+                for (int j = 0; j < g.n1; ++j) {
+                    const int s = (gkv + j) % KV_STAGES;
+                    const uint32_t ph = ((gkv + j) / KV_STAGES) & 1;
+                    int pages[BKV / kPageTokens];
                     if constexpr (kPaged) {
+                        const int* bt = p.block_table + (int64_t)g.b * p.max_pages;
 #pragma unroll
-                        for (int i = 0; i < BKV / kPageTokens; ++i)
-                            tma_load_4d(dst + i * kPageTokens * 128, &tmK, &k_full[s], sl * 64, 0,
-                                        hk, pages[i]);
-                    } else {
-                        tma_load_3d(dst, &tmK, &k_full[s], sl * 64, j * BKV, bh_kv);
+                        for (int i = 0; i < BKV / kPageTokens; ++i) {
+                            const int pg = bt[min(j * (BKV / kPageTokens) + i, last_page)];
+                            const bool bad = pg < 0 || pg >= p.num_pages;
+                            if (bad && g.S_kv > 0) atomicExch(p.status, AMP_DEV_ERR_BAD_PAGE);
+                            pages[i] = bad ? 0 : pg;
+                        }
                     }
-                }
-                if (!mbar_wait(&v_empty[s], ph ^ 1, p.status)) break;
-                mbar_arrive_expect_tx(&v_full[s], CF::TILE);
+                    if (!mbar_wait(&k_empty[s], ph ^ 1, p.status)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&k_full[s], CF::TILE);
 #pragma unroll
-                for (int sl = 0; sl < CF::SLABS; ++sl) {
-                    uint8_t* dst = v_s + s * CF::TILE + sl * SLAB_BYTES;
-                    if constexpr (kPaged) {
+                    for (int sl = 0; sl < CF::SLABS; ++sl) {
+                        uint8_t* dst = k_s + s * CF::TILE + sl * SLAB_BYTES;
+                        if constexpr (kPaged) {
 #pragma unroll
-                        for (int i = 0; i < BKV / kPageTokens; ++i)
-                            tma_load_4d(dst + i * kPageTokens * 128, &tmV, &v_full[s], sl * 64, 0,
-                                        hk, pages[i]);
-                    } else {
-                        tma_load_3d(dst, &tmV, &v_full[s], sl * 64, j * BKV, bh_kv);
+                            for (int i = 0; i < BKV / kPageTokens; ++i)
+                                tma_load_4d(dst + i * kPageTokens * 128, &tmK, &k_full[s], sl * 64,
+                                            0, hk, pages[i]);
+                        } else {
+                            tma_load_3d(dst, &tmK, &k_full[s], sl * 64, j * BKV, g.bh_kv);
+                        }
                     }
+                    if (!mbar_wait(&v_empty[s], ph ^ 1, p.status)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&v_full[s], CF::TILE);
+#pragma unroll
+                    for (int sl = 0; sl < CF::SLABS; ++sl) {
+                        uint8_t* dst = v_s + s * CF::TILE + sl * SLAB_BYTES;
+                        if constexpr (kPaged) {
+#pragma unroll
+                            for (int i = 0; i < BKV / kPageTokens; ++i)
+                                tma_load_4d(dst + i * kPageTokens * 128, &tmV, &v_full[s], sl * 64,
+                                            0, hk, pages[i]);
+                        } else {
+                            tma_load_3d(dst, &tmV, &v_full[s], sl * 64, j * BKV, g.bh_kv);
+                        }
+                    }
+                    if (kPersist && j == 0 && !load_q(1)) { ok = false; break; }
                 }
+                gkv += g.n1;
+                ++li;
             }
         }
     } else if (warp == 1) {
@@ -254,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t q_addr = smem_u32(q_s);
             // S_t = Q_t K^T (K-major x K-major, 16-deep steps along the head dim)
             auto qk = [&](int t, uint32_t k_addr) {
-                const uint32_t qa = q_addr + t * CF::TILE;
+                const uint32_t qa = opaque_u32(q_addr + t * CF::TILE);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * SLAB_BYTES + (kk & 3) * 32;
@@ -262,49 +337,108 @@ __global__ void __launch_bounds__(kThreads, 1)
                                smem_desc_sw128(k_addr + off, 16, 1024), CF::IDESC_QK, kk != 0);
                 }
             };
-            bool ok = mbar_wait(q_full, 0, p.status) && mbar_wait(&k_full[0], 0, p.status);
-            if (ok) {
-                tc_fence_after();
-                const uint32_t k_addr = smem_u32(k_s);
-                qk(0, k_addr);
-                tc_commit(&s_full[0]);
-                qk(1, k_addr);
-                tc_commit(&s_full[1]);
-                tc_commit(&k_empty[0]);
-            }
-            for (int j = 0; ok && j < n1; ++j) {
-                const int s = j % KV_STAGES, s1 = (j + 1) % KV_STAGES;
-                if (!mbar_wait(&v_full[s], (j / KV_STAGES) & 1, p.status)) break;
-                const uint32_t v_addr = smem_u32(v_s + s * CF::TILE);
-                const uint32_t k1_addr = smem_u32(k_s + s1 * CF::TILE);
-                bool k1_ready = false;
+            // gkv: K/V tiles consumed before this item (ring stage / phase as in the
+            // load warp); c[t]: query tile t's steps before this item (phase of
+            // s_full / p_full / pv_done); li: items before this one (q_full, q_empty,
+            // o_free)
+            int gkv = 0, li = 0, c[2] = {0, 0};
+            bool ok = true, pre0 = false;   // pre0: this item's QK_0 was issued early
+            for (int k = 0; ok; ++k) {
+                int bh, qb;
+                const int st = item_at(k, bh, qb);
+                if (st == 0) break;
+                if (st == 2) continue;
+                const Geo g = geo(bh, qb);
+                const int n0 = g.n0, n1 = g.n1;
+                // S_t = Q_t K_0^T of this item.  S_t may still hold P_t of the previous
+                // item's last step: its PV was issued earlier, and runs first.
+                {
+                    const int s0 = gkv % KV_STAGES;
+                    if (!mbar_wait(&k_full[s0], (gkv / KV_STAGES) & 1, p.status)) break;
+                    const uint32_t k_addr = opaque_u32(smem_u32(k_s + s0 * CF::TILE));
 #pragma unroll
-                for (int t = 0; t < 2; ++t) {
-                    const int nt = t ? n1 : n0;
-                    if (j >= nt) continue;
-                    if (!mbar_wait(&p_full[t], j & 1, p.status)) { ok = false; break; }
-                    tc_fence_after();
-#pragma unroll
-                    for (int kk = 0; kk < BKV / 16; ++kk)
-                        tc_mma_f16_ts(tmem + CF::O_COL + t * D, tmem + t * BKV + kk * 8,
-                                      smem_desc_sw128(v_addr + kk * 16 * 128, SLAB_BYTES, 1024),
-                                      CF::IDESC_PV, (j | kk) != 0);
-                    tc_commit(&pv_done[t]);
-                    if (t == 1) tc_commit(&v_empty[s]);
-                    if (j + 1 < nt) {
-                        if (!k1_ready) {
-                            if (!mbar_wait(&k_full[s1], ((j + 1) / KV_STAGES) & 1, p.status)) { ok = false; break; }
-                            tc_fence_after();
-                            k1_ready = true;
-                        }
-                        // P_t,j sits in S_t, which this QK overwrites: tcgen05.mma
-                        // operations issued by one thread execute in issue order, so
-                        // PV_t,j has read P before QK_t,j+1 writes S_t -- no wait here.
-                        qk(t, k1_addr);
+                    for (int t = 0; t < 2; ++t) {
+                        if (t == 0 && pre0) continue;
+                        if (!mbar_wait(&q_full[t], li & 1, p.status)) { ok = false; break; }
+                        tc_fence_after();
+                        qk(t, k_addr);
                         tc_commit(&s_full[t]);
-                        if (t == 1) tc_commit(&k_empty[s1]);
+                        if ((t ? n1 : n0) == 1) tc_commit(&q_empty[t]);
+                    }
+                    if (!ok) break;
+                    tc_commit(&k_empty[s0]);
+                    pre0 = false;
+                }
+                for (int j = 0; ok && j < n1; ++j) {
+                    const int gj = gkv + j;
+                    const int s = gj % KV_STAGES, s1 = (gj + 1) % KV_STAGES;
+                    if (!mbar_wait(&v_full[s], (gj / KV_STAGES) & 1, p.status)) { ok = false; break; }
+                    const uint32_t v_addr = opaque_u32(smem_u32(v_s + s * CF::TILE));
+                    const uint32_t k1_addr = opaque_u32(smem_u32(k_s + s1 * CF::TILE));
+                    bool k1_ready = false;
+#pragma unroll
+                    for (int t = 0; t < 2; ++t) {
+                        const int nt = t ? n1 : n0;
+                        if (j >= nt) continue;
+                        if (t == 1 && j == n1 - 1 && j >= n0) {
+                            // Tile 0 is done with this item: S_0 of the next item now,
+                            // while tile 1 runs its last step (S_0 held P_0 of this
+                            // item's last tile-0 step, whose PV was issued before).
+                            int kn = k + 1, bh2, qb2, st2;
+                            while ((st2 = item_at(kn, bh2, qb2)) == 2) ++kn;
+                            if (st2 == 1) {
+                                const int n0n = geo(bh2, qb2).n0;
+                                const int gn = gkv + n1, sn = gn % KV_STAGES;
+                                if (!mbar_wait(&k_full[sn], (gn / KV_STAGES) & 1, p.status) ||
+                                    !mbar_wait(&q_full[0], (li + 1) & 1, p.status)) {
+                                    ok = false;
+                                    break;
+                                }
+                                tc_fence_after();
+                                qk(0, opaque_u32(smem_u32(k_s + sn * CF::TILE)));
+                                tc_commit(&s_full[0]);
+                                if (n0n == 1) tc_commit(&q_empty[0]);
+                                pre0 = true;
+                            }
+                        }
+                        // the first PV_t of an item overwrites O_t: the previous item's
+                        // epilogue must have read it
+                        if (j == 0 && li > 0 && !mbar_wait(&o_free[t], (li - 1) & 1, p.status)) {
+                            ok = false;
+                            break;
+                        }
+                        if (!mbar_wait(&p_full[t], (c[t] + j) & 1, p.status)) { ok = false; break; }
+                        tc_fence_after();
+#pragma unroll
+                        for (int kk = 0; kk < BKV / 16; ++kk)
+                            tc_mma_f16_ts(tmem + CF::O_COL + t * D, tmem + t * BKV + kk * 8,
+                                          smem_desc_sw128(v_addr + kk * 16 * 128, SLAB_BYTES, 1024),
+                                          CF::IDESC_PV, (j | kk) != 0);
+                        tc_commit(&pv_done[t]);
+                        if (t == 1) tc_commit(&v_empty[s]);
+                        if (j + 1 < nt) {
+                            if (!k1_ready) {
+                                if (!mbar_wait(&k_full[s1], ((gj + 1) / KV_STAGES) & 1, p.status)) {
+                                    ok = false;
+                                    break;
+                                }
+                                tc_fence_after();
+                                k1_ready = true;
+                            }
+                            // P_t,j sits in S_t, which this QK overwrites: tcgen05.mma
+                            // operations issued by one thread execute in issue order, so
+                            // PV_t,j has read P before QK_t,j+1 writes S_t -- no wait here.
+                            qk(t, k1_addr);
+                            tc_commit(&s_full[t]);
+                            if (j + 2 == nt) tc_commit(&q_empty[t]);   // the item's last QK_t
+                            if (t == 1) tc_commit(&k_empty[s1]);
+                        }
                     }
                 }
+                gkv += n1;
+                c[0] += n0;
+                c[1] += n1;
+                ++li;
             }
             tc_commit(drain);
             mbar_wait(drain, 0, p.status);
@@ -316,16 +450,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int t = (warp - 4) >> 2;
         const int quad = warp & 3;
         const int r = quad * 32 + lane;
-        const int qi = q0 + t * BQ + r;
-        const int nt = t ? n1 : n0;
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
         const uint32_t s_col = t * BKV, o_col = CF::O_COL + t * D;
         const float c = p.scale_log2;
+        // c_t: this tile's steps before the current item (phase of s_full / pv_done)
+        int c_t = 0;
+        bool ok = true;
+        for (int it = 0; ok; ++it) {
+        int bh, qb;
+        const int st_item = item_at(it, bh, qb);
+        if (st_item == 0) break;
+        if (st_item == 2) continue;
+        const Geo g = geo(bh, qb);
+        const int q0 = g.q0, S_kv = g.S_kv, coff = g.coff;
+        const int qi = q0 + t * BQ + r;
+        const int nt = t ? g.n1 : g.n0;
         const int vis_hi = p.causal ? min(S_kv - 1, qi + coff) : S_kv - 1;
         float m_run = -INFINITY, l_run = 0.0f;
-        bool ok = true;
         for (int j = 0; j < nt; ++j) {
-            if (!mbar_wait_warp(&s_full[t], j & 1, p.status)) { ok = false; break; }
+            if (!mbar_wait_warp(&s_full[t], (c_t + j) & 1, p.status)) { ok = false; break; }
             tc_fence_after();
             uint32_t sr[BKV / 32][32];
             __syncwarp();
@@ -359,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (__any_sync(0xffffffffu, need)) {
                 const float alpha = (m_run == -INFINITY) ? 0.0f : ex2_approx(m_run - m_new);
                 if (j > 0) {
-                    if (!mbar_wait_warp(&pv_done[t], (j - 1) & 1, p.status)) { ok = false; break; }
+                    if (!mbar_wait_warp(&pv_done[t], (c_t + j - 1) & 1, p.status)) { ok = false; break; }
                     tc_fence_after();
                     __syncwarp();
 #pragma unroll
@@ -407,7 +550,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[t]);
         }
-        if (ok && mbar_wait_warp(&pv_done[t], (nt - 1) & 1, p.status)) {
+        if (ok && !mbar_wait_warp(&pv_done[t], (c_t + nt - 1) & 1, p.status)) ok = false;
+        if (ok) {
             tc_fence_after();
             const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
             const bool row_ok = qi < p.S_q;
@@ -422,6 +566,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t o[32];
                     tmem_ld_32x32b_x32(lane_base + o_col + oc * 32, o);
                     tmem_ld_wait();
+                    if (oc == D / 32 - 1) {  // O_t is read out: the next item's PV may run
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&o_free[t]);
+                    }
                     if (row_ok) {
 #pragma unroll
                         for (int e = 0; e < 32; e += 8) {
@@ -474,6 +623,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (row_ok && p.lse_peers) p.lse_peers[d][grow + lane] = lse_v;
                 }
             }
+        }
+        c_t += nt;
         }
     }
     if constexpr (kAllGather) {
@@ -572,9 +723,19 @@ int launch_fa(const void* Q, const void* K, const void* V, void* O, float* lse, 
             kern = k_flash_fwd<D, kPaged, true>;
         }
     }
+    const int n_qb = (S_q + 2 * BQ - 1) / (2 * BQ);
+    dim3 grid(n_qb, B * Hq);
+    if constexpr (!kPaged) {
+        const int64_t units = (int64_t)B * Hq * ((n_qb + 1) / 2);
+        if (!ag && units <= INT32_MAX / 2) {
+            // dense, one GPU's output: one persistent CTA per SM over units of two
+            // query-tile pairs (k_flash_fwd's item_at)
+            kern = k_flash_fwd<D, kPaged, false, true>;
+            grid = dim3((unsigned)std::min<int64_t>(units, sm_count()), 1);
+        }
+    }
     AMPB_CHECK_CUDA(
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FaCfg<D>::SMEM));
-    dim3 grid((S_q + 2 * BQ - 1) / (2 * BQ), B * Hq);
     kern<<<grid, kThreads, FaCfg<D>::SMEM, st>>>(tq, tk, tv, p);
     AMPB_CHECK_LAUNCH("k_flash_fwd");
     return AMP_OK;
