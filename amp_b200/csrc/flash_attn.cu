@@ -561,27 +561,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.O) +
                                       ((int64_t)bh * p.S_q + (row_ok ? qi : 0)) * D;
                 __syncwarp();
+                // all of O_t into registers (one wait), then O_t is free for the next
+                // item's first PV while this warp normalises and stores
+                uint32_t o[D / 32][32];
 #pragma unroll
-                for (int oc = 0; oc < D / 32; ++oc) {
-                    uint32_t o[32];
-                    tmem_ld_32x32b_x32(lane_base + o_col + oc * 32, o);
-                    tmem_ld_wait();
-                    if (oc == D / 32 - 1) {  // O_t is read out: the next item's PV may run
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&o_free[t]);
-                    }
-                    if (row_ok) {
+                for (int oc = 0; oc < D / 32; ++oc)
+                    tmem_ld_32x32b_x32(lane_base + o_col + oc * 32, o[oc]);
+                tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&o_free[t]);
+                if (row_ok) {
+#pragma unroll
+                    for (int oc = 0; oc < D / 32; ++oc)
 #pragma unroll
                         for (int e = 0; e < 32; e += 8) {
                             uint4 w;
-                            w.x = f32x2_to_bf16x2(__uint_as_float(o[e]) * inv_l, __uint_as_float(o[e + 1]) * inv_l);
-                            w.y = f32x2_to_bf16x2(__uint_as_float(o[e + 2]) * inv_l, __uint_as_float(o[e + 3]) * inv_l);
-                            w.z = f32x2_to_bf16x2(__uint_as_float(o[e + 4]) * inv_l, __uint_as_float(o[e + 5]) * inv_l);
-                            w.w = f32x2_to_bf16x2(__uint_as_float(o[e + 6]) * inv_l, __uint_as_float(o[e + 7]) * inv_l);
+                            w.x = f32x2_to_bf16x2(__uint_as_float(o[oc][e]) * inv_l, __uint_as_float(o[oc][e + 1]) * inv_l);
+                            w.y = f32x2_to_bf16x2(__uint_as_float(o[oc][e + 2]) * inv_l, __uint_as_float(o[oc][e + 3]) * inv_l);
+                            w.z = f32x2_to_bf16x2(__uint_as_float(o[oc][e + 4]) * inv_l, __uint_as_float(o[oc][e + 5]) * inv_l);
+                            w.w = f32x2_to_bf16x2(__uint_as_float(o[oc][e + 6]) * inv_l, __uint_as_float(o[oc][e + 7]) * inv_l);
                             *reinterpret_cast<uint4*>(orow + oc * 32 + e) = w;
                         }
-                    }
                 }
                 if (row_ok && p.lse) p.lse[(int64_t)bh * p.S_q + qi] = lse_v;
             } else {
