@@ -106,14 +106,6 @@ __device__ __forceinline__ float lg2_approx(float x) {
     return y;
 }
 
-// The value, opaque to the compiler: shared-memory descriptors built from it are
-// recomputed at each use instead of being hoisted out of the item and step loops
-// into registers the 72-register control warps do not have.
-__device__ __forceinline__ uint32_t opaque_u32(uint32_t x) {
-    asm volatile("mov.b32 %0, %0;" : "+r"(x));
-    return x;
-}
-
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));

@@ -13,7 +13,8 @@
 //                  back over them as bf16; dV += P^T dO and dK += dS^T Q
 //                  accumulate in TMEM over every query tile of every query head
 //                  that shares the kv head (GQA).
-//   k_fa_bwd_dq    one CTA per (batch * query head, 128-query tile).  S = Q K^T,
+//   k_fa_bwd_dq    per (batch * query head, 128-query tile), on persistent
+//                  CTAs (one per SM) that walk pairs of such tiles.  S = Q K^T,
 //                  dP = dO V^T with queries on the lanes; dS back over dP;
 //                  dQ += dS K over the visible key tiles.
 // Steps overlap: the element-wise warps write P (or P^T) first and dS after, so
@@ -94,28 +95,52 @@ __device__ __forceinline__ void mma_ts(uint32_t acc, uint32_t t_col, uint32_t b_
 }
 
 // ---------------------------------------------------------------- Delta
-// Delta[row] = sum_d dO[row][d] * O[row][d] in fp32; one warp per row.
+// Delta[row] = sum_d dO[row][d] * O[row][d] in fp32.  HBM-bound (reads O and dO
+// once): D/8 lanes per row with 16-byte loads, kDeltaLoads rows per lane group in
+// flight, and the row's partial sums reduced within its lane group.
+constexpr int kDeltaLoads = 4;
 template <int D>
 __global__ void __launch_bounds__(256) k_fa_bwd_delta(const __nv_bfloat16* __restrict__ O,
                                                       const __nv_bfloat16* __restrict__ dO,
                                                       float* __restrict__ delta, int64_t rows) {
     pdl_wait();
     pdl_trigger();
+    constexpr int LPR = D / 8;            // lanes per row, 8 bf16 (16 bytes) each
+    constexpr int RPW = 32 / LPR;         // rows per warp-wide load
+    constexpr int ROWS = RPW * kDeltaLoads;
+    static_assert(LPR >= 1 && LPR <= 32 && (LPR & (LPR - 1)) == 0, "D/8 lanes per row");
     const int lane = threadIdx.x & 31;
-    for (int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); r < rows;
-         r += (int64_t)gridDim.x * 8) {
-        float acc = 0.0f;
+    const int sub = lane / LPR, col = (lane % LPR) * 8;
+    const int64_t nwarps = (int64_t)gridDim.x * 8;
+    for (int64_t r0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * ROWS; r0 < rows;
+         r0 += nwarps * ROWS) {
+        uint4 o[kDeltaLoads], g[kDeltaLoads];
 #pragma unroll
-        for (int c = lane * 4; c < D; c += 128) {
-            const uint2 o = *reinterpret_cast<const uint2*>(O + r * D + c);
-            const uint2 g = *reinterpret_cast<const uint2*>(dO + r * D + c);
-            acc = fmaf(bf16_lo(o.x), bf16_lo(g.x), acc);
-            acc = fmaf(bf16_hi(o.x), bf16_hi(g.x), acc);
-            acc = fmaf(bf16_lo(o.y), bf16_lo(g.y), acc);
-            acc = fmaf(bf16_hi(o.y), bf16_hi(g.y), acc);
+        for (int u = 0; u < kDeltaLoads; ++u) {
+            const int64_t r = r0 + u * RPW + sub;
+            if (r < rows) {
+                o[u] = *reinterpret_cast<const uint4*>(O + r * D + col);
+                g[u] = *reinterpret_cast<const uint4*>(dO + r * D + col);
+            } else {
+                o[u] = make_uint4(0u, 0u, 0u, 0u);
+                g[u] = o[u];
+            }
         }
-        acc = warp_sum(acc);
-        if (lane == 0) delta[r] = acc;
+#pragma unroll
+        for (int u = 0; u < kDeltaLoads; ++u) {
+            const uint32_t ow[4] = {o[u].x, o[u].y, o[u].z, o[u].w};
+            const uint32_t gw[4] = {g[u].x, g[u].y, g[u].z, g[u].w};
+            float acc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                acc = fmaf(bf16_lo(ow[i]), bf16_lo(gw[i]), acc);
+                acc = fmaf(bf16_hi(ow[i]), bf16_hi(gw[i]), acc);
+            }
+#pragma unroll
+            for (int m = LPR / 2; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+            const int64_t r = r0 + u * RPW + sub;
+            if (lane % LPR == 0 && r < rows) delta[r] = acc;
+        }
     }
 }
 
@@ -425,6 +450,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------- dQ
+// One persistent CTA per SM walks units of two (batch * query head, 128-query tile)
+// items of one head: tile n_qt-1-q (the heaviest under a causal mask) and tile q, so
+// units of a causal square problem carry the same work.  K/V tiles, S buffers and
+// the per-step barriers count on across items (step g of the CTA: ring stage and
+// S buffer g & 1); Q/dO reload once the item's last dP has been issued (q_empty),
+// and an item's first dQ MMA waits for the previous item's epilogue to have read
+// dQ out of TMEM (dq_free).
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     k_fa_bwd_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -446,28 +478,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* k_empty = bars + 3;     // [2]
     uint64_t* v_full = bars + 5;      // [2]
     uint64_t* v_empty = bars + 7;     // [2]
-    uint64_t* s_full = bars + 9;      // [2]: S of step j in TMEM buffer j & 1
+    uint64_t* s_full = bars + 9;      // [2]: S of step g in TMEM buffer g & 1
     uint64_t* dp_full = bars + 11;
     uint64_t* ds_full = bars + 12;
     uint64_t* dq_done = bars + 13;    // dQ has read dS: dP may be rewritten
     uint64_t* drain = bars + 14;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+    uint64_t* q_empty = bars + 15;    // the item's last MMA reading Q / dO has completed
+    uint64_t* dq_free = bars + 16;    // the item's epilogue has read dQ out of TMEM
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_qt = (p.S_q + BT - 1) / BT;
-    const int it = n_qt - 1 - (int)blockIdx.x;   // heaviest causal tiles first
-    const int bh = blockIdx.y;
-    const int b = bh / p.Hq, h = bh % p.Hq;
-    const int bh_kv = b * p.Hkv + h / (p.Hq / p.Hkv);
-    const int q0 = it * BT;
-    int n_kv = (p.S_kv + BT - 1) / BT;
-    if (p.causal) {
-        const int last = q0 + BT - 1 + p.causal_offset;
-        n_kv = min(n_kv, last < 0 ? 0 : last / BT + 1);
-    }
+    const int half_units = (n_qt + 1) / 2;
+    const int units = p.B * p.Hq * half_units;
+    // k-th item of this CTA: 0 = no more, 1 = item (bh, it), 2 = empty slot
+    auto item_at = [&](int k, int& bh, int& it) -> int {
+        const int u = (int)blockIdx.x + (k >> 1) * (int)gridDim.x;
+        if (u >= units) return 0;
+        bh = u / half_units;
+        const int q = u % half_units;
+        it = (k & 1) ? q : n_qt - 1 - q;
+        return ((k & 1) && q == n_qt - 1 - q) ? 2 : 1;
+    };
+    auto kv_tiles = [&](int it) {
+        int n_kv = (p.S_kv + BT - 1) / BT;
+        if (p.causal) {
+            const int last = it * BT + BT - 1 + p.causal_offset;
+            n_kv = min(n_kv, last < 0 ? 0 : last / BT + 1);
+        }
+        return n_kv;
+    };
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
+        mbar_init(dq_free, 8);
         for (int s = 0; s < 2; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], 1);
@@ -497,70 +542,107 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegCtl));
     if (warp == 0) {
-        if (lane == 0 && n_kv > 0) {
+        if (lane == 0) {
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
-            mbar_arrive_expect_tx(q_full, 2 * CF::TILE);
+            int g = 0, li = 0;   // K/V tiles loaded; items with work loaded
+            bool ok = true;
+            for (int k = 0; ok; ++k) {
+                int bh, it;
+                const int st = item_at(k, bh, it);
+                if (st == 0) break;
+                const int n_kv = st == 1 ? kv_tiles(it) : 0;
+                if (n_kv == 0) continue;
+                const int b = bh / p.Hq, h = bh % p.Hq;
+                const int bh_kv = b * p.Hkv + h / (p.Hq / p.Hkv);
+                if (li > 0 && !mbar_wait(q_empty, (li - 1) & 1, p.status)) break;
+                mbar_arrive_expect_tx(q_full, 2 * CF::TILE);
 #pragma unroll
-            for (int sl = 0; sl < CF::SLABS; ++sl) {
-                tma_load_3d(q_s + sl * SLAB_BYTES, &tmQ, q_full, sl * 64, q0, bh);
-                tma_load_3d(o_s + sl * SLAB_BYTES, &tmdO, q_full, sl * 64, q0, bh);
-            }
-            for (int j = 0; j < n_kv; ++j) {
-                const int s = j & 1;
-                const uint32_t ph = ((j >> 1) & 1) ^ 1;
-                if (!mbar_wait(&k_empty[s], ph, p.status)) break;
-                mbar_arrive_expect_tx(&k_full[s], CF::TILE);
+                for (int sl = 0; sl < CF::SLABS; ++sl) {
+                    tma_load_3d(q_s + sl * SLAB_BYTES, &tmQ, q_full, sl * 64, it * BT, bh);
+                    tma_load_3d(o_s + sl * SLAB_BYTES, &tmdO, q_full, sl * 64, it * BT, bh);
+                }
+                for (int j = 0; j < n_kv; ++j, ++g) {
+                    const int s = g & 1;
+                    const uint32_t ph = ((g >> 1) & 1) ^ 1;
+                    if (!mbar_wait(&k_empty[s], ph, p.status)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&k_full[s], CF::TILE);
 #pragma unroll
-                for (int sl = 0; sl < CF::SLABS; ++sl)
-                    tma_load_3d(k_s + s * CF::TILE + sl * SLAB_BYTES, &tmK, &k_full[s], sl * 64,
-                                j * BT, bh_kv);
-                if (!mbar_wait(&v_empty[s], ph, p.status)) break;
-                mbar_arrive_expect_tx(&v_full[s], CF::TILE);
+                    for (int sl = 0; sl < CF::SLABS; ++sl)
+                        tma_load_3d(k_s + s * CF::TILE + sl * SLAB_BYTES, &tmK, &k_full[s],
+                                    sl * 64, j * BT, bh_kv);
+                    if (!mbar_wait(&v_empty[s], ph, p.status)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&v_full[s], CF::TILE);
 #pragma unroll
-                for (int sl = 0; sl < CF::SLABS; ++sl)
-                    tma_load_3d(v_s + s * CF::TILE + sl * SLAB_BYTES, &tmV, &v_full[s], sl * 64,
-                                j * BT, bh_kv);
+                    for (int sl = 0; sl < CF::SLABS; ++sl)
+                        tma_load_3d(v_s + s * CF::TILE + sl * SLAB_BYTES, &tmV, &v_full[s],
+                                    sl * 64, j * BT, bh_kv);
+                }
+                ++li;
             }
         }
     } else if (warp == 1) {
-        if (lane == 0 && n_kv > 0) {
+        if (lane == 0) {
             // tensor-core order per step j:  S_{j+1}, dQ_j, dP_{j+1}
-            const uint32_t qa = smem_u32(q_s), oa = smem_u32(o_s);
-            auto ka = [&](int j) { return smem_u32(k_s + (j & 1) * CF::TILE); };
-            auto va = [&](int j) { return smem_u32(v_s + (j & 1) * CF::TILE); };
-            bool ok = mbar_wait(q_full, 0, p.status) && mbar_wait(&k_full[0], 0, p.status) &&
-                      mbar_wait(&v_full[0], 0, p.status);
-            if (ok) {
+            const uint32_t qa0 = smem_u32(q_s), oa0 = smem_u32(o_s);
+            auto ka = [&](int g) { return opaque_u32(smem_u32(k_s + (g & 1) * CF::TILE)); };
+            auto va = [&](int g) { return opaque_u32(smem_u32(v_s + (g & 1) * CF::TILE)); };
+            int g = 0, li = 0;   // steps before this item; items with work before it
+            bool ok = true;
+            for (int k = 0; ok; ++k) {
+                int bh, it;
+                const int st = item_at(k, bh, it);
+                if (st == 0) break;
+                const int n_kv = st == 1 ? kv_tiles(it) : 0;
+                if (n_kv == 0) continue;
+                const uint32_t qa = opaque_u32(qa0), oa = opaque_u32(oa0);
+                const int s0 = g & 1;
+                const uint32_t ph0 = (g >> 1) & 1;
+                if (!(mbar_wait(q_full, li & 1, p.status) && mbar_wait(&k_full[s0], ph0, p.status) &&
+                      mbar_wait(&v_full[s0], ph0, p.status)))
+                    break;
+                // S buffer s0 held S of step g-2, read before ds_full(g-2); dP held the
+                // previous item's last dS, read by its dQ, issued before
                 tc_fence_after();
-                mma_ss<D>(T_S, qa, ka(0));     // S_0 = Q K_0^T
-                tc_commit(&s_full[0]);
-                mma_ss<D>(T_dP, oa, va(0));    // dP_0 = dO V_0^T
-                tc_commit(&v_empty[0]);
+                mma_ss<D>(T_S + s0 * BT, qa, ka(g));     // S_0 = Q K_0^T
+                tc_commit(&s_full[s0]);
+                mma_ss<D>(T_dP, oa, va(g));              // dP_0 = dO V_0^T
+                tc_commit(&v_empty[s0]);
                 tc_commit(dp_full);
-            }
-            for (int j = 0; ok && j < n_kv; ++j) {
-                const bool more = j + 1 < n_kv;
-                const int n1 = (j + 1) & 1;
-                const uint32_t ph1 = ((j + 1) >> 1) & 1;
-                if (more) {   // S buffer n1 held S_{j-1}, read before ds_full(j-1)
-                    if (!mbar_wait(&k_full[n1], ph1, p.status)) break;
+                if (n_kv == 1) tc_commit(q_empty);
+                for (int j = 0; ok && j < n_kv; ++j) {
+                    const int gj = g + j;
+                    const bool more = j + 1 < n_kv;
+                    const int n1 = (gj + 1) & 1;
+                    const uint32_t ph1 = ((gj + 1) >> 1) & 1;
+                    if (more) {   // S buffer n1 held S of step gj-1, read before ds_full(gj-1)
+                        if (!mbar_wait(&k_full[n1], ph1, p.status)) { ok = false; break; }
+                        tc_fence_after();
+                        mma_ss<D>(T_S + n1 * BT, qa, ka(gj + 1));
+                        tc_commit(&s_full[n1]);
+                    }
+                    if (!mbar_wait(ds_full, gj & 1, p.status)) { ok = false; break; }
+                    // the item's first dQ overwrites the accumulator: the previous
+                    // item's epilogue must have read it
+                    if (j == 0 && li > 0 && !mbar_wait(dq_free, (li - 1) & 1, p.status)) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
-                    mma_ss<D>(T_S + n1 * BT, qa, ka(j + 1));
-                    tc_commit(&s_full[n1]);
+                    mma_ts<D>(T_dQ, T_dP, ka(gj), j != 0);   // dQ += dS K
+                    tc_commit(dq_done);
+                    tc_commit(&k_empty[gj & 1]);
+                    if (more) {   // dP_{j+1} over dS_j, after dQ_j in issue order
+                        if (!mbar_wait(&v_full[n1], ph1, p.status)) { ok = false; break; }
+                        tc_fence_after();
+                        mma_ss<D>(T_dP, oa, va(gj + 1));
+                        tc_commit(&v_empty[n1]);
+                        tc_commit(dp_full);
+                        if (j + 2 == n_kv) tc_commit(q_empty);   // the item's last dP
+                    }
                 }
-                if (!mbar_wait(ds_full, j & 1, p.status)) break;
-                tc_fence_after();
-                mma_ts<D>(T_dQ, T_dP, ka(j), j != 0);   // dQ += dS K
-                tc_commit(dq_done);
-                tc_commit(&k_empty[j & 1]);
-                if (more) {   // dP_{j+1} over dS_j, after dQ_j in issue order
-                    if (!mbar_wait(&v_full[n1], ph1, p.status)) break;
-                    tc_fence_after();
-                    mma_ss<D>(T_dP, oa, va(j + 1));
-                    tc_commit(&v_empty[n1]);
-                    tc_commit(dp_full);
-                }
+                g += n_kv;
+                ++li;
             }
             tc_commit(drain);
             mbar_wait(drain, 0, p.status);
@@ -574,25 +656,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         // into [96, 128) (the layout mma_ts reads).
         const int quad = warp & 3, half = (warp - 4) >> 2;
         const int r = quad * 32 + lane;               // query row == TMEM lane
-        const int qi = q0 + r;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         const uint32_t src_col = half * 64, dst_col = half ? 96 : 0;
         const uint64_t c2 = f2pack(p.scale_log2, p.scale_log2);
+        int g = 0;   // steps before this item
+        bool ok = true;
+        for (int k = 0; ok; ++k) {
+        int bh, it;
+        const int st = item_at(k, bh, it);
+        if (st == 0) break;
+        if (st == 2) continue;
+        const int n_kv = kv_tiles(it);
+        const int qi = it * BT + r;
         const int64_t row = (int64_t)bh * p.S_q + qi;
+        __nv_bfloat16* dq_row = static_cast<__nv_bfloat16*>(p.dq) + ((int64_t)bh * p.S_q + (qi < p.S_q ? qi : 0)) * D;
+        if (n_kv == 0) {   // no visible key: dQ = 0, no barriers
+            if (qi < p.S_q) store_zero_row<D>(dq_row, half);
+            continue;
+        }
         const float lse = qi < p.S_q ? p.lse[row] : -INFINITY;
         const float nl2 = lse == -INFINITY ? -INFINITY : -lse * kLog2e;   // -inf: P = 0
         const float ndl = qi < p.S_q ? -p.delta[row] : 0.0f;
         const uint64_t nl2x2 = f2pack(nl2, nl2), ndlx2 = f2pack(ndl, ndl);
         const int vis_hi = p.causal ? min(p.S_kv - 1, qi + p.causal_offset) : p.S_kv - 1;
-        bool ok = true;
         for (int j = 0; j < n_kv; ++j) {
+            const int gj = g + j;
             // this half's key columns e > hi are masked
             const int hi = vis_hi - (j * BT + half * 64);
             const bool dense = __all_sync(0xffffffffu, hi >= 63);
             // phase P (needs S only), kept in registers as bf16 pairs
-            if (!mbar_wait_warp(&s_full[j & 1], (j >> 1) & 1, p.status)) { ok = false; break; }
+            if (!mbar_wait_warp(&s_full[gj & 1], (gj >> 1) & 1, p.status)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sb = T_S + (j & 1) * BT;
+            const uint32_t sb = T_S + (gj & 1) * BT;
             uint32_t sv[2][32];
             __syncwarp();
             tmem_ld_32x32b_x32(sb + lane_base + src_col, sv[0]);
@@ -613,7 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pw[e >> 1] = f32x2_to_bf16x2(ex2_approx(x0), ex2_approx(x1));
             }
             // phase dS (needs dP): dS = P (dP - Delta) back over dP
-            if (!mbar_wait_warp(dp_full, j & 1, p.status)) { ok = false; break; }
+            if (!mbar_wait_warp(dp_full, gj & 1, p.status)) { ok = false; break; }
             tc_fence_after();
             __syncwarp();
             tmem_ld_32x32b_x32(T_dP + lane_base + src_col, sv[0]);
@@ -636,13 +731,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(ds_full);
         }
-
-        __nv_bfloat16* dq_row = static_cast<__nv_bfloat16*>(p.dq) + ((int64_t)bh * p.S_q + (qi < p.S_q ? qi : 0)) * D;
-        if (n_kv == 0) {
-            if (qi < p.S_q) store_zero_row<D>(dq_row, half);
-        } else if (ok && mbar_wait_warp(dq_done, (n_kv - 1) & 1, p.status)) {
-            tc_fence_after();
-            store_row<D>(T_dQ + lane_base, p.scale, dq_row, qi < p.S_q, half);
+        if (ok && !mbar_wait_warp(dq_done, (g + n_kv - 1) & 1, p.status)) ok = false;
+        if (!ok) break;
+        tc_fence_after();
+        store_row<D>(T_dQ + lane_base, p.scale, dq_row, qi < p.S_q, half);
+        // store_row has read this half of dQ out of TMEM: the next item's dQ may run
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_free);
+        g += n_kv;
         }
     }
 
@@ -684,7 +781,9 @@ int launch_bwd(const void* Q, const void* K, const void* V, const void* O, const
     p.dv = dV;
     p.status = status;
     const int64_t rows = (int64_t)B * Hq * S_q;
-    const int dgrid = (int)std::min<int64_t>((rows + 7) / 8, (int64_t)sm_count() * 16);
+    const int64_t delta_rows_per_block = 8 * (32 / (D / 8)) * kDeltaLoads;
+    const int dgrid = (int)std::min<int64_t>((rows + delta_rows_per_block - 1) / delta_rows_per_block,
+                                             (int64_t)sm_count() * 8);
     AMPB_CHECK_CUDA(launch_pdl(k_fa_bwd_delta<D>, dim3(dgrid), dim3(256), 0, st,
                                static_cast<const __nv_bfloat16*>(O),
                                static_cast<const __nv_bfloat16*>(dO), delta, rows));
@@ -702,8 +801,11 @@ int launch_bwd(const void* Q, const void* K, const void* V, const void* O, const
     }
     AMPB_CHECK_CUDA(launch_pdl(k_fa_bwd_dkdv<D>, dim3((S_kv + BT - 1) / BT, B * Hkv),
                                dim3(kThreads), SMEM_KV, st, tq, tk, tv, to, p));
-    AMPB_CHECK_CUDA(launch_pdl(k_fa_bwd_dq<D>, dim3((S_q + BT - 1) / BT, B * Hq), dim3(kThreads),
-                               SMEM_Q, st, tq, tk, tv, to, p));
+    // dQ: one persistent CTA per SM over units of two query tiles (k_fa_bwd_dq)
+    const int64_t dq_units = (int64_t)B * Hq * (((S_q + BT - 1) / BT + 1) / 2);
+    AMPB_REQUIRE(dq_units <= INT32_MAX / 2, AMP_ERR_UNSUPPORTED, "attention too large");
+    AMPB_CHECK_CUDA(launch_pdl(k_fa_bwd_dq<D>, dim3((unsigned)std::min<int64_t>(dq_units, sm_count())),
+                               dim3(kThreads), SMEM_Q, st, tq, tk, tv, to, p));
     return AMP_OK;
 }
 

@@ -38,6 +38,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// The value, opaque to the compiler: shared-memory descriptors built from it are
+// recomputed at each use instead of being hoisted out of a kernel's loops into
+// registers that the 72-register control warps do not have.
+__device__ __forceinline__ uint32_t opaque_u32(uint32_t x) {
+    asm volatile("mov.b32 %0, %0;" : "+r"(x));
+    return x;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
