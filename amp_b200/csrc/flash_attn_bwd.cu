@@ -8,7 +8,8 @@
 //   dV = P^T dO,  dK = scale dS^T Q,  dQ = scale dS K
 // in two passes shaped like the forward, so every product is one of its MMA
 // forms (SS, K-major x K-major; TS with P / dS in TMEM and an MN-major B):
-//   k_fa_bwd_dkdv  one CTA per (batch * kv head, 128-key tile).  S^T = K Q^T and
+//   k_fa_bwd_dkdv  per (batch * kv head, 128-key tile), on persistent CTAs (one
+//                  per SM) that walk pairs of such tiles.  S^T = K Q^T and
 //                  dP^T = V dO^T put keys on the TMEM lanes; P^T and dS^T go
 //                  back over them as bf16; dV += P^T dO and dK += dS^T Q
 //                  accumulate in TMEM over every query tile of every query head
@@ -206,24 +207,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* dk_done = bars + 10;    // dK has read dS^T: dP^T may be rewritten
     uint64_t* drain = bars + 11;
     uint64_t* cols_ready = bars + 12; // [2]: the 256 element-wise threads posted the step
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+    uint64_t* kv_empty = bars + 14;   // the item's last MMA reading K / V has completed
+    uint64_t* dkv_free = bars + 15;   // the item's epilogue has read dK, dV out of TMEM
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int jt = blockIdx.x, bh_kv = blockIdx.y;
-    const int b = bh_kv / p.Hkv, hk = bh_kv % p.Hkv;
     const int G = p.Hq / p.Hkv;
-    const int k0 = jt * BT;
     const int n_qt = (p.S_q + BT - 1) / BT;
-    int i_lo = 0;
-    if (p.causal) {   // first query tile with a query that sees a key of this tile
-        const int first_q = k0 - p.causal_offset;
-        i_lo = first_q <= 0 ? 0 : first_q / BT;
-    }
-    const int per_head = max(0, n_qt - i_lo);
-    const int steps = G * per_head;
+    const int n_kt = (p.S_kv + BT - 1) / BT;
+    // Persistent: unit u = blockIdx.x + (k/2) * gridDim.x pairs key tile n_kt-1-q with
+    // key tile q of one kv head (under a causal mask they see the fewest and the most
+    // query tiles), so the units of a causal square problem carry the same work.
+    const int half_units = (n_kt + 1) / 2;
+    const int units = p.B * p.Hkv * half_units;
+    // k-th item of this CTA: 0 = no more, 1 = item (bh_kv, jt), 2 = empty slot
+    auto item_at = [&](int k, int& bh_kv, int& jt) -> int {
+        const int u = (int)blockIdx.x + (k >> 1) * (int)gridDim.x;
+        if (u >= units) return 0;
+        bh_kv = u / half_units;
+        const int q = u % half_units;
+        jt = (k & 1) ? q : n_kt - 1 - q;
+        return ((k & 1) && q == n_kt - 1 - q) ? 2 : 1;
+    };
+    // first query tile with a query that sees a key of tile jt
+    auto first_tile = [&](int jt) {
+        int i_lo = 0;
+        if (p.causal) {
+            const int first_q = jt * BT - p.causal_offset;
+            i_lo = first_q <= 0 ? 0 : first_q / BT;
+        }
+        return i_lo;
+    };
 
     if (threadIdx.x == 0) {
         mbar_init(kv_full, 1);
+        mbar_init(kv_empty, 1);
+        mbar_init(dkv_free, 8);
         for (int s = 0; s < 2; ++s) {
             mbar_init(&qs_full[s], 1);
             mbar_init(&qs_empty[s], 1);
@@ -252,67 +271,110 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegCtl));
     if (warp == 0) {
-        if (lane == 0 && steps > 0) {
+        if (lane == 0) {
             tma_prefetch_desc(&tmQ);
             tma_prefetch_desc(&tmdO);
-            mbar_arrive_expect_tx(kv_full, 2 * CF::TILE);
-#pragma unroll
-            for (int sl = 0; sl < CF::SLABS; ++sl) {
-                tma_load_3d(k_s + sl * SLAB_BYTES, &tmK, kv_full, sl * 64, k0, bh_kv);
-                tma_load_3d(v_s + sl * SLAB_BYTES, &tmV, kv_full, sl * 64, k0, bh_kv);
-            }
-            for (int t = 0; t < steps; ++t) {
-                const int s = t & 1;
-                if (!mbar_wait(&qs_empty[s], ((t >> 1) & 1) ^ 1, p.status)) break;
-                const int g = t / per_head, it = i_lo + t % per_head;
-                const int bh_q = b * p.Hq + hk * G + g;
-                mbar_arrive_expect_tx(&qs_full[s], 2 * CF::TILE);
+            int g = 0, li = 0;   // Q/dO tiles loaded (ring stage g & 1); items with work
+            bool ok = true;
+            for (int k = 0; ok; ++k) {
+                int bh_kv, jt;
+                const int st = item_at(k, bh_kv, jt);
+                if (st == 0) break;
+                if (st == 2) continue;
+                const int i_lo = first_tile(jt);
+                const int per_head = max(0, n_qt - i_lo);
+                const int steps = G * per_head;
+                if (steps == 0) continue;
+                const int b = bh_kv / p.Hkv, hk = bh_kv % p.Hkv;
+                // K_j / V_j once the previous item's last MMA reading them has completed
+                if (li > 0 && !mbar_wait(kv_empty, (li - 1) & 1, p.status)) break;
+                mbar_arrive_expect_tx(kv_full, 2 * CF::TILE);
 #pragma unroll
                 for (int sl = 0; sl < CF::SLABS; ++sl) {
-                    tma_load_3d(q_s + s * CF::TILE + sl * SLAB_BYTES, &tmQ, &qs_full[s], sl * 64,
-                                it * BT, bh_q);
-                    tma_load_3d(o_s + s * CF::TILE + sl * SLAB_BYTES, &tmdO, &qs_full[s], sl * 64,
-                                it * BT, bh_q);
+                    tma_load_3d(k_s + sl * SLAB_BYTES, &tmK, kv_full, sl * 64, jt * BT, bh_kv);
+                    tma_load_3d(v_s + sl * SLAB_BYTES, &tmV, kv_full, sl * 64, jt * BT, bh_kv);
                 }
+                for (int t = 0; t < steps; ++t, ++g) {
+                    const int s = g & 1;
+                    if (!mbar_wait(&qs_empty[s], ((g >> 1) & 1) ^ 1, p.status)) { ok = false; break; }
+                    const int gq = t / per_head, it = i_lo + t % per_head;
+                    const int bh_q = b * p.Hq + hk * G + gq;
+                    mbar_arrive_expect_tx(&qs_full[s], 2 * CF::TILE);
+#pragma unroll
+                    for (int sl = 0; sl < CF::SLABS; ++sl) {
+                        tma_load_3d(q_s + s * CF::TILE + sl * SLAB_BYTES, &tmQ, &qs_full[s],
+                                    sl * 64, it * BT, bh_q);
+                        tma_load_3d(o_s + s * CF::TILE + sl * SLAB_BYTES, &tmdO, &qs_full[s],
+                                    sl * 64, it * BT, bh_q);
+                    }
+                }
+                ++li;
             }
         }
     } else if (warp == 1) {
-        if (lane == 0 && steps > 0) {
+        if (lane == 0) {
             // tensor-core order per step t:  dV_t, S^T_{t+1}, dK_t, dP^T_{t+1} -- so the
             // next step's S^T runs while the element-wise warps compute dS^T_t
-            const uint32_t ka = smem_u32(k_s), va = smem_u32(v_s);
-            auto qa = [&](int t) { return smem_u32(q_s + (t & 1) * CF::TILE); };
-            auto oa = [&](int t) { return smem_u32(o_s + (t & 1) * CF::TILE); };
-            bool ok = mbar_wait(kv_full, 0, p.status) && mbar_wait(&qs_full[0], 0, p.status);
-            if (ok) {
+            const uint32_t ka0 = smem_u32(k_s), va0 = smem_u32(v_s);
+            auto qa = [&](int g) { return opaque_u32(smem_u32(q_s + (g & 1) * CF::TILE)); };
+            auto oa = [&](int g) { return opaque_u32(smem_u32(o_s + (g & 1) * CF::TILE)); };
+            int g = 0, li = 0;   // steps before this item; items with work before it
+            bool ok = true;
+            for (int k = 0; ok; ++k) {
+                int bh_kv, jt;
+                const int st = item_at(k, bh_kv, jt);
+                if (st == 0) break;
+                if (st == 2) continue;
+                const int steps = G * max(0, n_qt - first_tile(jt));
+                if (steps == 0) continue;
+                const uint32_t ka = opaque_u32(ka0), va = opaque_u32(va0);
+                if (!(mbar_wait(kv_full, li & 1, p.status) &&
+                      mbar_wait(&qs_full[g & 1], (g >> 1) & 1, p.status)))
+                    break;
+                // S^T held the previous item's last P^T, read by its dV; dP^T its last
+                // dS^T, read by its dK: both were issued before
                 tc_fence_after();
-                mma_ss<D>(T_S, ka, qa(0));     // S^T_0 = K Q_0^T
+                mma_ss<D>(T_S, ka, qa(g));     // S^T_0 = K Q_0^T
                 tc_commit(s_full);
-                mma_ss<D>(T_dP, va, oa(0));    // dP^T_0 = V dO_0^T
+                mma_ss<D>(T_dP, va, oa(g));    // dP^T_0 = V dO_0^T
                 tc_commit(dp_full);
-            }
-            for (int t = 0; ok && t < steps; ++t) {
-                const bool more = t + 1 < steps;
-                if (!mbar_wait(p_full, t & 1, p.status)) break;
-                tc_fence_after();
-                mma_ts<D>(T_dV, T_S, oa(t), t != 0);    // dV += P^T dO
-                if (more) {
-                    // S^T_{t+1} overwrites P^T_t, which dV_t reads: tcgen05.mma operations
-                    // issued by one thread execute in issue order, so no wait is needed
-                    if (!mbar_wait(&qs_full[(t + 1) & 1], ((t + 1) >> 1) & 1, p.status)) break;
+                if (steps == 1) tc_commit(kv_empty);
+                for (int t = 0; ok && t < steps; ++t) {
+                    const int gt = g + t;
+                    const bool more = t + 1 < steps;
+                    if (!mbar_wait(p_full, gt & 1, p.status)) { ok = false; break; }
+                    // the item's first dV / dK overwrite the accumulators: the previous
+                    // item's epilogue must have read them
+                    if (t == 0 && li > 0 && !mbar_wait(dkv_free, (li - 1) & 1, p.status)) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
-                    mma_ss<D>(T_S, ka, qa(t + 1));
-                    tc_commit(s_full);
+                    mma_ts<D>(T_dV, T_S, oa(gt), t != 0);    // dV += P^T dO
+                    if (more) {
+                        // S^T_{t+1} overwrites P^T_t, which dV_t reads: tcgen05.mma operations
+                        // issued by one thread execute in issue order, so no wait is needed
+                        if (!mbar_wait(&qs_full[(gt + 1) & 1], ((gt + 1) >> 1) & 1, p.status)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        mma_ss<D>(T_S, ka, qa(gt + 1));
+                        tc_commit(s_full);
+                    }
+                    if (!mbar_wait(ds_full, gt & 1, p.status)) { ok = false; break; }
+                    tc_fence_after();
+                    mma_ts<D>(T_dK, T_dP, qa(gt), t != 0);   // dK += dS^T Q
+                    tc_commit(dk_done);
+                    tc_commit(&qs_empty[gt & 1]);
+                    if (more) {   // dP^T_{t+1} over dS^T_t, after dK_t in issue order
+                        mma_ss<D>(T_dP, va, oa(gt + 1));
+                        tc_commit(dp_full);
+                        if (t + 2 == steps) tc_commit(kv_empty);   // the item's last S^T / dP^T
+                    }
                 }
-                if (!mbar_wait(ds_full, t & 1, p.status)) break;
-                tc_fence_after();
-                mma_ts<D>(T_dK, T_dP, qa(t), t != 0);   // dK += dS^T Q
-                tc_commit(dk_done);
-                tc_commit(&qs_empty[t & 1]);
-                if (more) {   // dP^T_{t+1} over dS^T_t, after dK_t in issue order
-                    mma_ss<D>(T_dP, va, oa(t + 1));
-                    tc_commit(dp_full);
-                }
+                g += steps;
+                ++li;
             }
             tc_commit(drain);
             mbar_wait(drain, 0, p.status);
@@ -328,33 +390,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quad = warp & 3, half = (warp - 4) >> 2;
         const int tid = threadIdx.x - 128;            // 0..255
         const int kr = quad * 32 + lane;              // key row == TMEM lane
-        const int kj = k0 + kr;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         const uint32_t src_col = half * 64, dst_col = half ? 96 : 0;
         const uint64_t c2 = f2pack(p.scale_log2, p.scale_log2);
+        int gs = 0;   // steps before this item
         bool ok = true;
+        for (int k = 0; ok; ++k) {
+        int bh_kv, jt;
+        const int st = item_at(k, bh_kv, jt);
+        if (st == 0) break;
+        if (st == 2) continue;
+        const int b = bh_kv / p.Hkv, hk = bh_kv % p.Hkv;
+        const int kj = jt * BT + kr;
+        const int i_lo = first_tile(jt);
+        const int per_head = max(0, n_qt - i_lo);
+        const int steps = G * per_head;
+        __nv_bfloat16* dk_row = static_cast<__nv_bfloat16*>(p.dk) + ((int64_t)bh_kv * p.S_kv + (kj < p.S_kv ? kj : 0)) * D;
+        __nv_bfloat16* dv_row = static_cast<__nv_bfloat16*>(p.dv) + ((int64_t)bh_kv * p.S_kv + (kj < p.S_kv ? kj : 0)) * D;
+        if (steps == 0) {   // no query sees these keys: dK = dV = 0, no barriers
+            if (kj < p.S_kv) {
+                store_zero_row<D>(dk_row, half);
+                store_zero_row<D>(dv_row, half);
+            }
+            continue;
+        }
         // -lse2 / -Delta of query `tid` of step t's tile (threads tid < 128)
         auto fetch = [&](int t, float& nl2, float& ndl) {
-            const int g = t / per_head, it = i_lo + t % per_head;
+            const int gq = t / per_head, it = i_lo + t % per_head;
             const int q = it * BT + tid;
-            const int64_t row = (int64_t)(b * p.Hq + hk * G + g) * p.S_q + q;
+            const int64_t row = (int64_t)(b * p.Hq + hk * G + gq) * p.S_q + q;
             const float lse = q < p.S_q ? p.lse[row] : -INFINITY;
             nl2 = lse == -INFINITY ? -INFINITY : -lse * kLog2e;   // -inf: the column's P is 0
             ndl = q < p.S_q ? -p.delta[row] : 0.0f;
         };
         float nl2 = 0.0f, ndl = 0.0f;
-        if (steps > 0 && tid < BT) fetch(0, nl2, ndl);
+        if (tid < BT) fetch(0, nl2, ndl);
         for (int t = 0; t < steps; ++t) {
+            const int gt = gs + t;
             // [-lse2 | -Delta] of this step's query tile; a buffer is rewritten two
             // steps later, after all 256 threads have posted the step in between (so
             // every thread has finished reading this one)
-            float* cl = cols + (t & 1) * 2 * BT;
+            float* cl = cols + (gt & 1) * 2 * BT;
             if (tid < BT) {
                 cl[tid] = nl2;
                 cl[BT + tid] = ndl;
             }
-            mbar_arrive(&cols_ready[t & 1]);
-            if (!mbar_wait_warp(&cols_ready[t & 1], (t >> 1) & 1, p.status)) { ok = false; break; }
+            mbar_arrive(&cols_ready[gt & 1]);
+            if (!mbar_wait_warp(&cols_ready[gt & 1], (gt >> 1) & 1, p.status)) { ok = false; break; }
             if (t + 1 < steps && tid < BT) fetch(t + 1, nl2, ndl);
             // key kj sees query q iff kj <= q + causal_offset: this half's columns
             // e < lo are masked (q = q0 + e)
@@ -365,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool dense = __all_sync(0xffffffffu, lo == 0);
             const float* hcl = cl + half * 64;
             // phase P (needs S^T only): P^T = exp2(S^T c - lse2), kept as bf16 pairs
-            if (!mbar_wait_warp(s_full, t & 1, p.status)) { ok = false; break; }
+            if (!mbar_wait_warp(s_full, gt & 1, p.status)) { ok = false; break; }
             tc_fence_after();
             uint32_t sv[2][32];
             __syncwarp();
@@ -397,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full);
             // phase dS (needs dP^T): dS^T = P^T (dP^T - Delta) back over dP^T
-            if (!mbar_wait_warp(dp_full, t & 1, p.status)) { ok = false; break; }
+            if (!mbar_wait_warp(dp_full, gt & 1, p.status)) { ok = false; break; }
             tc_fence_after();
             __syncwarp();
             tmem_ld_32x32b_x32(T_dP + lane_base + src_col, sv[0]);
@@ -427,17 +509,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 
         // epilogue: dK = scale * acc, dV = acc (each half stores half of the columns)
-        __nv_bfloat16* dk_row = static_cast<__nv_bfloat16*>(p.dk) + ((int64_t)bh_kv * p.S_kv + (kj < p.S_kv ? kj : 0)) * D;
-        __nv_bfloat16* dv_row = static_cast<__nv_bfloat16*>(p.dv) + ((int64_t)bh_kv * p.S_kv + (kj < p.S_kv ? kj : 0)) * D;
-        if (steps == 0) {
-            if (kj < p.S_kv) {
-                store_zero_row<D>(dk_row, half);
-                store_zero_row<D>(dv_row, half);
-            }
-        } else if (ok && mbar_wait_warp(dk_done, (steps - 1) & 1, p.status)) {
-            tc_fence_after();
-            store_row<D>(T_dK + lane_base, p.scale, dk_row, kj < p.S_kv, half);
-            store_row<D>(T_dV + lane_base, 1.0f, dv_row, kj < p.S_kv, half);
+        if (ok && !mbar_wait_warp(dk_done, (gs + steps - 1) & 1, p.status)) ok = false;
+        if (!ok) break;
+        tc_fence_after();
+        store_row<D>(T_dK + lane_base, p.scale, dk_row, kj < p.S_kv, half);
+        store_row<D>(T_dV + lane_base, 1.0f, dv_row, kj < p.S_kv, half);
+        // both accumulators are read out of TMEM: the next item's dV / dK may run
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dkv_free);
+        gs += steps;
         }
     }
 
@@ -799,7 +880,10 @@ int launch_bwd(const void* Q, const void* K, const void* V, const void* O, const
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_Q));
         if (dev < 64) attr_done.fetch_or(1ull << dev);
     }
-    AMPB_CHECK_CUDA(launch_pdl(k_fa_bwd_dkdv<D>, dim3((S_kv + BT - 1) / BT, B * Hkv),
+    // dK/dV: one persistent CTA per SM over units of two key tiles (k_fa_bwd_dkdv)
+    const int64_t kv_units = (int64_t)B * Hkv * (((S_kv + BT - 1) / BT + 1) / 2);
+    AMPB_REQUIRE(kv_units <= INT32_MAX / 2, AMP_ERR_UNSUPPORTED, "attention too large");
+    AMPB_CHECK_CUDA(launch_pdl(k_fa_bwd_dkdv<D>, dim3((unsigned)std::min<int64_t>(kv_units, sm_count())),
                                dim3(kThreads), SMEM_KV, st, tq, tk, tv, to, p));
     // dQ: one persistent CTA per SM over units of two query tiles (k_fa_bwd_dq)
     const int64_t dq_units = (int64_t)B * Hq * (((S_q + BT - 1) / BT + 1) / 2);
