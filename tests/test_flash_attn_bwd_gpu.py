@@ -66,3 +66,28 @@ def test_bwd_rejects_causal_cross_lengths(cuda, amp_lib):
     lse = torch.zeros(1, 1, 128, device="cuda")
     with pytest.raises(AmpError, match="S_q == S_kv"):
         attention.flash_attn_bwd(q, k, k, q, q, lse, True)
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_persistent_passes_bit_identical(causal, cuda):
+    """Both backward passes run one CTA per SM over units of two tiles of one head.  B=6 S=384
+    has three tiles a head, so each head's second unit holds one tile and an empty slot; with
+    32 query and 16 kv heads the dQ pass has 6*32*2 = 384 units and the dK/dV pass 6*16*2 = 192,
+    so CTAs walk several.  dQ, dK and dV must equal, bit for bit, those of per-sequence
+    launches on the same O and lse (64 and 32 units, at most one a CTA)."""
+    B, Hq, Hkv, S, D = 6, 32, 16, 384, 128
+    g = torch.Generator().manual_seed(43)
+    q, do = (torch.randn(B, Hq, S, D, generator=g).to(torch.bfloat16).cuda() for _ in range(2))
+    k, v = (torch.randn(B, Hkv, S, D, generator=g).to(torch.bfloat16).cuda() for _ in range(2))
+    o, lse = attention.flash_attn_fwd(q, k, v, causal)
+    dq, dk, dv = attention.flash_attn_bwd(q, k, v, o, do, lse, causal)
+    for b in range(B):
+        s = slice(b, b + 1)
+        dqb, dkb, dvb = attention.flash_attn_bwd(
+            q[s].contiguous(), k[s].contiguous(), v[s].contiguous(), o[s].contiguous(),
+            do[s].contiguous(), lse[s].contiguous(), causal)
+        assert torch.equal(dq[s], dqb)
+        assert torch.equal(dk[s], dkb)
+        assert torch.equal(dv[s], dvb)
+    torch.cuda.synchronize()
+    assert lib().amp_device_status(1) == 0

@@ -115,3 +115,23 @@ def test_allgather_attention_single_rank(S, D, cuda):
     finally:
         pl.close()
         po.close()
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_persistent_schedule_bit_identical(causal, cuda):
+    """The dense forward runs one CTA per SM over units of two query-tile pairs of one head.
+    B=6 H=32 S=640 has three pairs a head, so each head's second unit holds one item and an
+    empty slot, and its 6*32*2 = 384 units make a CTA walk up to three of them.  An item's
+    arithmetic does not depend on the CTA that runs it, so O and lse must equal, bit for bit,
+    those of per-sequence launches (64 units, one a CTA)."""
+    B, Hq, Hkv, S, D = 6, 32, 8, 640, 128
+    q, k, v = make_qkv(B, Hq, Hkv, S, S, D, seed=41)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    o, lse = attention.flash_attn_fwd(qd, kd, vd, causal)
+    for b in range(B):
+        ob, lb = attention.flash_attn_fwd(qd[b:b + 1].contiguous(), kd[b:b + 1].contiguous(),
+                                          vd[b:b + 1].contiguous(), causal)
+        assert torch.equal(o[b:b + 1], ob)
+        assert torch.equal(lse[b:b + 1], lb)
+    torch.cuda.synchronize()
+    assert lib().amp_device_status(1) == 0
